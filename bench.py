@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""TTCLayer forward+backward throughput (tokens/s) on B200 -- BASELINE.json's metric.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl cuda|reference]
+
+One step = TTCLayer forward + backward on one batch of the chosen config (default:
+config 2, fp32, x[4,1024,16,64], h_dim 16, T 64), rows read as [B, L*H, in_dim].  At N > 1
+(torchrun) every rank runs the same per-GPU batch on its own data and the parameter
+gradients are all-reduced (NCCL) inside the step: weak scaling.  Rank 0 prints one JSON line.
+
+``--impl reference`` times the reference's CPU algorithm (the oracle's restatement of the
+``riccati`` solver with autograd backward, all host threads) on a row sample of the same
+workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (REPO, os.path.join(REPO, "ttc-net_b200"), os.path.join(REPO, "tests")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+from ttc_cases import CONFIGS, layer_input, layer_weights  # noqa: E402
+
+METRIC = "TTCLayer fwd+bwd tokens/sec"
+L2_BYTES = 126 * 2**20
+SM_COUNT_B200 = 148
+FP32_LANES_PER_SM = 128
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    ap.add_argument("--chunk-rows", type=int, default=0,
+                    help="sequence rows (of L*H) per layer call inside a step (0: auto)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="target CPU time of the cpu_baseline sample")
+    return ap.parse_args(argv)
+
+
+# ------------------------------------------------------------------------- FLOP model
+def solver_flops(cfg):
+    """Algorithmic FLOPs per LQR problem (2 per FMA; recompute not counted)."""
+    d = du = cfg.h_dim
+    T = cfg.T
+    fwd = T * 4 * d * d * du + (T - 1) * 2 * d**3 + (2 / 3) * d**3 + 2 * d**3 + 4 * d * d + 4 * d * du
+    bwd = T * (8 * d * d + 12 * d * du) + 2 * d * du + 2 * d * d
+    return fwd, bwd
+
+
+# ------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.lines:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------- setup
+def dist_setup(ngpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != ngpus:
+        raise SystemExit(f"--gpus {ngpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def make_layer(cfg, device, dtype):
+    from ttc_b200 import TTCLayer
+    layer = TTCLayer(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
+                     solver_impl="cuda")
+    layer.load_state_dict({k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()})
+    return layer.to(device=device, dtype=dtype)
+
+
+def auto_chunk(cfg, dtype):
+    """Sequence rows (dim 1 of x[B, L*H, in]) per layer call so one call's activations
+    stay near 24 GB: the whole batch for configs 1-2, row chunks for configs 3-5."""
+    es = 2 if dtype == torch.bfloat16 else 4
+    d, nh = cfg.h_dim, cfg.H
+    per_row = es * (3 * cfg.width + 4 * nh * d * d + 6 * d * d) + 4 * nh * (4 * d + d * d)
+    fit_rows = max(cfg.B, (24 << 30) // per_row)
+    return max(1, min(cfg.L * cfg.H, fit_rows // cfg.B))
+
+
+def run_step(layer, x, dy, T, chunk, world):
+    """One fwd+bwd over the batch (row chunks when the batch does not fit one call)."""
+    layer.zero_grad(set_to_none=True)
+    rows = x.shape[1]
+    for s in range(0, rows, chunk):
+        y = layer(x[:, s:s + chunk], T)
+        y.backward(dy[:, s:s + chunk])
+    if world > 1:
+        import torch.distributed as dist
+        for p in layer.parameters():
+            dist.all_reduce(p.grad)
+
+
+# ------------------------------------------------------------------------- CPU legs
+def cpu_sample(cfg, target_s, threads):
+    """Reference algorithm on the host: oracle riccati layer fwd + autograd bwd on a row
+    sample sized to ~target_s seconds.  Returns (tokens/s, rows, seconds)."""
+    from oracle import ttc_oracle as O
+    torch.set_num_threads(threads)
+    layer = O.TTCLayerOracle(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
+                             solver_impl="riccati")
+    layer.load_state_dict({k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()})
+
+    def once(rows):
+        x_np, dy_np = layer_input(cfg, rows, seed=cfg.seed + 77)
+        x = torch.from_numpy(x_np)[None].requires_grad_(cfg.backward)
+        t0 = time.perf_counter()
+        y = layer(x, T=cfg.T)
+        if cfg.backward:
+            y.backward(torch.from_numpy(dy_np)[None])
+        return time.perf_counter() - t0
+
+    probe = max(1, cfg.H // 8)
+    t = once(probe)
+    rows = int(max(probe, min(cfg.rows, probe * target_s / max(t, 1e-6))))
+    dt = once(rows)
+    return (rows / cfg.H) / dt, rows, dt
+
+
+def reference_arm(args, cfg):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    vals = []
+    rows_used = 0
+    for k in range(args.warmup + args.steps):
+        v, rows, _ = cpu_sample(cfg, budget, threads)
+        rows_used = rows
+        if k >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    sample = (f"{rows_used} of {cfg.rows} rows per step ({cfg.name}: riccati fwd + autograd "
+              f"bwd, fp32, oracle port)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * (rows_used / cfg.H) / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(cfg, world, args, chunk=None),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def workload_config(cfg, world, args, chunk):
+    return {
+        "workload": f"{cfg.name}: TTCLayer fwd+bwd, x[{cfg.B},{cfg.L},{cfg.H},{cfg.in_dim}] per GPU "
+                    f"as [B, L*H, in] rows, h_dim={cfg.h_dim}, rank={cfg.rank}, T={cfg.T}",
+        "B_per_gpu": cfg.B, "L": cfg.L, "H": cfg.H, "in_dim": cfg.in_dim, "out_dim": cfg.out_dim,
+        "h_dim": cfg.h_dim, "num_heads": cfg.H, "rank": cfg.rank, "T": cfg.T,
+        "rows_per_gpu": cfg.rows, "lqr_problems_per_gpu": cfg.problems,
+        "global_batch": cfg.B * world, "activations": cfg.dtype, "solver_state": "f32",
+        "parallelism": f"dp{world}" if world > 1 else "single",
+        "chunk_rows": chunk, "l2": "rotating input sets larger than L2 (no flush)",
+    }
+
+
+# ------------------------------------------------------------------------- main
+def main(argv=None):
+    args = parse_args(argv)
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return reference_arm(args, cfg)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    world, rank, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dtype = torch.bfloat16 if cfg.dtype == "bfloat16" else torch.float32
+
+    from ttc_b200.solver import KernelTimer, set_kernel_timer
+    layer = make_layer(cfg, device, dtype)
+    chunk = args.chunk_rows or auto_chunk(cfg, dtype)
+    rows = cfg.L * cfg.H
+
+    # Rotating (x, dy) sets on the device, together larger than L2.
+    set_bytes = cfg.B * rows * (cfg.in_dim + cfg.out_dim) * (2 if dtype == torch.bfloat16 else 4)
+    nsets = max(2, math.ceil(2 * L2_BYTES / set_bytes))
+    nsets = min(nsets, 16)
+    sets = []
+    for s in range(nsets):
+        x_np, dy_np = layer_input(cfg, cfg.rows, seed=1000 * rank + s)
+        sets.append((torch.from_numpy(x_np).to(device, dtype).view(cfg.B, rows, cfg.in_dim),
+                     torch.from_numpy(dy_np).to(device, dtype).view(cfg.B, rows, cfg.out_dim)))
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for k in range(args.warmup):
+        run_step(layer, *sets[k % nsets], cfg.T, chunk, world)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region
+    timer = KernelTimer()
+    phys = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(phys) as clocks:
+        set_kernel_timer(timer)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for k in range(args.steps):
+            run_step(layer, *sets[k % nsets], cfg.T, chunk, world)
+        end.record()
+        torch.cuda.synchronize()
+        set_kernel_timer(None)
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end))
+    tokens_per_step = cfg.tokens * world
+    value = tokens_per_step * args.steps / (ms / 1000.0)
+    kern = timer.durations_ms()
+    launches = sum(len(v) for v in kern.values())
+
+    # ---- end to end through the public API, host buffers, copies inside the region
+    x_host = [torch.from_numpy(layer_input(cfg, cfg.rows, seed=500 + s)[0]).to(dtype).pin_memory()
+              for s in range(2)]
+    dy_host = [torch.from_numpy(layer_input(cfg, cfg.rows, seed=500 + s)[1]).to(dtype).pin_memory()
+               for s in range(2)]
+    dx_host = torch.empty(cfg.rows, cfg.in_dim, dtype=dtype).pin_memory()
+
+    def e2e_step(k):
+        x = x_host[k % 2].to(device, non_blocking=True).view(cfg.B, rows, cfg.in_dim)
+        dy = dy_host[k % 2].to(device, non_blocking=True).view(cfg.B, rows, cfg.out_dim)
+        x.requires_grad_(True)
+        layer.zero_grad(set_to_none=True)
+        for s in range(0, rows, chunk):
+            y = layer(x[:, s:s + chunk], cfg.T)
+            y.backward(dy[:, s:s + chunk])
+        if world > 1:
+            import torch.distributed as dist
+            for p in layer.parameters():
+                dist.all_reduce(p.grad)
+        dx_host.copy_(x.grad.view(cfg.rows, cfg.in_dim), non_blocking=True)
+
+    e2e_step(0)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for k in range(args.steps):
+        e2e_step(k)
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1))
+    es = 2 if dtype == torch.bfloat16 else 4
+    h2d = cfg.rows * (cfg.in_dim + cfg.out_dim) * es
+    d2h = cfg.rows * cfg.in_dim * es
+
+    if rank == 0:
+        fwd_f, bwd_f = solver_flops(cfg)
+        fwd_ms = kern.get("ttc_lqr_fwd", [float("nan")])
+        bwd_ms = kern.get("ttc_lqr_bwd", [float("nan")])
+        calls_per_step = math.ceil(rows / chunk)
+        probs_per_launch = cfg.problems / calls_per_step
+        sm_max = clocks.summary().get("sm_max_mhz") or 1965.0
+        fp32_peak = SM_COUNT_B200 * FP32_LANES_PER_SM * 2 * sm_max * 1e6 / 1e12
+        fwd_tflops = fwd_f * probs_per_launch / (statistics.mean(fwd_ms) / 1e3) / 1e12
+        bwd_tflops = bwd_f * probs_per_launch / (statistics.mean(bwd_ms) / 1e3) / 1e12
+        traffic = load_traffic(cfg.name)
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if dtype == torch.float32 else "bf16 activations, f32 solver",
+            "data": "synthetic (seeded N(0,1) x and dy, reference init distributions)",
+            "config": workload_config(cfg, world, args, chunk),
+            "roofline": {
+                "kernel": "ttc_lqr_fwd (sweep + solve + first step)",
+                "bound": "fp32", "achieved": fwd_tflops, "peak": fp32_peak, "unit": "TFLOP/s",
+                "frac": fwd_tflops / fp32_peak,
+                "peak_source": f"nominal FP32 FMA: 148 SMs x 128 lanes x 2 x {sm_max:.0f} MHz "
+                               "(MEASURED_PEAKS.json has no FP32 figure)",
+                "flops_per_launch": fwd_f * probs_per_launch,
+                "launch_ms": statistics.mean(fwd_ms), "traffic": traffic,
+            },
+            "kernels": {
+                "ttc_lqr_fwd": {"launches": len(fwd_ms), "mean_ms": statistics.mean(fwd_ms),
+                                "tflops": fwd_tflops},
+                "ttc_lqr_bwd": {"launches": len(bwd_ms), "mean_ms": statistics.mean(bwd_ms),
+                                "tflops": bwd_tflops,
+                                "frac_fp32_peak": bwd_tflops / fp32_peak},
+            },
+            "clocks": clocks.summary(),
+            "e2e": {"value": tokens_per_step * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches * world,
+            "gpu_launches_per_gpu": launches,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            v, rows_used, dt = cpu_sample(cfg, args.cpu_seconds, threads)
+            out["cpu_baseline"] = {
+                "value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"{rows_used} of {cfg.rows} rows ({rows_used / cfg.H:.1f} tokens), "
+                          f"{dt:.1f} s: oracle riccati layer fwd + autograd bwd, fp32"}
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def load_traffic(workload):
+    """DRAM bytes per launch of the roofline kernel from the committed ncu summary."""
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+if __name__ == "__main__":
+    main()

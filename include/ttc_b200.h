@@ -1,0 +1,108 @@
+/*
+ * ttc_b200.h -- C-ABI of the B200 (sm_100a) LQR solve behind TTC-Net's TTCLayer.
+ *
+ * The reference (VITA-Group/TTC-Net) is Python + Triton; its solver boundary is
+ * the Python callable registered in LQR_SOLVER_IMPL_MAP (ttc/layers/ttc_layer.py:18-22,
+ * called at :137) and, one level down, the host functions of its "fused" solver
+ * that launch three Triton kernels.  The entry points below replace those host
+ * functions one for one; the Python package ttc_b200 binds them with ctypes and
+ * registers the result as solver_impl="cuda".
+ *
+ * Conventions for every entry point
+ *   - All pointers are device pointers (cudaMalloc / torch CUDA storage) unless a
+ *     comment says otherwise; every tensor is dense, row-major, contiguous.
+ *   - Sizes: N rows, nh heads per row, state dim d, action dim du, horizon T >= 1.
+ *     "Activation dtype" tensors are float32 (TTC_DTYPE_F32) or bfloat16
+ *     (TTC_DTYPE_BF16); solver state and the saved tensors are always float32.
+ *   - Work is enqueued on `stream` (a cudaStream_t, NULL = legacy default stream);
+ *     nothing blocks the host.  Instability is reported through `status`, a device
+ *     int the kernels OR bits into (TTC_STATUS_*); the caller zeroes it before the
+ *     call and reads it afterwards.
+ *   - Return value: TTC_OK, or a TTC_ERR_* code for argument errors and launch
+ *     failures (ttc_last_error() gives the message).  Calls are thread-safe apart
+ *     from the shared last-error text.
+ */
+#ifndef TTC_B200_H_
+#define TTC_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTC_ABI_VERSION 1
+
+#define TTC_DTYPE_F32 0
+#define TTC_DTYPE_BF16 1
+
+#define TTC_OK 0
+#define TTC_ERR_INVALID 1      /* null pointer, bad size or dtype */
+#define TTC_ERR_UNSUPPORTED 2  /* (d, du) pair without a compiled kernel */
+#define TTC_ERR_CUDA 3         /* CUDA launch / attribute error */
+
+/* Status bits -- the reference's RuntimeError checks, same trigger (NaN, Inf or |x| >= 1e6). */
+#define TTC_STATUS_FWD_UNSTABLE 1 /* Y1/Y2 after the sweep      (ttc/solvers/fused_lqr.py:99-101)  */
+#define TTC_STATUS_LU_UNSTABLE 2  /* pivots / P = Y1^-1 Y2       (ttc/solvers/fused_lqr.py:108-110) */
+#define TTC_STATUS_BWD_UNSTABLE 4 /* any of the nine gradients    (ttc/solvers/fused_lqr.py:243-246) */
+#define TTC_STATUS_U_NAN 8        /* NaN in u                     (ttc/layers/ttc_layer.py:139-140)  */
+
+/* ABI version of the loaded library (== TTC_ABI_VERSION it was built with). */
+int ttc_abi_version(void);
+
+/* 1 if kernels for state dim d and action dim du are compiled in, else 0. */
+int ttc_supported(int d, int du);
+
+/* Message of the last TTC_ERR_* returned by this library ("" if none). */
+const char* ttc_last_error(void);
+
+/*
+ * Forward LQR solve.  Replaces fused_lqr_layer_fwd (ttc/solvers/fused_lqr.py:18-146):
+ * the symplectic sweep (Triton lqr_symplectic_rev_iter, symplectic_iter.py:48-356),
+ * the LU solve P = Y1^-1 Y2 (fused_lqr.py:103-105) and the first-step decode
+ * (lqr_symplectic_dec_first_step, symplectic_iter.py:373-539), in one kernel.
+ *
+ * Inputs (activation dtype): A_diag [N,nh,d], B [N,d,du], Q [N,d,d], R_inv [N,nh,du],
+ *   Q_f [N,nh,d,d], log_gamma_A [N,nh], log_gamma_B [N,nh,du], log_gamma_Q [N,nh,d],
+ *   h0 [N,nh,d]  -- the solver signature of ttc_layer.py:137.
+ * Outputs: u [N,nh,du] (activation dtype);
+ *   lam0 [N,nh,d] float32 = P h0 (may be NULL);
+ *   M [N,nh,d,du] float32 = Y1^-1 Y3, what the backward needs to form
+ *     d_p = Y1^-1 (Y3 du) (fused_lqr.py:185-187) without the LU factors (may be NULL:
+ *     the backward then recomputes the sweep).
+ */
+int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
+                const void* log_gamma_Q, const void* h0, int64_t N, int nh, int d, int du,
+                int T, int dtype, void* u, float* lam0, float* M, int* status,
+                void* stream);
+
+/*
+ * Backward LQR solve.  Replaces fused_lqr_layer_bwd (ttc/solvers/fused_lqr.py:148-253):
+ * d_p = Y1^-1 (Y3 d_u) and the forward-in-time adjoint integration (Triton
+ * lqr_symplectic_fwd_iter_diff, symplectic_iter.py:553-885).  Gradients over the
+ * heads of a row (grad_B, grad_Q) are reduced inside one CTA in a fixed order, so
+ * results are deterministic (the reference uses gpu-scope atomics).
+ *
+ * Inputs: the nine forward inputs (Q_f is read only when M == NULL), d_u [N,nh,du]
+ *   (activation dtype), and the forward's lam0 and M.  With M == NULL the kernel
+ *   recomputes the sweep and ignores lam0 (both may be NULL).  With M != NULL, lam0
+ *   must be given.
+ * Outputs (activation dtype): grad_A [N,nh,d], grad_B [N,d,du], grad_Q [N,d,d],
+ *   grad_R_inv [N,nh,du], grad_Q_f [N,nh,d,d], grad_lgA [N,nh], grad_lgB [N,nh,du],
+ *   grad_lgQ [N,nh,d], grad_h0 [N,nh,d].  Q and Q_f gradients use the symmetrised
+ *   convention of the reference's fused and kkt backward ((h dh^T + dh h^T)/2).
+ */
+int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
+                const void* log_gamma_Q, const void* h0, const float* lam0, const float* M,
+                const void* d_u, int64_t N, int nh, int d, int du, int T, int dtype,
+                void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_Q_f,
+                void* grad_lgA, void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status,
+                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TTC_B200_H_ */

@@ -1,0 +1,83 @@
+"""CPU checks of the C-ABI library: it builds for sm_100a, loads, exports every symbol
+include/ttc_b200.h declares, and rejects bad arguments before touching the GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "ttc_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import build as ttc_build  # ttc-net_b200/build.py
+    from ttc_b200 import _lib
+    ttc_build.build()
+    return _lib.load()
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ttc_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ("ttc_lqr_fwd", "ttc_lqr_bwd", "ttc_abi_version", "ttc_supported", "ttc_last_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from ttc_b200 import _lib
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in include/ttc_b200.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_abi_version(lib):
+    from ttc_b200 import _lib
+    assert lib.ttc_abi_version() == _lib.ABI_VERSION
+
+
+def test_supported_shapes(lib):
+    assert lib.ttc_supported(16, 16) == 1
+    assert lib.ttc_supported(32, 32) == 1
+    assert lib.ttc_supported(24, 24) == 0
+
+
+def _fwd(lib, N=1, nh=1, d=16, du=16, T=4, dtype=0, null_inputs=False):
+    p = None if null_inputs else 16  # never dereferenced: rejected before any launch
+    return lib.ttc_lqr_fwd(*([p] * 9), N, nh, d, du, T, dtype, p, p, None, p, None)
+
+
+def test_fwd_rejects_bad_arguments_without_gpu(lib):
+    from ttc_b200 import _lib
+    assert _fwd(lib, N=-1) == _lib.ERR_INVALID
+    assert b"N (rows)" in lib.ttc_last_error()
+    assert _fwd(lib, nh=0) == _lib.ERR_INVALID
+    assert _fwd(lib, T=0) == _lib.ERR_INVALID
+    assert _fwd(lib, dtype=7) == _lib.ERR_INVALID
+    assert _fwd(lib, d=24, du=24) == _lib.ERR_UNSUPPORTED
+    assert b"h_dim=24" in lib.ttc_last_error()
+    assert _fwd(lib, null_inputs=True) == _lib.ERR_INVALID
+    assert _fwd(lib, N=0) == _lib.OK  # empty batch: nothing to launch
+
+
+def test_bwd_rejects_bad_arguments_without_gpu(lib):
+    from ttc_b200 import _lib
+    P = 16
+    base = dict(N=1, nh=1, d=16, du=16, T=4, dtype=0)
+
+    def bwd(Qf=P, lam0=P, M=P, grads=P, **kw):
+        a = {**base, **kw}
+        return lib.ttc_lqr_bwd(P, P, P, P, Qf, P, P, P, P, lam0, M, P, a["N"], a["nh"], a["d"],
+                               a["du"], a["T"], a["dtype"], *([grads] * 9), P, None)
+
+    assert bwd(M=None, Qf=None) == _lib.ERR_INVALID        # recompute needs Q_f
+    assert bwd(lam0=None) == _lib.ERR_INVALID              # M without lam0
+    assert bwd(grads=None) == _lib.ERR_INVALID
+    assert bwd(d=64, du=64) == _lib.ERR_UNSUPPORTED
+    assert bwd(N=0) == _lib.OK

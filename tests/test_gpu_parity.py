@@ -1,0 +1,244 @@
+"""Parity of the CUDA path (libttc_b200.so through ttc_b200) with the reference.
+
+Targets: forward u / y within max-rel 1e-4 (fp32) or 2e-2 (bf16
+activations) of the reference ``riccati`` solver; gradients within max-rel 1e-3 (fp32) of
+the reference ``fused`` backward, whose Q/Q_f convention the reference ``kkt`` solver
+shares.  Golden fixtures are the reference's own outputs; larger seeded cases use the
+CPU oracle (oracle/ttc_oracle.py) as the checker.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ttc_oracle as O
+from ttc_cases import CONFIGS, SOLVER_ARG_NAMES, layer_input, layer_weights, solver_inputs_synthetic
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+GRAD_NAMES = ["g_" + n for n in SOLVER_ARG_NAMES]
+FWD_TOL_F32, FWD_TOL_BF16, GRAD_TOL_F32 = 1e-4, 2e-2, 1e-3
+
+# d = 64 has no kernel yet: its fixtures are not run here.
+SOLVER_CASES = ["solver_bench_d16", "solver_synth_d32", "solver_T1", "solver_T2",
+                "solver_growth", "prologue_cfg1", "prologue_cfg2", "prologue_cfg3"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda_lib():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import build as ttc_build
+    ttc_build.build()
+    from ttc_b200 import _lib
+    return _lib.load()
+
+
+def load(name):
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    return {k: z[k] for k in z.files}
+
+
+def cuda_args(z, dtype=torch.float32, grad=True):
+    return [torch.from_numpy(z[n]).to("cuda", dtype).requires_grad_(grad) for n in SOLVER_ARG_NAMES]
+
+
+def run_cuda(args, T, dy, save_budget=None):
+    from ttc_b200 import cuda_lqr_solve
+    u = cuda_lqr_solve(*args, T, save_budget=save_budget)
+    (u * dy).sum().backward()
+    return u.detach(), [a.grad.detach() for a in args]
+
+
+@pytest.mark.parametrize("case", SOLVER_CASES)
+@pytest.mark.parametrize("save_budget", [None, 0], ids=["saved", "recompute"])
+def test_solver_matches_reference_golden(case, save_budget):
+    z = load(case)
+    T = int(z["T"])
+    args = cuda_args(z)
+    dy = torch.from_numpy(z["dy"]).cuda()
+    u, grads = run_cuda(args, T, dy, save_budget)
+    assert O.max_rel(u.cpu(), torch.from_numpy(z["u_riccati"])) < FWD_TOL_F32
+    for gn, g in zip(GRAD_NAMES, grads):
+        assert O.max_rel(g.cpu(), torch.from_numpy(z[gn])) < GRAD_TOL_F32, gn
+
+
+@pytest.mark.parametrize("d,nh,N,T", [(16, 16, 24, 64), (16, 3, 7, 33), (16, 20, 5, 16),
+                                      (32, 32, 6, 128), (32, 5, 9, 40), (32, 1, 3, 7)])
+def test_solver_matches_oracle_seeded(d, nh, N, T):
+    """Seeded synthetic problems, head counts that leave CTA groups idle, odd sizes."""
+    host = [torch.from_numpy(a) for a in solver_inputs_synthetic(N, nh, d, d, seed=100 + d + nh)]
+    dy = torch.randn(N, nh, d, dtype=torch.float64, generator=torch.Generator().manual_seed(7))
+    leaves = [a.clone().requires_grad_(True) for a in host]
+    u_ref = O.fused_solve(*leaves, T)
+    (u_ref * dy).sum().backward()
+    u_ric = O.riccati_solve(*host, T, solve_dtype=None)
+    args = [a.to("cuda", torch.float32).requires_grad_(True) for a in host]
+    u, grads = run_cuda(args, T, dy.float().cuda())
+    assert O.max_rel(u.cpu(), u_ric) < FWD_TOL_F32
+    for name, g, leaf in zip(SOLVER_ARG_NAMES, grads, leaves):
+        assert O.max_rel(g.cpu(), leaf.grad) < GRAD_TOL_F32, name
+
+
+def test_solver_bf16_matches_reference_golden():
+    z = load("prologue_cfg3_bf16")
+    from ttc_b200 import cuda_lqr_solve
+    args = cuda_args(z, torch.bfloat16, grad=False)
+    u = cuda_lqr_solve(*args, int(z["T"]))
+    assert u.dtype == torch.bfloat16
+    assert O.max_rel(u.float().cpu(), torch.from_numpy(z["u_riccati"])) < FWD_TOL_BF16
+
+
+def test_saved_and_recompute_backward_agree():
+    z = load("prologue_cfg3")
+    T = int(z["T"])
+    dy = torch.from_numpy(z["dy"]).cuda()
+    u1, g1 = run_cuda(cuda_args(z), T, dy, None)
+    u2, g2 = run_cuda(cuda_args(z), T, dy, 0)
+    assert torch.equal(u1, u2)
+    for a, b in zip(g1, g2):
+        assert O.max_rel(a.cpu(), b.cpu()) < 1e-5
+
+
+def test_deterministic_and_batch_invariant():
+    """Bitwise reproducible, and a row's result does not depend on the batch around it."""
+    host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(40, 8, 16, 16, seed=9)]
+    dy = torch.randn(40, 8, 16, generator=torch.Generator().manual_seed(3)).cuda()
+    args1 = [a.cuda().requires_grad_(True) for a in host]
+    args2 = [a.cuda().requires_grad_(True) for a in host]
+    u1, g1 = run_cuda(args1, 32, dy)
+    u2, g2 = run_cuda(args2, 32, dy)
+    assert torch.equal(u1, u2)
+    assert all(torch.equal(a, b) for a, b in zip(g1, g2))
+    sub = [a[10:17].cuda().requires_grad_(True) for a in host]
+    u3, g3 = run_cuda(sub, 32, dy[10:17])
+    assert torch.equal(u3, u1[10:17])
+    assert all(torch.equal(a, b[10:17]) for a, b in zip(g3, g1))
+
+
+def test_empty_batch():
+    from ttc_b200 import cuda_lqr_solve
+    host = [torch.from_numpy(a).float()[:0] for a in solver_inputs_synthetic(1, 4, 16, 16, seed=1)]
+    args = [a.cuda().requires_grad_(True) for a in host]
+    u = cuda_lqr_solve(*args, 8)
+    assert u.shape == (0, 4, 16)
+    u.sum().backward()
+    assert args[0].grad.shape == (0, 4, 16)
+
+
+def _inputs(N=4, nh=2, d=16):
+    return [torch.from_numpy(a).float().cuda() for a in solver_inputs_synthetic(N, nh, d, d, seed=21)]
+
+
+def test_forward_instability_raises():
+    from ttc_b200 import cuda_lqr_solve
+    args = _inputs()
+    args[4][1, 0, 3, 3] = float("nan")       # Q_f -> Y2 NaN after the sweep
+    with pytest.raises(RuntimeError, match="forward recurrence"):
+        cuda_lqr_solve(*args, 16)
+
+
+def test_lu_instability_raises():
+    """B = 0 and T = 1 give Y1 = A^-1, Y2 = Q_f A (both renormalised below 1e6) and
+    P = A Q_f A >= 1e6: the reference's LU-solve check (fused_lqr.py:108-110) fires."""
+    from ttc_b200 import cuda_lqr_solve
+    args = _inputs()
+    args[1].zero_()
+    args[4][0, 0] = 1e7 * torch.eye(16, device="cuda")
+    with pytest.raises(RuntimeError, match="LU solve"):
+        cuda_lqr_solve(*args, 1)
+
+
+def test_nan_in_u_raises_in_layer():
+    from ttc_b200 import TTCLayer
+    torch.manual_seed(0)
+    layer = TTCLayer(32, 32, 16, 4, 16, 16).cuda()
+    x = torch.randn(1, 6, 32, device="cuda")
+    with torch.no_grad():
+        layer.in_proj.weight[0, :] = float("nan")    # first h0 entry of head 0 -> u NaN
+    with pytest.raises(RuntimeError, match="NaN detected in TTC layer solver output"):
+        layer(x, T=8)
+
+
+def test_backward_instability_raises():
+    from ttc_b200 import cuda_lqr_solve
+    args = [a.requires_grad_(True) for a in _inputs()]
+    u = cuda_lqr_solve(*args, 16)
+    dy = torch.zeros_like(u)
+    dy[2, 1, 0] = float("inf")
+    with pytest.raises(RuntimeError, match="backward pass"):
+        (u * dy).sum().backward()
+
+
+def test_cpu_tensors_rejected():
+    from ttc_b200 import cuda_lqr_solve
+    host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(2, 2, 16, 16, seed=1)]
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        cuda_lqr_solve(*host, 4)
+
+
+# ----------------------------------------------------------------------------- layer
+def _layers(cfg, dtype=torch.float32):
+    from ttc_b200 import TTCLayer
+    w = {k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()}
+    cu = TTCLayer(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank)
+    cu.load_state_dict(w)
+    return cu.to("cuda", dtype)
+
+
+@pytest.mark.parametrize("case", ["layer_cfg1", "layer_cfg2", "layer_cfg3"])
+def test_layer_matches_reference_golden(case):
+    z = load(case)
+    cfg = CONFIGS[int(z["cfg"])]
+    layer = _layers(cfg)
+    x = torch.from_numpy(z["x"]).cuda()[None].requires_grad_(True)
+    y = layer(x, T=int(z["T"]))
+    assert O.max_rel(y[0].detach().cpu(), torch.from_numpy(z["y"])) < FWD_TOL_F32
+    if "g_x" not in z:
+        return
+    (y[0] * torch.from_numpy(z["dy"]).cuda()).sum().backward()
+    assert O.max_rel(x.grad[0].cpu(), torch.from_numpy(z["g_x"])) < GRAD_TOL_F32
+    for pn, p in layer.named_parameters():
+        s = int(z["stride_" + pn])
+        assert O.max_rel(p.grad[::s].cpu(), torch.from_numpy(z["g_" + pn])) < GRAD_TOL_F32, pn
+
+
+def test_layer_bf16_matches_reference_golden():
+    z = load("layer_cfg3_bf16")
+    cfg = CONFIGS[int(z["cfg"])]
+    layer = _layers(cfg, torch.bfloat16)
+    y = layer(torch.from_numpy(z["x"]).to("cuda", torch.bfloat16)[None], T=int(z["T"]))
+    assert y.dtype == torch.bfloat16
+    assert O.max_rel(y[0].float().cpu(), torch.from_numpy(z["y"])) < FWD_TOL_BF16
+
+
+@pytest.mark.parametrize("cfg_id", [1, 2])
+def test_layer_full_config_row_slices(cfg_id):
+    """Full-size layer run (all rows of configs 1 and 2) on the GPU; rows sampled across
+    the batch are checked against the oracle layer (riccati forward, fused backward
+    restatement on a separate slice run so CPU time stays bounded)."""
+    cfg = CONFIGS[cfg_id]
+    layer = _layers(cfg)
+    x_np, dy_np = layer_input(cfg, cfg.rows)
+    x = torch.from_numpy(x_np).cuda()
+    y = layer(x.reshape(cfg.B, cfg.L * cfg.H, cfg.in_dim), T=cfg.T).reshape(cfg.rows, -1)
+    assert torch.isfinite(y).all()
+    rows = torch.linspace(0, cfg.rows - 1, 24).long()
+    ref = O.TTCLayerOracle(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
+                           solver_impl="riccati")
+    ref.load_state_dict({k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()})
+    with torch.no_grad():
+        y_ref = ref(torch.from_numpy(x_np)[rows][None], T=cfg.T)[0]
+    assert O.max_rel(y[rows].cpu(), y_ref) < FWD_TOL_F32
+
+
+def test_layer_4d_input_convention():
+    cfg = CONFIGS[1]
+    layer = _layers(cfg)
+    x = torch.randn(2, 3, cfg.H, cfg.in_dim, device="cuda")
+    y4 = layer(x, T=8)
+    y3 = layer(x.reshape(2, 3 * cfg.H, cfg.in_dim), T=8).reshape(2, 3, cfg.H, -1)
+    assert y4.shape == (2, 3, cfg.H, cfg.out_dim)
+    assert torch.equal(y4, y3)

@@ -1,0 +1,86 @@
+// Shared device helpers for the TTC LQR kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ttc {
+
+// Renormalisation threshold of the symplectic sweep (ttc/solvers/fused_lqr.py:94,
+// symplectic_iter.py:286-300) and the instability bound of the reference's checks
+// (fused_lqr.py:99-110,243-246).
+constexpr float kNormThreshold = 1e3f;
+constexpr float kUnstable = 1e6f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ldf(const float* p) { return *p; }
+__device__ __forceinline__ float ldf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void stf(float* p, float v) { *p = v; }
+__device__ __forceinline__ void stf(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+// True for NaN, +-Inf and |v| >= 1e6: the reference's isnan | isinf | abs >= 1e6.
+__device__ __forceinline__ bool unstable(float v) { return !(fabsf(v) < kUnstable); }
+
+// 1/x without the IEEE-division slow-path call (whose register save/restore spills every
+// live value of the unrolled state): the hardware approximation from __fdividef refined by
+// one Newton-Raphson step r <- r + r (1 - x r), within about 1 ulp for normal x.
+__device__ __forceinline__ float recip(float x) {
+  const float r = __fdividef(1.0f, x);
+  return fmaf(r, fmaf(-x, r, 1.0f), r);
+}
+
+// exp(lg * t) as exp2(lg * log2(e) * t); lg2 is lg pre-multiplied by log2(e).
+__device__ __forceinline__ float exp_scaled(float lg2, float t) { return exp2f(lg2 * t); }
+
+// A group of D threads owns one LQR problem (one head of one row); thread i of the
+// group holds row i of the d x d state.  D = 16 packs two groups in a warp; D = 64
+// spans two warps and synchronises with a named barrier (ids 1..15, 0 is
+// __syncthreads).
+template <int D>
+struct Group {
+  int g;          // group index in the CTA
+  int i;          // row owned by this thread
+  unsigned mask;  // lanes of this group inside its warp
+  __device__ __forceinline__ explicit Group(int tid) : g(tid / D), i(tid % D) {
+    if constexpr (D < 32) {
+      mask = ((1u << D) - 1u) << (((tid & 31) / D) * D);
+    } else {
+      mask = 0xffffffffu;
+    }
+  }
+  __device__ __forceinline__ void sync() const {
+    if constexpr (D <= 32) {
+      __syncwarp(mask);
+    } else {
+      asm volatile("bar.sync %0, %1;" ::"r"(g + 1), "r"(D) : "memory");
+    }
+  }
+};
+
+// Max over the lanes of a warp-sized row block (min(D, 32) rows).  Deterministic.
+template <int D>
+__device__ __forceinline__ float rowblock_max(const Group<D>& G, float v) {
+  constexpr int W = D < 32 ? D : 32;
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(G.mask, v, o, W));
+  return v;
+}
+
+// Sum over the D threads of a group, same fixed order on every call.  For D = 64
+// the two warp partials meet in `red` (2 floats of group scratch).
+template <int D>
+__device__ __forceinline__ float group_sum(const Group<D>& G, float v, float* red) {
+  constexpr int W = D < 32 ? D : 32;
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) v += __shfl_xor_sync(G.mask, v, o, W);
+  if constexpr (D > 32) {
+    if ((G.i & 31) == 0) red[G.i >> 5] = v;
+    G.sync();
+    v = red[0] + red[1];
+    G.sync();
+  }
+  return v;
+}
+
+}  // namespace ttc

@@ -1,0 +1,115 @@
+// Kernel launchers, explicitly instantiated per (d, du, dtype) in inst_*.cu so the
+// sm_100a build compiles in parallel; the C-ABI in ttc_abi.cu dispatches to them.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdio>
+
+#include "lqr_kernels.cuh"
+
+namespace ttc {
+
+// Records `msg` as the text returned by ttc_last_error() and returns `code`.
+int set_error(int code, const char* msg);
+
+inline int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return TTC_OK;
+  char buf[400];
+  snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
+  return set_error(TTC_ERR_CUDA, buf);
+}
+
+// Groups (heads in flight) per CTA: up to kThreads / d threads, at most one per head.
+// D > 32 groups use named barriers 1..15, and kThreads / 64 = 4 stays below that.
+inline int groups_for(int nh, int d) {
+  int g = kThreads / d;
+  if (g > nh) g = nh;
+  return g < 1 ? 1 : g;
+}
+
+template <int D, int DU, typename TIn>
+int launch_fwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+               const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N, int nh,
+               int T, void* u, float* lam0, float* M, int* status, cudaStream_t st);
+
+template <int D, int DU, typename TIn>
+int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+               const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
+               const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
+               int* status, cudaStream_t st);
+
+#ifdef TTC_DEFINE_LAUNCHERS
+template <typename Kern>
+int set_smem(Kern k, size_t bytes) {
+  if (bytes <= 48 * 1024) return TTC_OK;
+  return cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
+                    "cudaFuncSetAttribute");
+}
+
+template <int D, int DU, typename TIn>
+int launch_fwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+               const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N, int nh,
+               int T, void* u, float* lam0, float* M, int* status, cudaStream_t st) {
+  const int G = groups_for(nh, D);
+  const dim3 grid((unsigned)N), block(G * D);
+  if (M != nullptr) {
+    auto k = ttc::lqr_fwd_kernel<D, DU, TIn, true>;
+    const size_t smem = ttc::FwdLayout<D, DU, true>::bytes(G);
+    if (int rc = set_smem(k, smem)) return rc;
+    k<<<grid, block, smem, st>>>((const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R,
+                                 (const TIn*)Qf, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ,
+                                 (const TIn*)h0, nh, T, (TIn*)u, lam0, M, status);
+  } else {
+    auto k = ttc::lqr_fwd_kernel<D, DU, TIn, false>;
+    const size_t smem = ttc::FwdLayout<D, DU, false>::bytes(G);
+    if (int rc = set_smem(k, smem)) return rc;
+    k<<<grid, block, smem, st>>>((const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R,
+                                 (const TIn*)Qf, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ,
+                                 (const TIn*)h0, nh, T, (TIn*)u, lam0, nullptr, status);
+  }
+  return cuda_check(cudaGetLastError(), "lqr_fwd_kernel launch");
+}
+
+template <int D, int DU, typename TIn>
+int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+               const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
+               const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
+               int* status, cudaStream_t st) {
+  const int G = groups_for(nh, D);
+  const dim3 grid((unsigned)N), block(G * D);
+#define TTC_BWD_ARGS                                                                          \
+  (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf, (const TIn*)lA, \
+      (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0, lam0, M, (const TIn*)dU, nh, T,          \
+      (TIn*)g[0], (TIn*)g[1], (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6],      \
+      (TIn*)g[7], (TIn*)g[8], status
+  if (M == nullptr) {
+    auto k = ttc::lqr_bwd_kernel<D, DU, TIn, true>;
+    const size_t smem = ttc::BwdLayout<D, DU, true>::bytes(G);
+    if (int rc = set_smem(k, smem)) return rc;
+    k<<<grid, block, smem, st>>>(TTC_BWD_ARGS);
+  } else {
+    auto k = ttc::lqr_bwd_kernel<D, DU, TIn, false>;
+    const size_t smem = ttc::BwdLayout<D, DU, false>::bytes(G);
+    if (int rc = set_smem(k, smem)) return rc;
+    k<<<grid, block, smem, st>>>(TTC_BWD_ARGS);
+  }
+#undef TTC_BWD_ARGS
+  return cuda_check(cudaGetLastError(), "lqr_bwd_kernel launch");
+}
+
+
+#endif  // TTC_DEFINE_LAUNCHERS
+
+}  // namespace ttc
+
+#define TTC_INSTANTIATE(D, DU, TIn)                                                          \
+  template int ttc::launch_fwd<D, DU, TIn>(const void*, const void*, const void*, const void*, \
+                                           const void*, const void*, const void*, const void*, \
+                                           const void*, int64_t, int, int, void*, float*,      \
+                                           float*, int*, cudaStream_t);                        \
+  template int ttc::launch_bwd<D, DU, TIn>(const void*, const void*, const void*, const void*, \
+                                           const void*, const void*, const void*, const void*, \
+                                           const void*, const float*, const float*,            \
+                                           const void*, int64_t, int, int, void* const*, int*, \
+                                           cudaStream_t);

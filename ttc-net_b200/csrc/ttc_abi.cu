@@ -1,0 +1,106 @@
+// C-ABI entry points of include/ttc_b200.h: argument checks, kernel selection, launch.
+#include <cstdio>
+#include <mutex>
+
+#include "lqr_launch.cuh"
+#include "ttc_b200.h"
+
+// ======================================================================================
+// C-ABI
+// ======================================================================================
+namespace {
+
+std::mutex g_err_mu;
+char g_err[512] = "";
+
+int fail(int code, const char* msg) { return ttc::set_error(code, msg); }
+
+bool supported(int d, int du) { return (d == 16 && du == 16) || (d == 32 && du == 32); }
+
+int check_common(int64_t N, int nh, int d, int du, int T, int dtype) {
+  if (N < 0 || N > 0x7fffffffLL) return fail(TTC_ERR_INVALID, "N (rows) must be in [0, 2^31)");
+  if (nh < 1) return fail(TTC_ERR_INVALID, "num_heads must be >= 1");
+  if (T < 1) return fail(TTC_ERR_INVALID, "T must be >= 1");
+  if (dtype != TTC_DTYPE_F32 && dtype != TTC_DTYPE_BF16)
+    return fail(TTC_ERR_INVALID, "unknown dtype code (0 = float32, 1 = bfloat16)");
+  if (!supported(d, du)) {
+    char buf[128];
+    snprintf(buf, sizeof(buf), "no kernel for h_dim=%d u_dim=%d", d, du);
+    return fail(TTC_ERR_UNSUPPORTED, buf);
+  }
+  return TTC_OK;
+}
+
+}  // namespace
+
+int ttc::set_error(int code, const char* msg) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  snprintf(g_err, sizeof(g_err), "%s", msg);
+  return code;
+}
+
+extern "C" {
+
+int ttc_abi_version(void) { return TTC_ABI_VERSION; }
+
+int ttc_supported(int d, int du) { return supported(d, du) ? 1 : 0; }
+
+const char* ttc_last_error(void) { return g_err; }
+
+int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
+                const void* log_gamma_Q, const void* h0, int64_t N, int nh, int d, int du,
+                int T, int dtype, void* u, float* lam0, float* M, int* status, void* stream) {
+  if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (N == 0) return TTC_OK;
+  if (!A_diag || !B || !Q || !R_inv || !Q_f || !log_gamma_A || !log_gamma_B || !log_gamma_Q ||
+      !h0 || !u || !status)
+    return fail(TTC_ERR_INVALID, "null pointer argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define TTC_FWD(DD, DDU, TT)                                                                 \
+  return ttc::launch_fwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,        \
+                                 log_gamma_Q, h0, N, nh, T, u, lam0, M, status, st)
+  if (dtype == TTC_DTYPE_F32) {
+    if (d == 16) TTC_FWD(16, 16, float);
+    TTC_FWD(32, 32, float);
+  } else {
+    if (d == 16) TTC_FWD(16, 16, __nv_bfloat16);
+    TTC_FWD(32, 32, __nv_bfloat16);
+  }
+#undef TTC_FWD
+}
+
+int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
+                const void* log_gamma_Q, const void* h0, const float* lam0, const float* M,
+                const void* d_u, int64_t N, int nh, int d, int du, int T, int dtype,
+                void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_Q_f,
+                void* grad_lgA, void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status,
+                void* stream) {
+  if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (N == 0) return TTC_OK;
+  if (!A_diag || !B || !Q || !R_inv || !log_gamma_A || !log_gamma_B || !log_gamma_Q || !h0 ||
+      !d_u || !status)
+    return fail(TTC_ERR_INVALID, "null pointer argument");
+  if (M == nullptr && Q_f == nullptr)
+    return fail(TTC_ERR_INVALID, "Q_f is required when M is NULL (sweep recompute)");
+  if (M != nullptr && lam0 == nullptr)
+    return fail(TTC_ERR_INVALID, "lam0 is required together with M");
+  void* g[9] = {grad_A, grad_B, grad_Q, grad_R_inv, grad_Q_f, grad_lgA, grad_lgB, grad_lgQ, grad_h0};
+  for (void* p : g)
+    if (!p) return fail(TTC_ERR_INVALID, "null gradient pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define TTC_BWD(DD, DDU, TT)                                                                  \
+  return ttc::launch_bwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,         \
+                                 log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, st)
+  if (dtype == TTC_DTYPE_F32) {
+    if (d == 16) TTC_BWD(16, 16, float);
+    TTC_BWD(32, 32, float);
+  } else {
+    if (d == 16) TTC_BWD(16, 16, __nv_bfloat16);
+    TTC_BWD(32, 32, __nv_bfloat16);
+  }
+#undef TTC_BWD
+}
+
+}  // extern "C"

@@ -1,0 +1,129 @@
+"""TTCLayer with the B200 LQR solver -- a drop-in for ttc.TTCLayer
+(ttc/layers/ttc_layer.py:24-153): same constructor signature, parameter names, shapes
+and initialisation, so a reference ``state_dict`` loads 1:1.
+
+The prologue (in_proj, split, l2norm / softplus, low-rank B / Q / Q_f mixtures,
+ttc_layer.py:104-135) and epilogue (l2norm, out_proj, :142-150) run as PyTorch ops on
+the GPU; the LQR solve runs in libttc_b200.so through ``LQR_SOLVER_IMPL_MAP``.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .solver import LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_with_status
+from . import _lib
+
+
+def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """x / sqrt(sum(x^2) + eps) over the last dim in fp32, cast back (the formula of
+    fla.modules.l2norm used by the reference, fla/modules/l2norm.py:42)."""
+    xf = x.float()
+    return (xf * torch.rsqrt((xf * xf).sum(-1, keepdim=True) + eps)).to(x.dtype)
+
+
+class TTCLayer(nn.Module):
+    def __init__(self, in_dim: int, out_dim: int, h_dim: int, num_heads: int,
+                 b_rank: int, q_rank: int, u_dim: int | None = None,
+                 bias: bool = False, gamma_bias: bool = False, gamma_bias_init: str = "sqrt_dim",
+                 rescale: str = "l2_norm", q_reparam: str = "plain", solver_impl: str = "cuda"):
+        super().__init__()
+        if u_dim is None:
+            u_dim = h_dim
+        assert solver_impl in LQR_SOLVER_IMPL_MAP, f"Unknown LQR solver {solver_impl}"
+        self.solver_impl = solver_impl
+        self.solver = LQR_SOLVER_IMPL_MAP[solver_impl]
+        assert rescale in ["none", "l2_norm", "h0_norm"], f"Unknown rescale method {rescale}"
+        self.rescale = rescale
+        self.q_reparam = q_reparam
+        assert q_reparam in ["plain", "cholesky"], f"Unknown Q reparameterization {q_reparam}"
+        self.in_dim, self.out_dim, self.num_heads = in_dim, out_dim, num_heads
+        self.h_dim, self.u_dim, self.q_rank, self.b_rank = h_dim, u_dim, q_rank, b_rank
+
+        # Per-token projection: headwise [h0, A_diag, R_inv_diag, Qf coeffs, log-gammas]
+        # and the shared B / Q basis coefficients (ttc_layer.py:53-57).
+        self.in_proj = nn.Linear(in_dim, (4 * h_dim + 2 * u_dim + 1) * num_heads + b_rank + q_rank,
+                                 bias=bias)
+        self.out_proj = nn.Linear(u_dim * num_heads, out_dim, bias=bias)
+        self.Bs = nn.Parameter(torch.empty(b_rank, h_dim, u_dim))
+        self.Qs = nn.Parameter(torch.empty(q_rank, h_dim, h_dim))
+        self.ttc_gamma_bias_init = gamma_bias_init
+        assert gamma_bias_init in ["sqrt_dim", "zero"], f"Unknown gamma bias initialization {gamma_bias_init}"
+        self.bias_gamma = None
+        if gamma_bias:
+            self.bias_gamma = nn.Parameter(torch.empty(1 + u_dim + h_dim, dtype=torch.float32))
+        TTCLayer._init_module(self)
+
+    @staticmethod
+    def _init_module(module, std=0.02):
+        """ttc_layer.py:72-96."""
+        with torch.no_grad():
+            module.Bs.data.normal_(mean=0.0, std=std)
+            if module.q_reparam == "plain":
+                g = torch.empty_like(module.Qs).normal_(mean=0.0, std=std)
+                module.Qs.data.copy_(g @ g.transpose(1, 2) / math.sqrt(module.h_dim))
+            else:
+                module.Qs.data.normal_(mean=0.0, std=std)
+            if module.bias_gamma is not None:
+                if module.ttc_gamma_bias_init == "sqrt_dim":
+                    module.bias_gamma.data.fill_(math.log(1 / math.sqrt(module.h_dim)))
+                else:
+                    module.bias_gamma.data.fill_(0.0)
+
+    def solver_inputs(self, x2d: torch.Tensor):
+        """Prologue (ttc_layer.py:104-135): rows [N, in_dim] -> the nine solver inputs."""
+        nh, d, du = self.num_heads, self.h_dim, self.u_dim
+        gamma_split = [1, du, d]
+        head_split = [d, d, du, d, sum(gamma_split)]
+        heads, coeff_B, coeff_Q = torch.split(
+            self.in_proj(x2d), [sum(head_split) * nh, self.b_rank, self.q_rank], dim=-1)
+        h0, A_diag, R_inv_diag, coeff_Qf, log_gammas = torch.split(
+            heads.view(-1, nh, sum(head_split)), head_split, dim=-1)
+        A_diag = l2norm(A_diag)
+        coeff_B, coeff_Q, coeff_Qf = l2norm(coeff_B), l2norm(F.softplus(coeff_Q)), l2norm(F.softplus(coeff_Qf))
+        B = torch.einsum("...r,rmn->...mn", coeff_B, self.Bs)
+        if self.q_reparam == "plain":
+            Q = torch.einsum("...r,rmn->...mn", coeff_Q, self.Qs)
+            Q_f = torch.einsum("...r,rmn->...mn", coeff_Qf, self.Qs)
+        else:
+            Q = torch.einsum("...r,rmn,rkn->...mk", coeff_Q, self.Qs, self.Qs) / math.sqrt(d)
+            Q_f = torch.einsum("...r,rmn,rkn->...mk", coeff_Qf, self.Qs, self.Qs) / math.sqrt(d)
+        R_inv_diag = torch.clamp(l2norm(F.softplus(R_inv_diag)), min=1e-6)
+        if self.bias_gamma is not None:
+            log_gammas = -F.softplus(log_gammas) - F.relu(-self.bias_gamma[None, None, :])
+        else:
+            log_gammas = -F.softplus(log_gammas)
+        log_gamma_A, log_gamma_B, log_gamma_Q = torch.split(log_gammas, gamma_split, dim=-1)
+        return (A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A.squeeze(-1), log_gamma_B,
+                log_gamma_Q, h0)
+
+    def forward(self, h0: torch.Tensor, T: int) -> torch.Tensor:
+        """y = layer(x, T).  x is [bs, seq, in_dim] as in the reference; a 4-D
+        [B, L, H, in_dim] input is read as [B, L*H, in_dim] rows and returned as
+        [B, L, H, out_dim]."""
+        if h0.dim() == 4:
+            b, l, hh, _ = h0.shape
+            return self.forward(h0.reshape(b, l * hh, -1), T).reshape(b, l, hh, self.out_dim)
+        if T == 0:
+            return torch.zeros(h0.shape[0], h0.shape[1], self.out_dim, device=h0.device, dtype=h0.dtype)
+        bs, seq_len, in_dim = h0.shape
+        args = self.solver_inputs(h0.reshape(-1, in_dim))
+        if self.solver is cuda_lqr_solve:
+            u, status = lqr_solve_with_status(*args, T)
+            if status & _lib.STATUS_U_NAN:
+                raise RuntimeError(U_NAN_MSG)
+        else:
+            u = self.solver(*args, T)
+            if torch.isnan(u).any():
+                raise RuntimeError(U_NAN_MSG)
+        if self.rescale == "l2_norm":
+            u = l2norm(u)
+        elif self.rescale == "h0_norm":
+            x0 = args[-1]
+            h0_norm = torch.linalg.norm(x0, dim=-1, ord=2).detach()
+            u_norm = torch.linalg.norm(u, dim=-1, ord=2).detach()
+            u = u / u_norm[..., None] * h0_norm[..., None]
+        return self.out_proj(u.reshape(bs, seq_len, -1))

@@ -1,0 +1,185 @@
+"""``solver_impl="cuda"``: the B200 LQR solve behind TTCLayer's solver plug-in point.
+
+The reference picks its solver from a string -> callable map
+(ttc/layers/ttc_layer.py:18-22) and calls it as
+``solver(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T) -> u``
+(ttc_layer.py:137).  ``cuda_lqr_solve`` honours that signature and the behaviour of the
+reference's default ``fused`` solver (ttc/solvers/fused_lqr.py:255-304): same shapes and
+assertions, fp32 solver state, ``u`` and gradients in the inputs' dtype, symmetrised
+Q / Q_f gradients, and the same ``RuntimeError`` messages on NaN, Inf or |x| >= 1e6.
+
+The work runs in two kernels of libttc_b200.so (include/ttc_b200.h): ``ttc_lqr_fwd``
+(sweep + LU solve + first step, replacing fused_lqr.py:18-146) and ``ttc_lqr_bwd``
+(adjoint, replacing fused_lqr.py:148-253).  There is no CPU path: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+FWD_UNSTABLE_MSG = "Numerical instability detected during fused LQR forward recurrence."
+LU_UNSTABLE_MSG = "Numerical instability detected during fused LQR LU solve."
+BWD_UNSTABLE_MSG = "Numerical instability detected during fused LQR backward pass."
+U_NAN_MSG = "NaN detected in TTC layer solver output."
+
+# The backward needs d_p = Y1^-1 (Y3 du).  The forward keeps M = Y1^-1 Y3
+# ([N,nh,d,du] fp32) when it fits this budget, else the backward recomputes the sweep.
+SAVE_BUDGET_BYTES = 8 << 30
+
+_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+class KernelTimer:
+    """Opt-in CUDA-event timing of each solver launch, recorded on the launch stream.
+    ``durations_ms()`` synchronises and returns {kernel name: [ms per launch]}."""
+
+    def __init__(self):
+        self.pairs: dict[str, list] = {}
+
+    def start(self, stream):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        return ev
+
+    def stop(self, name, stream, start_ev):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        self.pairs.setdefault(name, []).append((start_ev, ev))
+
+    def durations_ms(self):
+        torch.cuda.synchronize()
+        return {k: [a.elapsed_time(b) for a, b in v] for k, v in self.pairs.items()}
+
+
+_timer: KernelTimer | None = None
+
+
+def set_kernel_timer(timer: KernelTimer | None) -> None:
+    """Install (or remove with None) the timer the solver launches report to."""
+    global _timer
+    _timer = timer
+
+
+def _launch(name, dev, fn, *args):
+    stream = torch.cuda.current_stream(dev)
+    t = _timer
+    ev = t.start(stream) if t is not None else None
+    rc = fn(*args, stream.cuda_stream)
+    if t is not None:
+        t.stop(name, stream, ev)
+    _lib.check(rc)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _check_shapes(A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T):
+    """Shape contract of fused_lqr_layer_fwd (ttc/solvers/fused_lqr.py:31-47)."""
+    assert T > 0, "T must be positive"
+    bs, nh, d = A_diag.shape
+    du = B.shape[-1]
+    assert B.shape == (bs, d, du), f"B must be [{bs},{d},{du}], got {tuple(B.shape)}"
+    assert Q.shape == (bs, d, d), f"Q must be [{bs},{d},{d}], got {tuple(Q.shape)}"
+    assert R_inv.shape == (bs, nh, du), f"R_inv must be [{bs},{nh},{du}]"
+    assert Q_f.shape == (bs, nh, d, d), f"Q_f must be [{bs},{nh},{d},{d}]"
+    assert lgA.shape == (bs, nh), f"log_gamma_A must be [{bs},{nh}]"
+    assert lgB.shape == (bs, nh, du), f"log_gamma_B must be [{bs},{nh},{du}]"
+    assert lgQ.shape == (bs, nh, d), f"log_gamma_Q must be [{bs},{nh},{d}]"
+    assert h0.shape == (bs, nh, d), f"h0 must be [{bs},{nh},{d}]"
+    return bs, nh, d, du
+
+
+def _prepare(tensors, dtype):
+    out = []
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError("ttc_b200 'cuda' solver needs CUDA tensors (there is no CPU path)")
+        out.append(t.detach().to(dtype).contiguous())
+    return out
+
+
+class LQRSolveFunction(torch.autograd.Function):
+    """Autograd wrapper of ttc_lqr_fwd / ttc_lqr_bwd (mirrors FusedLQRSolveFunc,
+    ttc/solvers/fused_lqr.py:255-291).  Returns (u, status) where status is a CPU int32
+    tensor carrying the forward's TTC_STATUS_* bits."""
+
+    @staticmethod
+    def forward(ctx, A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T, save_budget):
+        T = int(T)
+        N, nh, d, du = _check_shapes(A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T)
+        dtype = Q.dtype
+        if dtype not in _DTYPES:
+            raise TypeError(f"ttc_b200 'cuda' solver supports float32 and bfloat16, got {dtype}")
+        args = _prepare((A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0), dtype)
+        dev = Q.device
+        lib = _lib.load()
+        u = torch.empty(N, nh, du, device=dev, dtype=dtype)
+        lam0 = torch.empty(N, nh, d, device=dev, dtype=torch.float32)
+        keep_m = N * nh * d * du * 4 <= save_budget
+        M = torch.empty(N, nh, d, du, device=dev, dtype=torch.float32) if keep_m else None
+        status = torch.zeros(1, device=dev, dtype=torch.int32)
+        with torch.cuda.device(dev), torch.profiler.record_function("fwd:ttc_lqr_fwd"):
+            _launch("ttc_lqr_fwd", dev, lib.ttc_lqr_fwd, *[_ptr(a) for a in args], N, nh, d, du,
+                    T, _DTYPES[dtype], _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
+        st = int(status.item())
+        if st & _lib.STATUS_FWD_UNSTABLE:
+            raise RuntimeError(FWD_UNSTABLE_MSG)
+        if st & _lib.STATUS_LU_UNSTABLE:
+            raise RuntimeError(LU_UNSTABLE_MSG)
+        A_c, B_c, Q_c, R_c, Qf_c, lA_c, lB_c, lQ_c, h0_c = args
+        ctx.save_for_backward(A_c, B_c, Q_c, R_c, None if keep_m else Qf_c, lA_c, lB_c, lQ_c,
+                              h0_c, lam0 if keep_m else None, M)
+        ctx.dims = (N, nh, d, du, T)
+        ctx.dtype = dtype
+        ctx.in_dtypes = [t.dtype for t in (A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0)]
+        status_cpu = torch.tensor([st], dtype=torch.int32)
+        ctx.mark_non_differentiable(status_cpu)
+        return u, status_cpu
+
+    @staticmethod
+    def backward(ctx, d_u, _d_status):
+        A, B, Q, R, Qf, lA, lB, lQ, h0, lam0, M = ctx.saved_tensors
+        N, nh, d, du, T = ctx.dims
+        dtype = ctx.dtype
+        dev = Q.device
+        d_u = d_u.to(dtype).contiguous()
+        grads = [torch.empty_like(t) for t in (A, B, Q, R)]
+        grads.append(torch.empty(N, nh, d, d, device=dev, dtype=dtype))
+        grads += [torch.empty_like(t) for t in (lA, lB, lQ, h0)]
+        status = torch.zeros(1, device=dev, dtype=torch.int32)
+        lib = _lib.load()
+        with torch.cuda.device(dev), torch.profiler.record_function("bwd:ttc_lqr_bwd"):
+            _launch("ttc_lqr_bwd", dev, lib.ttc_lqr_bwd,
+                    *[_ptr(t) for t in (A, B, Q, R, Qf, lA, lB, lQ, h0)], _ptr(lam0), _ptr(M),
+                    _ptr(d_u), N, nh, d, du, T, _DTYPES[dtype], *[_ptr(g) for g in grads],
+                    _ptr(status))
+        if int(status.item()) & _lib.STATUS_BWD_UNSTABLE:
+            raise RuntimeError(BWD_UNSTABLE_MSG)
+        grads = [g.to(dt) for g, dt in zip(grads, ctx.in_dtypes)]
+        return (*grads, None, None)
+
+
+def lqr_solve_with_status(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q,
+                          h0, T, save_budget: int | None = None):
+    """Like ``cuda_lqr_solve`` but also returns the forward's status bits (host int)."""
+    budget = SAVE_BUDGET_BYTES if save_budget is None else int(save_budget)
+    u, status = LQRSolveFunction.apply(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B,
+                                       log_gamma_Q, h0, T, budget)
+    return u, int(status.item())
+
+
+def cuda_lqr_solve(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
+                   save_budget: int | None = None):
+    """Drop-in for the reference solvers (ttc_layer.py:137): returns u [N, nh, du]."""
+    return lqr_solve_with_status(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B,
+                                 log_gamma_Q, h0, T, save_budget)[0]
+
+
+# The plug-in map of ttc_layer.py:18-22.  "fused" (the reference's default name) maps to
+# the CUDA solver so TTCLayer(..., solver_impl="fused") keeps working after the switch.
+LQR_SOLVER_IMPL_MAP = {
+    "cuda": cuda_lqr_solve,
+    "fused": cuda_lqr_solve,
+}
