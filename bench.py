@@ -49,6 +49,8 @@ def parse_args(argv=None):
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--chunk-rows", type=int, default=0,
                     help="sequence rows (of L*H) per layer call inside a step (0: auto)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="sequences per GPU (0: the config's B); smaller batches for ncu captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU time of the cpu_baseline sample")
@@ -243,6 +245,9 @@ def workload_config(cfg, world, args, chunk):
 def main(argv=None):
     args = parse_args(argv)
     cfg = CONFIGS[args.config]
+    if args.batch:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, B=args.batch)
     if args.impl == "reference":
         return reference_arm(args, cfg)
     if args.warmup < 3:

@@ -1,0 +1,102 @@
+"""CPU tests of the host-side mirror of the reference interface (no GPU needed).
+
+The product's prologue / epilogue (ttc_b200.TTCLayer) runs in PyTorch; here it is
+exercised on the CPU with the oracle's solver put in place of the CUDA one, and compared
+with the reference's golden layer outputs."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ttc_oracle as O
+from ttc_cases import CONFIGS, layer_weights
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def test_registry_and_unknown_solver():
+    from ttc_b200 import LQR_SOLVER_IMPL_MAP, TTCLayer, cuda_lqr_solve
+    assert LQR_SOLVER_IMPL_MAP["cuda"] is cuda_lqr_solve
+    assert LQR_SOLVER_IMPL_MAP["fused"] is cuda_lqr_solve
+    with pytest.raises(AssertionError, match="Unknown LQR solver"):
+        TTCLayer(8, 8, 16, 2, 16, 16, solver_impl="triton")
+
+
+@pytest.mark.parametrize("kw", [{}, {"bias": True}, {"gamma_bias": True}, {"u_dim": 8},
+                                {"q_reparam": "cholesky"}])
+def test_parameters_match_reference_layout(kw):
+    """Same parameter names and shapes as ttc/layers/ttc_layer.py:56-68, so a reference
+    state_dict loads 1:1."""
+    from ttc_b200 import TTCLayer
+    a = TTCLayer(32, 24, 16, 4, 8, 16, **kw)
+    b = O.TTCLayerOracle(32, 24, 16, 4, 8, 16, **kw)
+    sa, sb = a.state_dict(), b.state_dict()
+    assert list(sa) == list(sb)
+    assert all(sa[k].shape == sb[k].shape for k in sa)
+    a.load_state_dict(sb)
+
+
+def test_init_distributions():
+    from ttc_b200 import TTCLayer
+    torch.manual_seed(0)
+    layer = TTCLayer(32, 32, 16, 8, 16, 16, gamma_bias=True)
+    assert torch.allclose(layer.Qs, layer.Qs.transpose(1, 2))
+    assert (torch.linalg.eigvalsh(layer.Qs.double()) > -1e-12).all()
+    assert abs(layer.Bs.std().item() - 0.02) < 0.002
+    assert torch.allclose(layer.bias_gamma, torch.full_like(layer.bias_gamma, -np.log(4.0)))
+
+
+def test_zero_horizon_returns_zeros():
+    from ttc_b200 import TTCLayer
+    layer = TTCLayer(32, 24, 16, 4, 16, 16)
+    y = layer(torch.randn(2, 3, 32), T=0)
+    assert y.shape == (2, 3, 24) and not y.any()
+
+
+def test_cuda_solver_rejects_cpu_tensors():
+    from ttc_b200 import cuda_lqr_solve
+    from ttc_cases import solver_inputs_synthetic
+    host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(2, 2, 16, 16, seed=1)]
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        cuda_lqr_solve(*host, 4)
+
+
+def test_solver_shape_contract():
+    from ttc_b200 import cuda_lqr_solve
+    from ttc_cases import solver_inputs_synthetic
+    host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(2, 2, 16, 16, seed=1)]
+    host[2] = host[2][:, :8]
+    with pytest.raises(AssertionError, match="Q must be"):
+        cuda_lqr_solve(*host, 4)
+
+
+@pytest.mark.parametrize("case", ["layer_cfg2", "layer_cfg3"])
+def test_product_prologue_epilogue_against_reference(case):
+    """ttc_b200.TTCLayer's own prologue/epilogue code with the oracle fused solver in the
+    solver slot reproduces the reference layer's y and gradients."""
+    from ttc_b200 import TTCLayer
+    z = np.load(os.path.join(GOLDEN, case + ".npz"))
+    cfg = CONFIGS[int(z["cfg"])]
+    layer = TTCLayer(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank)
+    layer.load_state_dict({k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()})
+    layer.solver = O.fused_solve
+    x = torch.from_numpy(z["x"])[None].requires_grad_(True)
+    y = layer(x, T=int(z["T"]))
+    assert O.max_rel(y[0], torch.from_numpy(z["y"])) < 1e-4
+    (y[0] * torch.from_numpy(z["dy"])).sum().backward()
+    assert O.max_rel(x.grad[0], torch.from_numpy(z["g_x"])) < 1e-3
+    for pn, p in layer.named_parameters():
+        s = int(z["stride_" + pn])
+        assert O.max_rel(p.grad[::s], torch.from_numpy(z["g_" + pn])) < 1e-3, pn
+
+
+def test_four_dim_input_convention():
+    from ttc_b200 import TTCLayer
+    layer = TTCLayer(8, 6, 16, 3, 16, 16)
+    layer.solver = O.fused_solve
+    x = torch.randn(2, 2, 3, 8)
+    y4 = layer(x, T=4)
+    y3 = layer(x.reshape(2, 6, 8), T=4).reshape(2, 2, 3, 6)
+    assert y4.shape == (2, 2, 3, 6)
+    assert torch.equal(y4, y3)
