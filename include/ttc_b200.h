@@ -46,6 +46,7 @@ extern "C" {
 #define TTC_STATUS_LU_UNSTABLE 2  /* pivots / P = Y1^-1 Y2       (ttc/solvers/fused_lqr.py:108-110) */
 #define TTC_STATUS_BWD_UNSTABLE 4 /* any of the nine gradients    (ttc/solvers/fused_lqr.py:243-246) */
 #define TTC_STATUS_U_NAN 8        /* NaN in u                     (ttc/layers/ttc_layer.py:139-140)  */
+#define TTC_STATUS_MMA_TIMEOUT 16 /* a tensor-core MMA did not complete within the kernel's poll limit */
 
 /* ABI version of the loaded library (== TTC_ABI_VERSION it was built with). */
 int ttc_abi_version(void);

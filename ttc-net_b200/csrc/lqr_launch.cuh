@@ -6,7 +6,7 @@
 
 #include <cstdio>
 
-#include "lqr_kernels.cuh"
+#include "lqr_tc.cuh"
 
 namespace ttc {
 
@@ -40,6 +40,26 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
                int* status, cudaStream_t st);
 
 #ifdef TTC_DEFINE_LAUNCHERS
+constexpr size_t kMaxSmem = 227 * 1024;
+
+// Tile slots per CTA for the tensor-core forward: one per 128-row tile of a row, at most
+// four (TMEM: 4 x 96 columns at d = 32), fewer if the shared-memory layout would not fit.
+template <int D, int DU, bool SAVE_M>
+int tc_slots(int nh) {
+  using CF = TcCfg<D, DU>;
+  const int tiles = (nh * D + 127) / 128;
+  int s = tiles < 4 ? tiles : 4;
+  while (s > 1 && TcFwdLayout<D, DU, SAVE_M>::bytes(s) > kMaxSmem) --s;
+  (void)sizeof(CF);
+  return s;
+}
+
+inline uint32_t tmem_cols_for(int cols) {
+  uint32_t c = 32;
+  while (c < static_cast<uint32_t>(cols)) c <<= 1;
+  return c;
+}
+
 template <typename Kern>
 int set_smem(Kern k, size_t bytes) {
   if (bytes <= 48 * 1024) return TTC_OK;
@@ -47,28 +67,31 @@ int set_smem(Kern k, size_t bytes) {
                     "cudaFuncSetAttribute");
 }
 
+template <int D, int DU, typename TIn, bool SAVE_M>
+int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+                  const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N,
+                  int nh, int T, void* u, float* lam0, float* M, int* status, cudaStream_t st) {
+  using CF = TcCfg<D, DU>;
+  const int slots = tc_slots<D, DU, SAVE_M>(nh);
+  const uint32_t cols = tmem_cols_for(slots * CF::kSlotCols);
+  const size_t smem = TcFwdLayout<D, DU, SAVE_M>::bytes(slots);
+  auto k = ttc::lqr_fwd_tc_kernel<D, DU, TIn, SAVE_M>;
+  if (int rc = set_smem(k, smem)) return rc;
+  k<<<dim3((unsigned)N), dim3(slots * 128), smem, st>>>(
+      (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf, (const TIn*)lA,
+      (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0, nh, T, cols, (TIn*)u, lam0, M, status);
+  return cuda_check(cudaGetLastError(), "lqr_fwd_tc_kernel launch");
+}
+
 template <int D, int DU, typename TIn>
 int launch_fwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N, int nh,
                int T, void* u, float* lam0, float* M, int* status, cudaStream_t st) {
-  const int G = groups_for(nh, D);
-  const dim3 grid((unsigned)N), block(G * D);
-  if (M != nullptr) {
-    auto k = ttc::lqr_fwd_kernel<D, DU, TIn, true>;
-    const size_t smem = ttc::FwdLayout<D, DU, true>::bytes(G);
-    if (int rc = set_smem(k, smem)) return rc;
-    k<<<grid, block, smem, st>>>((const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R,
-                                 (const TIn*)Qf, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ,
-                                 (const TIn*)h0, nh, T, (TIn*)u, lam0, M, status);
-  } else {
-    auto k = ttc::lqr_fwd_kernel<D, DU, TIn, false>;
-    const size_t smem = ttc::FwdLayout<D, DU, false>::bytes(G);
-    if (int rc = set_smem(k, smem)) return rc;
-    k<<<grid, block, smem, st>>>((const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R,
-                                 (const TIn*)Qf, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ,
-                                 (const TIn*)h0, nh, T, (TIn*)u, lam0, nullptr, status);
-  }
-  return cuda_check(cudaGetLastError(), "lqr_fwd_kernel launch");
+  if (M != nullptr)
+    return launch_fwd_tc<D, DU, TIn, true>(A, B, Q, R, Qf, lA, lB, lQ, h0, N, nh, T, u, lam0, M,
+                                           status, st);
+  return launch_fwd_tc<D, DU, TIn, false>(A, B, Q, R, Qf, lA, lB, lQ, h0, N, nh, T, u, lam0,
+                                          nullptr, status, st);
 }
 
 template <int D, int DU, typename TIn>

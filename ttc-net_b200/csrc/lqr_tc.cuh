@@ -1,0 +1,377 @@
+// Forward LQR solve with the symplectic sweep on the 5th-generation tensor cores.
+//
+// A tile is 128 state rows = 128 TMEM lanes = 128 / d heads of one batch row n; thread t
+// of the tile's four warps owns TMEM lane t, i.e. row (t % d) of head (t / d), and keeps
+// that row of Y1 and Y2 in registers exactly as the CUDA-core sweep does.  Each of the
+// three products of a step (symplectic_iter.py:231,233,256) is one chain of
+// tcgen05.mma kind::tf32 in 3xTF32 form (A_lo*B_hi + A_hi*B_lo + A_hi*B_hi, the
+// reference's tf32x3): the scaled state row goes to TMEM as A (hi = the fp32 value, lo
+// = its tf32 residual), the row's B, B^T and Q (shared by all heads) sit in shared memory
+// as hi/lo K-major operands, the product lands in TMEM and comes back with tcgen05.ld for
+// the per-head diagonal scalings.  A CTA runs several tiles ("slots") of the same row
+// so that one slot's MMAs overlap the others' elementwise work.
+#pragma once
+
+#include "lqr_kernels.cuh"
+#include "tc_primitives.cuh"
+
+namespace ttc {
+
+constexpr uint32_t kMaxPolls = 1u << 24;  // bounded mbarrier polls before TTC_STATUS_MMA_TIMEOUT
+
+template <int D, int DU>
+struct TcCfg {
+  static constexpr int kHeadsPerTile = 128 / D;
+  static constexpr int kMax = D > DU ? D : DU;
+  // TMEM columns of a slot: A_hi | A_lo | accumulator, 32-column aligned.
+  static constexpr int kSlotCols = (3 * kMax + 31) / 32 * 32;
+  // Operands (hi block then lo block, canonical K-major):
+  //   O1: N = DU, K = D,  (j, k) = B[k][j]   for  t  = Y2 B
+  //   O2: N = D,  K = DU, (k, j) = B[k][j]   for  dY1 = c B^T
+  //   O3: N = D,  K = D,  (k, j) = Q[j][k]   for  z  = w Q
+  static constexpr int kO1 = 0;
+  static constexpr int kO2 = kO1 + 2 * DU * D;
+  static constexpr int kO3 = kO2 + 2 * D * DU;
+  static constexpr int kOps = kO3 + 2 * D * D;
+  static constexpr int kHeader = 32;  // floats: mbarriers (8 x 8 B), TMEM base, flags
+};
+
+template <int D, int DU, bool SAVE_M>
+struct TcFwdLayout {
+  using C = TcCfg<D, DU>;
+  using G = FwdLayout<D, DU, SAVE_M>;
+  static size_t bytes(int slots) {
+    return sizeof(float) *
+           (size_t)(C::kOps + C::kHeader + slots * C::kHeadsPerTile * G::kGroup);
+  }
+};
+
+// OR of `pred` over the `count` threads of named barrier `id` (also a barrier).
+__device__ __forceinline__ bool slot_sync_or(int id, int count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+
+// Issues  acc (+)= A * Op^T  for A[128 x K] at TMEM column a_hi / a_lo and the N x K
+// operand at shared byte address op_hi / op_lo, in 3xTF32 (small terms first).
+template <int N, int K>
+__device__ __forceinline__ void issue_3xtf32(uint32_t acc, uint32_t a_hi, uint32_t a_lo,
+                                             uint32_t op_hi, uint32_t op_lo) {
+  constexpr uint32_t idesc = tc::idesc_tf32(N);
+  constexpr uint32_t lbo = N * 16, chunk = 2 * N * 16;
+  uint32_t accumulate = 0;
+#pragma unroll
+  for (int kk = 0; kk < K / 8; ++kk) {
+    const uint64_t bh = tc::smem_desc(op_hi + kk * chunk, lbo, 128);
+    const uint64_t bl = tc::smem_desc(op_lo + kk * chunk, lbo, 128);
+    tc::mma_tf32_ts(acc, a_lo + kk * 8, bh, idesc, accumulate);
+    accumulate = 1;
+    tc::mma_tf32_ts(acc, a_hi + kk * 8, bl, idesc, 1);
+  }
+#pragma unroll
+  for (int kk = 0; kk < K / 8; ++kk) {
+    const uint64_t bh = tc::smem_desc(op_hi + kk * chunk, lbo, 128);
+    tc::mma_tf32_ts(acc, a_hi + kk * 8, bh, idesc, 1);
+  }
+}
+
+// Tile context: TMEM addresses and the slot's barrier / mbarrier.
+struct TileCtx {
+  uint32_t my_hi, my_lo, my_acc;     // this thread's lane, per region
+  uint32_t t_hi, t_lo, t_acc;        // lane 0 of the tile (MMA operands)
+  uint64_t* mbar;
+  uint32_t parity;
+  int bar_id;
+  bool issuer;
+  bool timed_out;
+};
+
+// One product: A (this thread's row `a`, C columns) to TMEM, the MMA chain, result back
+// into `out`.  A timeout is agreed on slot-wide: a thread whose own wait expired marks the
+// context and carries on; the next slot barrier ORs the marks and every thread of the slot
+// returns false from the same call.
+template <int C, int N, int K>
+__device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], float (&out)[N],
+                                             uint32_t op_hi, uint32_t op_lo) {
+  static_assert(C == K && C % 8 == 0, "A width must equal K (a multiple of 8)");
+  tc::tmem_st<C>(X.my_hi, a);
+#pragma unroll
+  for (int k = 0; k < C; k += 8) {
+    tc::tmem_st8(X.my_lo + k, tc::tf32_residual(a[k]), tc::tf32_residual(a[k + 1]),
+                 tc::tf32_residual(a[k + 2]), tc::tf32_residual(a[k + 3]),
+                 tc::tf32_residual(a[k + 4]), tc::tf32_residual(a[k + 5]),
+                 tc::tf32_residual(a[k + 6]), tc::tf32_residual(a[k + 7]));
+  }
+  tc::tmem_wait_st();
+  tc::fence_before_sync();
+  if (slot_sync_or(X.bar_id, 128, X.timed_out)) {
+    X.timed_out = true;
+    return false;
+  }
+  tc::fence_after_sync();
+  if (X.issuer) {
+    issue_3xtf32<N, K>(X.t_acc, X.t_hi, X.t_lo, op_hi, op_lo);
+    tc::mma_commit(X.mbar);
+  }
+  const bool ok = tc::mbar_wait(X.mbar, X.parity, kMaxPolls);
+  X.parity ^= 1u;
+  if (!ok) {
+    X.timed_out = true;
+#pragma unroll
+    for (int j = 0; j < N; ++j) out[j] = 0.f;
+    return true;
+  }
+  tc::fence_after_sync();
+  tc::tmem_ld<N>(X.my_acc, out);
+  return true;
+}
+
+// Renormalisation of the row block (see renormalize()); returns the factor applied.
+template <int D>
+__device__ __forceinline__ float renormalize_rows(const Group<D>& G, float (&y1)[D], float (&y2)[D]) {
+  float r1 = 0.f, r2 = 0.f;
+#pragma unroll
+  for (int k = 0; k < D; ++k) {
+    r1 += fabsf(y1[k]);
+    r2 += fabsf(y2[k]);
+  }
+  const float m = rowblock_max<D>(G, fmaxf(r1, r2));
+  if (m > kNormThreshold) {
+    const float r = recip(m);
+#pragma unroll
+    for (int k = 0; k < D; ++k) {
+      y1[k] *= r;
+      y2[k] *= r;
+    }
+    return r;
+  }
+  return 1.0f;
+}
+
+// The sweep of symplectic_iter.py:226-300 for this thread's row, products on the tensor
+// cores.  Same per-step vectors, renormalisation and last-step Y3 as sweep() in
+// lqr_sweep.cuh; Y3 (when y3s is given) goes to shared memory, column j of this thread at
+// y3s[j * D + i].  Returns false, on every thread of the slot alike, after an MMA timeout.
+template <int D, int DU>
+__device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&y1)[D],
+                                         float (&y2)[D], float* y3s, const float* ops, float* vec,
+                                         float a, float lgA2, float lgQ2, float lgB2, float rinv,
+                                         int T) {
+  using V = SweepVec<D, DU>;
+  using CF = TcCfg<D, DU>;
+  const uint32_t o1h = tc::smem_u32(ops + CF::kO1), o1l = o1h + DU * D * 4;
+  const uint32_t o2h = tc::smem_u32(ops + CF::kO2), o2l = o2h + D * DU * 4;
+  const uint32_t o3h = tc::smem_u32(ops + CF::kO3), o3l = o3h + D * D * 4;
+  const int i = G.i;
+  for (int s = 0; s < T; ++s) {
+    float* v = vec + (s & 1) * V::kSize;
+    const float tau = static_cast<float>(T - s);
+    const float at = fmaf(a, exp_scaled(lgA2, tau), 1.0f);
+    v[V::kAt + i] = at;
+    v[V::kIA + i] = recip(at);
+    v[V::kDq + i] = exp_scaled(lgQ2, static_cast<float>(T - 1 - s));
+    if (i < DU) {
+      const float eb = exp_scaled(lgB2, tau);
+      v[V::kS2 + i] = eb * eb * rinv;
+      v[V::kEBR + i] = eb * rinv;
+    }
+    const bool last = (s == T - 1);
+    // t = Y2 B ; Y3 = -t EBR on the last step ; c = t * S2
+    float t[DU];
+    if (!tile_product<D, DU, D>(X, y2, t, o1h, o1l)) return false;
+    if (last && y3s != nullptr) {
+#pragma unroll
+      for (int j = 0; j < DU; ++j) y3s[j * D + i] = -t[j] * v[V::kEBR + j];
+    }
+#pragma unroll
+    for (int j = 0; j < DU; ++j) t[j] *= v[V::kS2 + j];
+    // Y1 = (Y1 + c B^T) / A
+    float u[D];
+    if (!tile_product<DU, D, DU>(X, t, u, o2h, o2l)) return false;
+#pragma unroll
+    for (int k = 0; k < D; ++k) y1[k] = (y1[k] + u[k]) * v[V::kIA + k];
+    if (!last) {
+      // Y2 = Y2 A + ((Y1 Dq) Q) Dq
+#pragma unroll
+      for (int k = 0; k < D; ++k) u[k] = y1[k] * v[V::kDq + k];
+      if (!tile_product<D, D, D>(X, u, u, o3h, o3l)) return false;
+#pragma unroll
+      for (int k = 0; k < D; ++k) y2[k] = fmaf(y2[k], v[V::kAt + k], u[k] * v[V::kDq + k]);
+      renormalize_rows<D>(G, y1, y2);
+    } else {
+#pragma unroll
+      for (int k = 0; k < D; ++k) y2[k] *= v[V::kAt + k];
+      const float r = renormalize_rows<D>(G, y1, y2);
+      if (r != 1.0f && y3s != nullptr) {
+#pragma unroll
+        for (int j = 0; j < DU; ++j) y3s[j * D + i] *= r;
+      }
+    }
+  }
+  return true;
+}
+
+template <int D, int DU, typename TIn, bool SAVE_M>
+__global__ void __launch_bounds__(512, 1)
+lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
+                  const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
+                  const TIn* __restrict__ Qf, const TIn* __restrict__ lgA,
+                  const TIn* __restrict__ lgB, const TIn* __restrict__ lgQ,
+                  const TIn* __restrict__ H0, int nh, int T, uint32_t tmem_cols,
+                  TIn* __restrict__ u_out, float* __restrict__ lam0_out, float* __restrict__ M_out,
+                  int* __restrict__ status) {
+  using CF = TcCfg<D, DU>;
+  using L = FwdLayout<D, DU, SAVE_M>;
+  extern __shared__ __align__(128) float smem[];
+  float* ops = smem;
+  uint64_t* mbars = reinterpret_cast<uint64_t*>(smem + CF::kOps);
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + CF::kOps + 16);
+  float* groups = smem + CF::kOps + CF::kHeader;
+
+  const int tid = threadIdx.x;
+  const int nslots = blockDim.x / 128;
+  const int slot = tid / 128;
+  const int lane = tid % 128;
+  const Group<D> G(tid);
+  const int64_t n = blockIdx.x;
+
+  // The row's operands, split into tf32 hi and residual.
+  for (int e = tid; e < D * DU; e += blockDim.x) {
+    const int k = e / DU, j = e % DU;
+    const float b = ldf(Bm + n * (D * DU) + e);
+    const float hi = tc::tf32_trunc(b), lo = b - hi;
+    ops[CF::kO1 + tc::canon(j, k, DU)] = hi;
+    ops[CF::kO1 + D * DU + tc::canon(j, k, DU)] = lo;
+    ops[CF::kO2 + tc::canon(k, j, D)] = hi;
+    ops[CF::kO2 + D * DU + tc::canon(k, j, D)] = lo;
+  }
+  for (int e = tid; e < D * D; e += blockDim.x) {
+    const int j = e / D, k = e % D;
+    const float q = ldf(Qm + n * (D * D) + e);
+    const float hi = tc::tf32_trunc(q);
+    ops[CF::kO3 + tc::canon(k, j, D)] = hi;
+    ops[CF::kO3 + D * D + tc::canon(k, j, D)] = q - hi;
+  }
+  if (tid == 0) {
+    for (int s = 0; s < nslots; ++s) tc::mbar_init(&mbars[s], 1);
+    tc::mbar_init_fence();
+  }
+  if (tid < 32) tc::tmem_alloc(tmem_base_s, tmem_cols);
+  tc::fence_smem_to_async();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+
+  const uint32_t tbase = *tmem_base_s;
+  TileCtx X;
+  {
+    const uint32_t col = tbase + slot * CF::kSlotCols;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * (lane / 32)) << 16;
+    X.t_hi = col;
+    X.t_lo = col + CF::kMax;
+    X.t_acc = col + 2 * CF::kMax;
+    X.my_hi = X.t_hi + lane_off;
+    X.my_lo = X.t_lo + lane_off;
+    X.my_acc = X.t_acc + lane_off;
+    X.mbar = &mbars[slot];
+    X.parity = 0;
+    X.bar_id = 1 + slot;
+    X.issuer = (lane == 0);
+    X.timed_out = false;
+  }
+  float* gs = groups + G.g * L::kGroup;
+  float* vec = gs;
+  float* rows = vec + L::kVec;
+  float* cand = rows + L::kRows;
+  float* sh0 = cand + 2 * D;
+  float* sa = sh0 + D;
+  float* slam = sa + D;
+
+  const int i = G.i;
+  const int tiles = (nh * D + 127) / 128;
+  int flags = 0;
+  for (int tile = slot; tile < tiles; tile += nslots) {
+    const int h = tile * CF::kHeadsPerTile + lane / D;
+    const bool valid = h < nh;
+    const int64_t p = n * nh + h;
+    float a = 0.f, lgA2 = 0.f, lgQ2 = 0.f, lgB2 = 0.f, rinv = 1.f, h0 = 0.f;
+    if (valid) {
+      a = ldf(A_diag + p * D + i);
+      lgA2 = ldf(lgA + p) * kLog2e;
+      lgQ2 = ldf(lgQ + p * D + i) * kLog2e;
+      h0 = ldf(H0 + p * D + i);
+      if (i < DU) {
+        lgB2 = ldf(lgB + p * DU + i) * kLog2e;
+        rinv = ldf(Rinv + p * DU + i);
+      }
+    }
+    sh0[i] = h0;
+    sa[i] = a;
+    float y1[D], y2[D];
+    const TIn* qf = Qf + (p * D + i) * D;
+#pragma unroll
+    for (int k = 0; k < D; ++k) {
+      y1[k] = (k == i) ? 1.0f : 0.0f;
+      y2[k] = valid ? ldf(qf + k) : 0.0f;
+    }
+    const bool swept = tc_sweep<D, DU>(G, X, y1, y2, SAVE_M ? rows + 2 * D * D : nullptr, ops,
+                                       vec, a, lgA2, lgQ2, lgB2, rinv, T);
+    // Uniform over the slot: a late timeout on the last product surfaces here too.
+    if (slot_sync_or(X.bar_id, 128, X.timed_out || !swept)) {
+      flags |= TTC_STATUS_MMA_TIMEOUT;
+      break;
+    }
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < D; ++k) {
+      bad |= unstable(y1[k]) | unstable(y2[k]);
+      rows[k * D + i] = y1[k];
+      rows[(D + k) * D + i] = y2[k];
+    }
+    if (bad && valid) flags |= TTC_STATUS_FWD_UNSTABLE;
+    float piv;
+    const int pc = gauss_jordan<D, L::kNR>(G, rows, cand, piv);
+    bool lbad = unstable(piv);
+    const float rpiv = recip(piv);
+    float lam0 = 0.f;
+    for (int c = 0; c < D; ++c) {
+      const float x = rows[(D + c) * D + i] * rpiv;
+      lbad |= unstable(x);
+      lam0 = fmaf(x, sh0[c], lam0);
+    }
+    if (lbad && valid) flags |= TTC_STATUS_LU_UNSTABLE;
+    if (valid && lam0_out != nullptr) lam0_out[p * D + pc] = lam0;
+    if constexpr (SAVE_M) {
+      if (valid) {
+        float* mrow = M_out + (p * D + pc) * DU;
+        for (int j = 0; j < DU; ++j) mrow[j] = rows[(2 * D + j) * D + i] * rpiv;
+      }
+    }
+    slam[pc] = lam0 * recip(fmaf(sa[pc], exp_scaled(lgA2, 1.0f), 1.0f));
+    G.sync();
+    if (valid && i < DU) {
+      float acc = 0.f;
+      for (int k = 0; k < D; ++k) {
+        // B[k][i] from the hi/lo operand O2 ((k, i) = B[k][i]).
+        const int idx = tc::canon(k, i, D);
+        acc = fmaf(ops[CF::kO2 + idx] + ops[CF::kO2 + D * DU + idx], slam[k], acc);
+      }
+      const float u = -(acc * exp_scaled(lgB2, 1.0f)) * rinv;
+      if (isnan(u)) flags |= TTC_STATUS_U_NAN;
+      stf(u_out + p * DU + i, u);
+    }
+    G.sync();
+  }
+  if (flags) atomicOr(status, flags);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (tid < 32) tc::tmem_dealloc(tbase, tmem_cols);
+}
+
+}  // namespace ttc
