@@ -43,12 +43,13 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
 constexpr size_t kMaxSmem = 227 * 1024;
 
 // Tile slots per CTA for the tensor-core forward: one per 128-row tile of a row, at most
-// four (TMEM: 4 x 96 columns at d = 32), fewer if the shared-memory layout would not fit.
+// TcLaunch<D>::kMaxSlots (TMEM: 4 x 96 columns at d = 32), fewer if the shared-memory
+// layout would not fit.
 template <int D, int DU, bool SAVE_M>
 int tc_slots(int nh) {
   using CF = TcCfg<D, DU>;
   const int tiles = (nh * D + 127) / 128;
-  int s = tiles < 4 ? tiles : 4;
+  int s = tiles < TcLaunch<D>::kMaxSlots ? tiles : TcLaunch<D>::kMaxSlots;
   while (s > 1 && TcFwdLayout<D, DU, SAVE_M>::bytes(s) > kMaxSmem) --s;
   (void)sizeof(CF);
   return s;

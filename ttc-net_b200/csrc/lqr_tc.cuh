@@ -36,6 +36,16 @@ struct TcCfg {
   static constexpr int kHeader = 32;  // floats: mbarriers (8 x 8 B), TMEM base, flags
 };
 
+// Launch shape: at d = 16 a thread needs ~80 registers, so 256-thread CTAs with three
+// resident per SM (6 tiles in flight) beat 512-thread CTAs at 128 registers (measured
+// 14 % on config 2); at d = 32 the 128-register budget of 4 tiles per SM is needed.
+template <int D>
+struct TcLaunch {
+  static constexpr int kMaxThreads = D <= 16 ? 256 : 512;
+  static constexpr int kMinBlocks = D <= 16 ? 3 : 1;
+  static constexpr int kMaxSlots = kMaxThreads / 128;
+};
+
 template <int D, int DU, bool SAVE_M>
 struct TcFwdLayout {
   using C = TcCfg<D, DU>;
@@ -59,26 +69,22 @@ __device__ __forceinline__ bool slot_sync_or(int id, int count, bool pred) {
 }
 
 // Issues  acc (+)= A * Op^T  for A[128 x K] at TMEM column a_hi / a_lo and the N x K
-// operand at shared byte address op_hi / op_lo, in 3xTF32 (small terms first).
+// operand whose K-step-0 descriptors are dh / dl, in 3xTF32 (small terms first).  Each
+// further K step of 8 is 2*N*16 bytes further on: a constant added to the descriptor's
+// start-address field.  Called by one elected lane of a warp-uniform branch, so the
+// descriptors stay in uniform registers.
 template <int N, int K>
 __device__ __forceinline__ void issue_3xtf32(uint32_t acc, uint32_t a_hi, uint32_t a_lo,
-                                             uint32_t op_hi, uint32_t op_lo) {
+                                             uint64_t dh, uint64_t dl) {
   constexpr uint32_t idesc = tc::idesc_tf32(N);
-  constexpr uint32_t lbo = N * 16, chunk = 2 * N * 16;
-  uint32_t accumulate = 0;
+  constexpr uint64_t step = (2 * N * 16) >> 4;
 #pragma unroll
   for (int kk = 0; kk < K / 8; ++kk) {
-    const uint64_t bh = tc::smem_desc(op_hi + kk * chunk, lbo, 128);
-    const uint64_t bl = tc::smem_desc(op_lo + kk * chunk, lbo, 128);
-    tc::mma_tf32_ts(acc, a_lo + kk * 8, bh, idesc, accumulate);
-    accumulate = 1;
-    tc::mma_tf32_ts(acc, a_hi + kk * 8, bl, idesc, 1);
+    tc::mma_tf32_ts(acc, a_lo + kk * 8, dh + kk * step, idesc, kk > 0);
+    tc::mma_tf32_ts(acc, a_hi + kk * 8, dl + kk * step, idesc, 1);
   }
 #pragma unroll
-  for (int kk = 0; kk < K / 8; ++kk) {
-    const uint64_t bh = tc::smem_desc(op_hi + kk * chunk, lbo, 128);
-    tc::mma_tf32_ts(acc, a_hi + kk * 8, bh, idesc, 1);
-  }
+  for (int kk = 0; kk < K / 8; ++kk) tc::mma_tf32_ts(acc, a_hi + kk * 8, dh + kk * step, idesc, 1);
 }
 
 // Tile context: TMEM addresses and the slot's barrier / mbarrier.
@@ -88,7 +94,7 @@ struct TileCtx {
   uint64_t* mbar;
   uint32_t parity;
   int bar_id;
-  bool issuer;
+  bool mma_warp;                     // warp 0 of the tile: one elected lane issues the MMAs
   bool timed_out;
 };
 
@@ -96,9 +102,13 @@ struct TileCtx {
 // into `out`.  A timeout is agreed on slot-wide: a thread whose own wait expired marks the
 // context and carries on; the next slot barrier ORs the marks and every thread of the slot
 // returns false from the same call.
-template <int C, int N, int K>
+struct NoOverlap {
+  __device__ __forceinline__ void operator()() const {}
+};
+
+template <int C, int N, int K, typename Overlap = NoOverlap>
 __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], float (&out)[N],
-                                             uint32_t op_hi, uint32_t op_lo) {
+                                             uint64_t dh, uint64_t dl, Overlap&& overlap = Overlap()) {
   static_assert(C == K && C % 8 == 0, "A width must equal K (a multiple of 8)");
   tc::tmem_st<C>(X.my_hi, a);
 #pragma unroll
@@ -115,10 +125,14 @@ __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], fl
     return false;
   }
   tc::fence_after_sync();
-  if (X.issuer) {
-    issue_3xtf32<N, K>(X.t_acc, X.t_hi, X.t_lo, op_hi, op_lo);
-    tc::mma_commit(X.mbar);
+  if (X.mma_warp) {
+    if (tc::elect_one()) {
+      issue_3xtf32<N, K>(X.t_acc, X.t_hi, X.t_lo, dh, dl);
+      tc::mma_commit(X.mbar);
+    }
+    __syncwarp();
   }
+  overlap();  // independent work while the tensor core runs
   const bool ok = tc::mbar_wait(X.mbar, X.parity, kMaxPolls);
   X.parity ^= 1u;
   if (!ok) {
@@ -135,12 +149,14 @@ __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], fl
 // Renormalisation of the row block (see renormalize()); returns the factor applied.
 template <int D>
 __device__ __forceinline__ float renormalize_rows(const Group<D>& G, float (&y1)[D], float (&y2)[D]) {
-  float r1 = 0.f, r2 = 0.f;
+  float p1[4] = {0.f, 0.f, 0.f, 0.f}, p2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int k = 0; k < D; ++k) {
-    r1 += fabsf(y1[k]);
-    r2 += fabsf(y2[k]);
+    p1[k & 3] += fabsf(y1[k]);
+    p2[k & 3] += fabsf(y2[k]);
   }
+  const float r1 = (p1[0] + p1[1]) + (p1[2] + p1[3]);
+  const float r2 = (p2[0] + p2[1]) + (p2[2] + p2[3]);
   const float m = rowblock_max<D>(G, fmaxf(r1, r2));
   if (m > kNormThreshold) {
     const float r = recip(m);
@@ -165,48 +181,96 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
                                          int T) {
   using V = SweepVec<D, DU>;
   using CF = TcCfg<D, DU>;
-  const uint32_t o1h = tc::smem_u32(ops + CF::kO1), o1l = o1h + DU * D * 4;
-  const uint32_t o2h = tc::smem_u32(ops + CF::kO2), o2l = o2h + D * DU * 4;
-  const uint32_t o3h = tc::smem_u32(ops + CF::kO3), o3l = o3h + D * D * 4;
+  // K-step-0 descriptors of the three operands (hi and lo blocks).
+  const uint32_t o1 = tc::smem_u32(ops + CF::kO1), o2 = tc::smem_u32(ops + CF::kO2),
+                 o3 = tc::smem_u32(ops + CF::kO3);
+  const uint64_t o1h = tc::smem_desc(o1, DU * 16, 128), o1l = tc::smem_desc(o1 + DU * D * 4, DU * 16, 128);
+  const uint64_t o2h = tc::smem_desc(o2, D * 16, 128), o2l = tc::smem_desc(o2 + D * DU * 4, D * 16, 128);
+  const uint64_t o3h = tc::smem_desc(o3, D * 16, 128), o3l = tc::smem_desc(o3 + D * D * 4, D * 16, 128);
   const int i = G.i;
-  for (int s = 0; s < T; ++s) {
-    float* v = vec + (s & 1) * V::kSize;
+  // Per-step column vectors of step s go to vec[(s & 1)]; step s+1's are written while
+  // step s's last product runs (they do not depend on the state).  The barrier at the
+  // start of the next product orders them before any read.
+  auto step_vectors = [&](int s) {
+    float* w = vec + (s & 1) * V::kSize;
     const float tau = static_cast<float>(T - s);
     const float at = fmaf(a, exp_scaled(lgA2, tau), 1.0f);
-    v[V::kAt + i] = at;
-    v[V::kIA + i] = recip(at);
-    v[V::kDq + i] = exp_scaled(lgQ2, static_cast<float>(T - 1 - s));
+    w[V::kAt + i] = at;
+    w[V::kIA + i] = recip(at);
+    w[V::kDq + i] = exp_scaled(lgQ2, static_cast<float>(T - 1 - s));
     if (i < DU) {
       const float eb = exp_scaled(lgB2, tau);
-      v[V::kS2 + i] = eb * eb * rinv;
-      v[V::kEBR + i] = eb * rinv;
+      w[V::kS2 + i] = eb * eb * rinv;
+      w[V::kEBR + i] = eb * rinv;
     }
+  };
+  step_vectors(0);
+  for (int s = 0; s < T; ++s) {
+    const float* v = vec + (s & 1) * V::kSize;
     const bool last = (s == T - 1);
+    const float4* v4 = reinterpret_cast<const float4*>(v);  // 16-byte aligned sections
     // t = Y2 B ; Y3 = -t EBR on the last step ; c = t * S2
     float t[DU];
     if (!tile_product<D, DU, D>(X, y2, t, o1h, o1l)) return false;
     if (last && y3s != nullptr) {
 #pragma unroll
-      for (int j = 0; j < DU; ++j) y3s[j * D + i] = -t[j] * v[V::kEBR + j];
+      for (int j4 = 0; j4 < DU / 4; ++j4) {
+        const float4 e = v4[V::kEBR / 4 + j4];
+        y3s[(4 * j4 + 0) * D + i] = -t[4 * j4 + 0] * e.x;
+        y3s[(4 * j4 + 1) * D + i] = -t[4 * j4 + 1] * e.y;
+        y3s[(4 * j4 + 2) * D + i] = -t[4 * j4 + 2] * e.z;
+        y3s[(4 * j4 + 3) * D + i] = -t[4 * j4 + 3] * e.w;
+      }
     }
 #pragma unroll
-    for (int j = 0; j < DU; ++j) t[j] *= v[V::kS2 + j];
+    for (int j4 = 0; j4 < DU / 4; ++j4) {
+      const float4 e = v4[V::kS2 / 4 + j4];
+      t[4 * j4 + 0] *= e.x;
+      t[4 * j4 + 1] *= e.y;
+      t[4 * j4 + 2] *= e.z;
+      t[4 * j4 + 3] *= e.w;
+    }
     // Y1 = (Y1 + c B^T) / A
     float u[D];
     if (!tile_product<DU, D, DU>(X, t, u, o2h, o2l)) return false;
 #pragma unroll
-    for (int k = 0; k < D; ++k) y1[k] = (y1[k] + u[k]) * v[V::kIA + k];
+    for (int k4 = 0; k4 < D / 4; ++k4) {
+      const float4 ia = v4[V::kIA / 4 + k4];
+      y1[4 * k4 + 0] = (y1[4 * k4 + 0] + u[4 * k4 + 0]) * ia.x;
+      y1[4 * k4 + 1] = (y1[4 * k4 + 1] + u[4 * k4 + 1]) * ia.y;
+      y1[4 * k4 + 2] = (y1[4 * k4 + 2] + u[4 * k4 + 2]) * ia.z;
+      y1[4 * k4 + 3] = (y1[4 * k4 + 3] + u[4 * k4 + 3]) * ia.w;
+    }
     if (!last) {
       // Y2 = Y2 A + ((Y1 Dq) Q) Dq
 #pragma unroll
-      for (int k = 0; k < D; ++k) u[k] = y1[k] * v[V::kDq + k];
-      if (!tile_product<D, D, D>(X, u, u, o3h, o3l)) return false;
+      for (int k4 = 0; k4 < D / 4; ++k4) {
+        const float4 dq = v4[V::kDq / 4 + k4];
+        u[4 * k4 + 0] = y1[4 * k4 + 0] * dq.x;
+        u[4 * k4 + 1] = y1[4 * k4 + 1] * dq.y;
+        u[4 * k4 + 2] = y1[4 * k4 + 2] * dq.z;
+        u[4 * k4 + 3] = y1[4 * k4 + 3] * dq.w;
+      }
+      if (!tile_product<D, D, D>(X, u, u, o3h, o3l, [&] { step_vectors(s + 1); })) return false;
 #pragma unroll
-      for (int k = 0; k < D; ++k) y2[k] = fmaf(y2[k], v[V::kAt + k], u[k] * v[V::kDq + k]);
+      for (int k4 = 0; k4 < D / 4; ++k4) {
+        const float4 at = v4[V::kAt / 4 + k4];
+        const float4 dq = v4[V::kDq / 4 + k4];
+        y2[4 * k4 + 0] = fmaf(y2[4 * k4 + 0], at.x, u[4 * k4 + 0] * dq.x);
+        y2[4 * k4 + 1] = fmaf(y2[4 * k4 + 1], at.y, u[4 * k4 + 1] * dq.y);
+        y2[4 * k4 + 2] = fmaf(y2[4 * k4 + 2], at.z, u[4 * k4 + 2] * dq.z);
+        y2[4 * k4 + 3] = fmaf(y2[4 * k4 + 3], at.w, u[4 * k4 + 3] * dq.w);
+      }
       renormalize_rows<D>(G, y1, y2);
     } else {
 #pragma unroll
-      for (int k = 0; k < D; ++k) y2[k] *= v[V::kAt + k];
+      for (int k4 = 0; k4 < D / 4; ++k4) {
+        const float4 at = v4[V::kAt / 4 + k4];
+        y2[4 * k4 + 0] *= at.x;
+        y2[4 * k4 + 1] *= at.y;
+        y2[4 * k4 + 2] *= at.z;
+        y2[4 * k4 + 3] *= at.w;
+      }
       const float r = renormalize_rows<D>(G, y1, y2);
       if (r != 1.0f && y3s != nullptr) {
 #pragma unroll
@@ -218,7 +282,7 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
 }
 
 template <int D, int DU, typename TIn, bool SAVE_M>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(TcLaunch<D>::kMaxThreads, TcLaunch<D>::kMinBlocks)
 lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                   const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
                   const TIn* __restrict__ Qf, const TIn* __restrict__ lgA,
@@ -282,7 +346,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     X.mbar = &mbars[slot];
     X.parity = 0;
     X.bar_id = 1 + slot;
-    X.issuer = (lane == 0);
+    X.mma_warp = (lane < 32);
     X.timed_out = false;
   }
   float* gs = groups + G.g * L::kGroup;
