@@ -100,28 +100,34 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
                const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
                const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
                int* status, cudaStream_t st) {
-  const int G = groups_for(nh, D);
-  const dim3 grid((unsigned)N), block(G * D);
-#define TTC_BWD_ARGS                                                                          \
-  (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf, (const TIn*)lA, \
-      (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0, lam0, M, (const TIn*)dU, nh, T,          \
-      (TIn*)g[0], (TIn*)g[1], (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6],      \
-      (TIn*)g[7], (TIn*)g[8], status
-  if (M == nullptr) {
-    auto k = ttc::lqr_bwd_kernel<D, DU, TIn, true>;
-    const size_t smem = ttc::BwdLayout<D, DU, true>::bytes(G);
+  if (M != nullptr) {
+    // The forward saved lambda0 and M: adjoint only, on the CUDA cores.
+    const int G = groups_for(nh, D);
+    auto k = ttc::lqr_bwd_kernel<D, DU, TIn>;
+    const size_t smem = ttc::BwdLayout<D, DU>::bytes(G);
     if (int rc = set_smem(k, smem)) return rc;
-    k<<<grid, block, smem, st>>>(TTC_BWD_ARGS);
-  } else {
-    auto k = ttc::lqr_bwd_kernel<D, DU, TIn, false>;
-    const size_t smem = ttc::BwdLayout<D, DU, false>::bytes(G);
-    if (int rc = set_smem(k, smem)) return rc;
-    k<<<grid, block, smem, st>>>(TTC_BWD_ARGS);
+    k<<<dim3((unsigned)N), dim3(G * D), smem, st>>>(
+        (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)lA, (const TIn*)lB,
+        (const TIn*)lQ, (const TIn*)h0, lam0, M, (const TIn*)dU, nh, T, (TIn*)g[0], (TIn*)g[1],
+        (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6], (TIn*)g[7], (TIn*)g[8], status);
+    return cuda_check(cudaGetLastError(), "lqr_bwd_kernel launch");
   }
-#undef TTC_BWD_ARGS
-  return cuda_check(cudaGetLastError(), "lqr_bwd_kernel launch");
+  // Recompute: the sweep again on the tensor cores, then the adjoint.
+  using CF = TcCfg<D, DU>;
+  const int tiles = (nh * D + 127) / 128;
+  int slots = tiles < TcLaunch<D>::kMaxSlots ? tiles : TcLaunch<D>::kMaxSlots;
+  while (slots > 1 && TcBwdLayout<D, DU>::bytes(slots) > kMaxSmem) --slots;
+  const uint32_t cols = tmem_cols_for(slots * CF::kSlotCols);
+  const size_t smem = TcBwdLayout<D, DU>::bytes(slots);
+  auto k = ttc::lqr_bwd_tc_kernel<D, DU, TIn>;
+  if (int rc = set_smem(k, smem)) return rc;
+  k<<<dim3((unsigned)N), dim3(slots * 128), smem, st>>>(
+      (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf, (const TIn*)lA,
+      (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0, (const TIn*)dU, nh, T, cols, (TIn*)g[0],
+      (TIn*)g[1], (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6], (TIn*)g[7],
+      (TIn*)g[8], status);
+  return cuda_check(cudaGetLastError(), "lqr_bwd_tc_kernel launch");
 }
-
 
 #endif  // TTC_DEFINE_LAUNCHERS
 

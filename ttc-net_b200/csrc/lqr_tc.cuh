@@ -146,7 +146,11 @@ __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], fl
   return true;
 }
 
-// Renormalisation of the row block (see renormalize()); returns the factor applied.
+// NORMALIZE_TYPE=2 of the reference (symplectic_iter.py:286-300): divide the row block by
+// its largest row abs-sum of Y1 or Y2 when that exceeds 1e3.  The row block is the group's
+// warp (min(d, 32) rows), the reference's BY-row tile with BY = min(d, 32); any row scaling
+// leaves P = Y1^-1 Y2 and Y1^-1 Y3 unchanged, so 1/m need not be correctly rounded.
+// Returns the factor applied.
 template <int D>
 __device__ __forceinline__ float renormalize_rows(const Group<D>& G, float (&y1)[D], float (&y2)[D]) {
   float p1[4] = {0.f, 0.f, 0.f, 0.f}, p2[4] = {0.f, 0.f, 0.f, 0.f};
@@ -170,13 +174,39 @@ __device__ __forceinline__ float renormalize_rows(const Group<D>& G, float (&y1)
   return 1.0f;
 }
 
-// The sweep of symplectic_iter.py:226-300 for this thread's row, products on the tensor
-// cores.  Same per-step vectors, renormalisation and last-step Y3 as sweep() in
-// lqr_sweep.cuh; Y3 (when y3s is given) goes to shared memory, column j of this thread at
-// y3s[j * D + i].  Returns false, on every thread of the slot alike, after an MMA timeout.
+// Where the sweep's last step puts this thread's row of Y3 = -Y2BR (symplectic_iter.py:
+// 241-243): put(j, value) per column, then scale(r) if the last renormalisation divided
+// the row block by 1/r.
+struct Y3Discard {  // the caller does not need Y3
+  __device__ __forceinline__ void put(int, float) {}
+  __device__ __forceinline__ void scale(float) {}
+};
 template <int D, int DU>
+struct Y3ToRows {  // into the Gauss-Jordan rows: column j of thread i at y3s[j * D + i]
+  float* y3s;
+  int i;
+  __device__ __forceinline__ void put(int j, float v) { y3s[j * D + i] = v; }
+  __device__ __forceinline__ void scale(float r) {
+#pragma unroll
+    for (int j = 0; j < DU; ++j) y3s[j * D + i] *= r;
+  }
+};
+template <int DU>
+struct Y3DotDu {  // contracted with the upstream gradient: acc = (Y3 d_u)_i (fused_lqr.py:185)
+  const float* du;
+  float acc;
+  __device__ __forceinline__ void put(int j, float v) { acc = fmaf(v, du[j], acc); }
+  __device__ __forceinline__ void scale(float r) { acc *= r; }
+};
+
+// The sweep of symplectic_iter.py:226-300 for this thread's row: (Y1, Y2) from (I, Q_f),
+// the three products of each step on the tensor cores, the per-head diagonal scalings and
+// the NORMALIZE_TYPE=2 renormalisation (per warp row block, see renormalize_rows) on the
+// CUDA cores, and Y3 handed to `y3` on the last step.  Returns false, on every thread of the
+// slot alike, after an MMA timeout.
+template <int D, int DU, typename Y3>
 __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&y1)[D],
-                                         float (&y2)[D], float* y3s, const float* ops, float* vec,
+                                         float (&y2)[D], Y3& y3, const float* ops, float* vec,
                                          float a, float lgA2, float lgQ2, float lgB2, float rinv,
                                          int T) {
   using V = SweepVec<D, DU>;
@@ -212,14 +242,14 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
     // t = Y2 B ; Y3 = -t EBR on the last step ; c = t * S2
     float t[DU];
     if (!tile_product<D, DU, D>(X, y2, t, o1h, o1l)) return false;
-    if (last && y3s != nullptr) {
+    if (last) {
 #pragma unroll
       for (int j4 = 0; j4 < DU / 4; ++j4) {
         const float4 e = v4[V::kEBR / 4 + j4];
-        y3s[(4 * j4 + 0) * D + i] = -t[4 * j4 + 0] * e.x;
-        y3s[(4 * j4 + 1) * D + i] = -t[4 * j4 + 1] * e.y;
-        y3s[(4 * j4 + 2) * D + i] = -t[4 * j4 + 2] * e.z;
-        y3s[(4 * j4 + 3) * D + i] = -t[4 * j4 + 3] * e.w;
+        y3.put(4 * j4 + 0, -t[4 * j4 + 0] * e.x);
+        y3.put(4 * j4 + 1, -t[4 * j4 + 1] * e.y);
+        y3.put(4 * j4 + 2, -t[4 * j4 + 2] * e.z);
+        y3.put(4 * j4 + 3, -t[4 * j4 + 3] * e.w);
       }
     }
 #pragma unroll
@@ -272,10 +302,7 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
         y2[4 * k4 + 3] *= at.w;
       }
       const float r = renormalize_rows<D>(G, y1, y2);
-      if (r != 1.0f && y3s != nullptr) {
-#pragma unroll
-        for (int j = 0; j < DU; ++j) y3s[j * D + i] *= r;
-      }
+      if (r != 1.0f) y3.scale(r);
     }
   }
   return true;
@@ -384,8 +411,14 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       y1[k] = (k == i) ? 1.0f : 0.0f;
       y2[k] = valid ? ldf(qf + k) : 0.0f;
     }
-    const bool swept = tc_sweep<D, DU>(G, X, y1, y2, SAVE_M ? rows + 2 * D * D : nullptr, ops,
-                                       vec, a, lgA2, lgQ2, lgB2, rinv, T);
+    bool swept;
+    if constexpr (SAVE_M) {
+      Y3ToRows<D, DU> y3{rows + 2 * D * D, i};
+      swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T);
+    } else {
+      Y3Discard y3;
+      swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T);
+    }
     // Uniform over the slot: a late timeout on the last product surfaces here too.
     if (slot_sync_or(X.bar_id, 128, X.timed_out || !swept)) {
       flags |= TTC_STATUS_MMA_TIMEOUT;
@@ -435,6 +468,199 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   if (flags) atomicOr(status, flags);
   tc::fence_before_sync();
   __syncthreads();
+  if (tid < 32) tc::tmem_dealloc(tbase, tmem_cols);
+}
+
+// --------------------------------------------------------------------------------------
+// Backward with the sweep recomputed on the tensor cores (no saved state beyond the
+// forward's inputs): per tile, the sweep of the forward, then Y1 [lambda0 | d_p] =
+// [Y2 h0 | Y3 d_u] in registers (fused_lqr.py:104-105,185-187), then the forward-in-time
+// adjoint per head on the CUDA cores.  grad_B / grad_Q of the row are summed over the
+// heads of a slot in head order and over slots in slot order: deterministic.
+// --------------------------------------------------------------------------------------
+template <int D, int DU>
+struct TcBwdLayout {
+  using CF = TcCfg<D, DU>;
+  static constexpr int kGroup = round4(2 * SweepVec<D, DU>::kSize + AdjLayout<D, DU>::kSize + 4 * D + 4);
+  static constexpr int kAcc = D * DU + D * D;  // per slot
+  static constexpr int kBp = round4(D * (DU + 1));
+  static constexpr int kQp = round4(D * (D + 1));
+  static constexpr int kFixed = CF::kOps + CF::kHeader + kBp + kQp;
+  static constexpr int kSlot = kAcc + CF::kHeadsPerTile * kGroup;
+  static size_t bytes(int slots) { return sizeof(float) * (size_t)(kFixed + slots * kSlot); }
+};
+
+template <int D, int DU, typename TIn>
+__global__ void __launch_bounds__(TcLaunch<D>::kMaxThreads, TcLaunch<D>::kMinBlocks)
+lqr_bwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
+                  const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
+                  const TIn* __restrict__ Qf, const TIn* __restrict__ lgA,
+                  const TIn* __restrict__ lgB, const TIn* __restrict__ lgQ,
+                  const TIn* __restrict__ H0, const TIn* __restrict__ dU, int nh, int T,
+                  uint32_t tmem_cols, TIn* __restrict__ gA_out, TIn* __restrict__ gB_out,
+                  TIn* __restrict__ gQ_out, TIn* __restrict__ gR_out, TIn* __restrict__ gQf_out,
+                  TIn* __restrict__ glgA_out, TIn* __restrict__ glgB_out,
+                  TIn* __restrict__ glgQ_out, TIn* __restrict__ gh0_out, int* __restrict__ status) {
+  using CF = TcCfg<D, DU>;
+  using L = TcBwdLayout<D, DU>;
+  extern __shared__ __align__(128) float smem[];
+  float* ops = smem;
+  uint64_t* mbars = reinterpret_cast<uint64_t*>(smem + CF::kOps);
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + CF::kOps + 16);
+  float* sBp = smem + CF::kOps + CF::kHeader;  // [D][DU+1]
+  float* sQp = sBp + L::kBp;                   // [D][D+1]
+  float* slots_base = smem + L::kFixed;
+
+  const int tid = threadIdx.x;
+  const int nslots = blockDim.x / 128;
+  const int slot = tid / 128;
+  const int lane = tid % 128;
+  const Group<D> G(tid);
+  const int64_t n = blockIdx.x;
+
+  float* accB = slots_base + slot * L::kSlot;  // [DU][D] transposed, per slot
+  float* accQ = accB + D * DU;                 // [D][D]
+  float* gs = accB + L::kAcc + (lane / D) * L::kGroup;
+  float* vec = gs;
+  float* adj = vec + 2 * SweepVec<D, DU>::kSize;
+  float* sh0 = adj + AdjLayout<D, DU>::kSize;
+  float* sdu = sh0 + D;
+  float* sx = sdu + D;
+  float* sdp = sx + D;
+  float* red = sdp + D;
+
+  bool sym_local = true;
+  for (int e = tid; e < D * DU; e += blockDim.x) {
+    const int k = e / DU, j = e % DU;
+    const float b = ldf(Bm + n * (D * DU) + e);
+    const float hi = tc::tf32_trunc(b), lo = b - hi;
+    ops[CF::kO1 + tc::canon(j, k, DU)] = hi;
+    ops[CF::kO1 + D * DU + tc::canon(j, k, DU)] = lo;
+    ops[CF::kO2 + tc::canon(k, j, D)] = hi;
+    ops[CF::kO2 + D * DU + tc::canon(k, j, D)] = lo;
+    sBp[k * (DU + 1) + j] = b;
+  }
+  for (int e = tid; e < D * D; e += blockDim.x) {
+    const int j = e / D, k = e % D;
+    const float q = ldf(Qm + n * (D * D) + e);
+    const float hi = tc::tf32_trunc(q);
+    ops[CF::kO3 + tc::canon(k, j, D)] = hi;
+    ops[CF::kO3 + D * D + tc::canon(k, j, D)] = q - hi;
+    sQp[j * (D + 1) + k] = q;
+    sym_local &= (q == ldf(Qm + n * (D * D) + k * D + j));
+  }
+  for (int e = lane; e < L::kAcc; e += 128) accB[e] = 0.0f;  // accB and accQ are contiguous
+  if (tid == 0) {
+    for (int s = 0; s < nslots; ++s) tc::mbar_init(&mbars[s], 1);
+    tc::mbar_init_fence();
+  }
+  if (tid < 32) tc::tmem_alloc(tmem_base_s, tmem_cols);
+  tc::fence_smem_to_async();
+  tc::fence_before_sync();
+  const bool sym = __syncthreads_and(sym_local);
+  tc::fence_after_sync();
+
+  const uint32_t tbase = *tmem_base_s;
+  TileCtx X;
+  {
+    const uint32_t col = tbase + slot * CF::kSlotCols;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * (lane / 32)) << 16;
+    X.t_hi = col;
+    X.t_lo = col + CF::kMax;
+    X.t_acc = col + 2 * CF::kMax;
+    X.my_hi = X.t_hi + lane_off;
+    X.my_lo = X.t_lo + lane_off;
+    X.my_acc = X.t_acc + lane_off;
+    X.mbar = &mbars[slot];
+    X.parity = 0;
+    X.bar_id = 1 + slot;
+    X.mma_warp = (lane < 32);
+    X.timed_out = false;
+  }
+
+  const int i = G.i;
+  const int hg = lane / D;  // head within the tile
+  const int tiles = (nh * D + 127) / 128;
+  int flags = 0;
+  for (int tile = slot; tile < tiles; tile += nslots) {
+    const int h = tile * CF::kHeadsPerTile + hg;
+    const bool valid = h < nh;
+    const int64_t p = n * nh + h;
+    float a = 0.f, lgA2 = 0.f, lgQ2 = 0.f, lgB2 = 0.f, rinv = 1.f, h0i = 0.f, dUi = 0.f;
+    if (valid) {
+      a = ldf(A_diag + p * D + i);
+      lgA2 = ldf(lgA + p) * kLog2e;
+      lgQ2 = ldf(lgQ + p * D + i) * kLog2e;
+      h0i = ldf(H0 + p * D + i);
+      if (i < DU) {
+        lgB2 = ldf(lgB + p * DU + i) * kLog2e;
+        rinv = ldf(Rinv + p * DU + i);
+        dUi = ldf(dU + p * DU + i);
+      }
+    }
+    sh0[i] = h0i;
+    if (i < DU) sdu[i] = dUi;
+    float y1[D], y2[D];
+    const TIn* qf = Qf + (p * D + i) * D;
+#pragma unroll
+    for (int k = 0; k < D; ++k) {
+      y1[k] = (k == i) ? 1.0f : 0.0f;
+      y2[k] = valid ? ldf(qf + k) : 0.0f;
+    }
+    // sh0 / sdu are read after the sweep's first slot barrier: visible by then.
+    Y3DotDu<DU> y3{sdu, 0.0f};
+    const bool swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T);
+    if (slot_sync_or(X.bar_id, 128, X.timed_out || !swept)) {
+      flags |= TTC_STATUS_MMA_TIMEOUT;
+      break;
+    }
+    float rhs[2] = {0.0f, y3.acc};
+#pragma unroll
+    for (int j = 0; j < D; ++j) rhs[0] = fmaf(y2[j], sh0[j], rhs[0]);
+    float piv;
+    const int pc = gauss_jordan_regs<D, 2>(G, y1, rhs, piv);
+    const float rp = recip(piv);
+    sx[pc] = rhs[0] * rp;   // lambda0 = P h0        (symplectic_iter.py:437)
+    sdp[pc] = rhs[1] * rp;  // d_p = Y1^-1 (Y3 d_u)  (fused_lqr.py:185-187)
+    G.sync();
+    const float lam = sx[i], dlam = sdp[i];
+    float gB[DU], gQ[D];
+    const bool bad = adjoint_head<D, DU, TIn>(G, valid, p, T, a, lgA2, lgQ2, lgB2, rinv, dUi, h0i,
+                                              lam, dlam, sBp, sQp, sym, adj, red, gB, gQ, gA_out,
+                                              gR_out, gQf_out, glgA_out, glgB_out, glgQ_out,
+                                              gh0_out);
+    if (bad && valid) flags |= TTC_STATUS_BWD_UNSTABLE;
+    // The slot's heads add into the slot accumulator one after the other.
+    for (int g = 0; g < CF::kHeadsPerTile; ++g) {
+      if (g == hg && valid) {
+#pragma unroll
+        for (int j = 0; j < DU; ++j) accB[j * D + i] += gB[j];
+#pragma unroll
+        for (int k = 0; k < D; ++k) accQ[k * D + i] += gQ[k];
+      }
+      tc::named_sync(X.bar_id, 128);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  // grad_B / grad_Q of the row: the slots' accumulators in slot order.
+  bool bad = false;
+  for (int e = tid; e < D * DU; e += blockDim.x) {
+    const int r = e / DU, c = e % DU;
+    float s = 0.f;
+    for (int sl = 0; sl < nslots; ++sl) s += slots_base[sl * L::kSlot + c * D + r];
+    bad |= unstable(s);
+    stf(gB_out + n * (D * DU) + e, s);
+  }
+  for (int e = tid; e < D * D; e += blockDim.x) {
+    const int r = e / D, c = e % D;
+    float s = 0.f;
+    for (int sl = 0; sl < nslots; ++sl) s += slots_base[sl * L::kSlot + D * DU + c * D + r];
+    bad |= unstable(s);
+    stf(gQ_out + n * (D * D) + e, s);
+  }
+  if (bad) flags |= TTC_STATUS_BWD_UNSTABLE;
+  if (flags) atomicOr(status, flags);
   if (tid < 32) tc::tmem_dealloc(tbase, tmem_cols);
 }
 
