@@ -20,16 +20,6 @@ __host__ __device__ constexpr int round4(int x) { return (x + 3) & ~3; }
 // --------------------------------------------------------------------------------------
 // Forward
 // --------------------------------------------------------------------------------------
-template <int D, int DU, bool SAVE_M>
-struct FwdLayout {
-  static constexpr int kNR = SAVE_M ? D + DU : D;        // right-hand sides: Y2 [| Y3]
-  static constexpr int kVec = 2 * SweepVec<D, DU>::kSize;
-  static constexpr int kRows = (D + kNR) * D;
-  static constexpr int kGroup = round4(kVec + kRows + 2 * D + 3 * D);  // + cand, h0, a, lam1
-  static constexpr int kShared = D * DU + D * D;
-  static size_t bytes(int groups) { return sizeof(float) * (size_t)(kShared + groups * kGroup); }
-};
-
 // --------------------------------------------------------------------------------------
 // Backward
 // --------------------------------------------------------------------------------------
@@ -82,26 +72,27 @@ __device__ __forceinline__ bool adjoint_head(
       // the same products give the log_gamma_Q gradient of step k-1 (:871-877).
       const float* p_hD = pb + 2 * D;
       const float* p_dhD = pb + 3 * D;
+      const float4* h4 = reinterpret_cast<const float4*>(p_hD);
+      const float4* dh4 = reinterpret_cast<const float4*>(p_dhD);
+      const float* qrow = sQp + i * (D + 1);
       float qh = 0.f, qdh = 0.f, qth = 0.f, qtdh = 0.f;
-      if (sym) {
-#pragma unroll 8
-        for (int j = 0; j < D; ++j) {
-          const float q = sQp[i * (D + 1) + j];
-          qh = fmaf(q, p_hD[j], qh);
-          qdh = fmaf(q, p_dhD[j], qdh);
+#pragma unroll
+      for (int j4 = 0; j4 < D / 4; ++j4) {
+        const float4 hv = h4[j4], dv = dh4[j4];  // broadcast 128-bit reads
+        const float q0 = qrow[4 * j4], q1 = qrow[4 * j4 + 1], q2 = qrow[4 * j4 + 2], q3 = qrow[4 * j4 + 3];
+        qh = fmaf(q0, hv.x, fmaf(q1, hv.y, fmaf(q2, hv.z, fmaf(q3, hv.w, qh))));
+        qdh = fmaf(q0, dv.x, fmaf(q1, dv.y, fmaf(q2, dv.z, fmaf(q3, dv.w, qdh))));
+        if (!sym) {
+          const int j = 4 * j4;
+          const float t0 = sQp[j * (D + 1) + i], t1 = sQp[(j + 1) * (D + 1) + i];
+          const float t2 = sQp[(j + 2) * (D + 1) + i], t3 = sQp[(j + 3) * (D + 1) + i];
+          qth = fmaf(t0, hv.x, fmaf(t1, hv.y, fmaf(t2, hv.z, fmaf(t3, hv.w, qth))));
+          qtdh = fmaf(t0, dv.x, fmaf(t1, dv.y, fmaf(t2, dv.z, fmaf(t3, dv.w, qtdh))));
         }
+      }
+      if (sym) {
         qth = qh;
         qtdh = qdh;
-      } else {
-#pragma unroll 8
-        for (int j = 0; j < D; ++j) {
-          const float q = sQp[i * (D + 1) + j];
-          const float qt = sQp[j * (D + 1) + i];
-          qh = fmaf(q, p_hD[j], qh);
-          qdh = fmaf(q, p_dhD[j], qdh);
-          qth = fmaf(qt, p_hD[j], qth);
-          qtdh = fmaf(qt, p_dhD[j], qtdh);
-        }
       }
       lam = fmaf(-dq_prev, qh, lam);
       dlam = fmaf(-dq_prev, qdh, dlam);
@@ -121,12 +112,17 @@ __device__ __forceinline__ bool adjoint_head(
     c_dlam[i] = dlam;
     G.sync();
     if (i < DU) {
+      const float4* l4 = reinterpret_cast<const float4*>(c_lam);
+      const float4* dl4 = reinterpret_cast<const float4*>(c_dlam);
       float bl = 0.f, bdl = 0.f;
-#pragma unroll 8
-      for (int r = 0; r < D; ++r) {
-        const float b = sBp[r * (DU + 1) + i];
-        bl = fmaf(b, c_lam[r], bl);
-        bdl = fmaf(b, c_dlam[r], bdl);
+#pragma unroll
+      for (int r4 = 0; r4 < D / 4; ++r4) {
+        const float4 lv = l4[r4], dv = dl4[r4];
+        const int r = 4 * r4;
+        const float b0 = sBp[r * (DU + 1) + i], b1 = sBp[(r + 1) * (DU + 1) + i];
+        const float b2 = sBp[(r + 2) * (DU + 1) + i], b3 = sBp[(r + 3) * (DU + 1) + i];
+        bl = fmaf(b0, lv.x, fmaf(b1, lv.y, fmaf(b2, lv.z, fmaf(b3, lv.w, bl))));
+        bdl = fmaf(b0, dv.x, fmaf(b1, dv.y, fmaf(b2, dv.z, fmaf(b3, dv.w, bdl))));
       }
       const float eB = exp_scaled(lgB2, ke);
       const float u = -(bl * eB) * rinv;
@@ -138,14 +134,20 @@ __device__ __forceinline__ bool adjoint_head(
       c_duE[i] = du * eB;
     }
     G.sync();
+    const float4* ue4 = reinterpret_cast<const float4*>(c_uE);
+    const float4* due4 = reinterpret_cast<const float4*>(c_duE);
+    const float* brow = sBp + i * (DU + 1);
     float bu = 0.f, bdu = 0.f;
 #pragma unroll
-    for (int j = 0; j < DU; ++j) {
-      const float b = sBp[i * (DU + 1) + j];
-      const float ue = c_uE[j], due = c_duE[j];
-      bu = fmaf(b, ue, bu);
-      bdu = fmaf(b, due, bdu);
-      gB[j] = fmaf(lam, due, fmaf(dlam, ue, gB[j]));
+    for (int j4 = 0; j4 < DU / 4; ++j4) {
+      const float4 uv = ue4[j4], dv = due4[j4];
+      const float b0 = brow[4 * j4], b1 = brow[4 * j4 + 1], b2 = brow[4 * j4 + 2], b3 = brow[4 * j4 + 3];
+      bu = fmaf(b0, uv.x, fmaf(b1, uv.y, fmaf(b2, uv.z, fmaf(b3, uv.w, bu))));
+      bdu = fmaf(b0, dv.x, fmaf(b1, dv.y, fmaf(b2, dv.z, fmaf(b3, dv.w, bdu))));
+      gB[4 * j4 + 0] = fmaf(lam, dv.x, fmaf(dlam, uv.x, gB[4 * j4 + 0]));
+      gB[4 * j4 + 1] = fmaf(lam, dv.y, fmaf(dlam, uv.y, gB[4 * j4 + 1]));
+      gB[4 * j4 + 2] = fmaf(lam, dv.z, fmaf(dlam, uv.z, gB[4 * j4 + 2]));
+      gB[4 * j4 + 3] = fmaf(lam, dv.w, fmaf(dlam, uv.w, gB[4 * j4 + 3]));
     }
     hs = fmaf(hs, At, bu);
     dh = fmaf(dh, At, bdu);
@@ -167,8 +169,16 @@ __device__ __forceinline__ bool adjoint_head(
         }
       }
     } else {
+      const float4* hD4 = reinterpret_cast<const float4*>(c_hD);
+      const float4* dhD4 = reinterpret_cast<const float4*>(c_dhD);
 #pragma unroll
-      for (int j = 0; j < D; ++j) gQ[j] = fmaf(0.5f, fmaf(hD, c_dhD[j], dhD * c_hD[j]), gQ[j]);
+      for (int j4 = 0; j4 < D / 4; ++j4) {
+        const float4 hv = hD4[j4], dv = dhD4[j4];
+        gQ[4 * j4 + 0] = fmaf(0.5f, fmaf(hD, dv.x, dhD * hv.x), gQ[4 * j4 + 0]);
+        gQ[4 * j4 + 1] = fmaf(0.5f, fmaf(hD, dv.y, dhD * hv.y), gQ[4 * j4 + 1]);
+        gQ[4 * j4 + 2] = fmaf(0.5f, fmaf(hD, dv.z, dhD * hv.z), gQ[4 * j4 + 2]);
+        gQ[4 * j4 + 3] = fmaf(0.5f, fmaf(hD, dv.w, dhD * hv.w), gQ[4 * j4 + 3]);
+      }
     }
     dq_prev = dq;
   }

@@ -1,5 +1,5 @@
 // Pieces of the symplectic Riccati sweep shared by the kernels: the per-step vector layout
-// and the in-group Gauss-Jordan solves of Y1 X = RHS.
+// and the in-group Gauss-Jordan solve of Y1 X = RHS.
 //
 // One group of D threads owns one LQR problem (row n, head h); thread i holds row i of
 // that problem's d x d state.
@@ -18,53 +18,12 @@ struct SweepVec {
   static constexpr int kSize = 3 * D + 2 * DU;
 };
 
-// Gauss-Jordan elimination with partial pivoting over the D threads of a group.
-// `rows` is (D + NR) x D floats of group shared memory, column c of thread i at
-// rows[c*D + i]: the thread's row of Y1 in columns [0,D) and of the right-hand sides in
-// [D, D+NR).  Pivot rows are never swapped: each step picks the largest |entry| in the
-// current column among the rows not yet used (first index on ties) and eliminates that
-// column from every other row.  On return the thread's row holds piv * (row `pc` of
-// Y1^-1 RHS) in [D, D+NR); the function returns pc and writes piv.  A NaN candidate
-// counts as 0, so every thread gets exactly one pivot column and all indices stay in
-// [0, D) whatever the data.
-template <int D, int NR>
-__device__ __forceinline__ int gauss_jordan(const Group<D>& G, float* rows, float* cand,
-                                            float& piv) {
-  const int i = G.i;
-  bool done = false;
-  int pc = 0;
-  piv = 1.0f;
-  for (int k = 0; k < D; ++k) {
-    float* cd = cand + (k & 1) * D;
-    cd[i] = done ? -1.0f : fmaxf(fabsf(rows[k * D + i]), 0.0f);
-    G.sync();
-    int p = 0;
-    float best = cd[0];
-    for (int r = 1; r < D; ++r) {
-      const float c = cd[r];
-      if (c > best) {
-        best = c;
-        p = r;
-      }
-    }
-    if (i == p) {
-      done = true;
-      pc = k;
-      piv = rows[k * D + i];
-    } else {
-      const float f = rows[k * D + i] * recip(rows[k * D + p]);
-      rows[k * D + i] = 0.0f;
-      for (int c = k + 1; c < D + NR; ++c) rows[c * D + i] = fmaf(-f, rows[c * D + p], rows[c * D + i]);
-    }
-  }
-  G.sync();
-  return pc;
-}
-
 // Gauss-Jordan with partial pivoting in registers (D <= 32, one group = D lanes of a
 // warp): thread i holds row i of Y1 in y1 and of NR right-hand sides in rhs; the pivot
-// row is broadcast by warp shuffles.  Pivot rule as in gauss_jordan (largest |entry| among
-// unused rows, lowest index on ties, NaN counts as 0).  On return rhs holds piv * (row pc
+// row is broadcast by warp shuffles.  Pivot rows are never swapped: each step picks the
+// largest |entry| of the current column among the rows not yet used (lowest index on
+// ties; NaN counts as 0, so every thread gets exactly one pivot column whatever the data)
+// and eliminates that column from every other row.  On return rhs holds piv * (row pc
 // of Y1^-1 RHS); returns pc and writes piv.
 template <int D, int NR>
 __device__ __forceinline__ int gauss_jordan_regs(const Group<D>& G, float (&y1)[D], float (&rhs)[NR],

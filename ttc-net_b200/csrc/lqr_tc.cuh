@@ -49,10 +49,10 @@ struct TcLaunch {
 template <int D, int DU, bool SAVE_M>
 struct TcFwdLayout {
   using C = TcCfg<D, DU>;
-  using G = FwdLayout<D, DU, SAVE_M>;
+  // per head: sweep vectors (double-buffered), h0, A_diag, lambda1 hand-over
+  static constexpr int kGroup = round4(2 * SweepVec<D, DU>::kSize + 3 * D);
   static size_t bytes(int slots) {
-    return sizeof(float) *
-           (size_t)(C::kOps + C::kHeader + slots * C::kHeadsPerTile * G::kGroup);
+    return sizeof(float) * (size_t)(C::kOps + C::kHeader + slots * C::kHeadsPerTile * kGroup);
   }
 };
 
@@ -181,16 +181,6 @@ struct Y3Discard {  // the caller does not need Y3
   __device__ __forceinline__ void put(int, float) {}
   __device__ __forceinline__ void scale(float) {}
 };
-template <int D, int DU>
-struct Y3ToRows {  // into the Gauss-Jordan rows: column j of thread i at y3s[j * D + i]
-  float* y3s;
-  int i;
-  __device__ __forceinline__ void put(int j, float v) { y3s[j * D + i] = v; }
-  __device__ __forceinline__ void scale(float r) {
-#pragma unroll
-    for (int j = 0; j < DU; ++j) y3s[j * D + i] *= r;
-  }
-};
 template <int DU>
 struct Y3DotDu {  // contracted with the upstream gradient: acc = (Y3 d_u)_i (fused_lqr.py:185)
   const float* du;
@@ -318,7 +308,8 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                   TIn* __restrict__ u_out, float* __restrict__ lam0_out, float* __restrict__ M_out,
                   int* __restrict__ status) {
   using CF = TcCfg<D, DU>;
-  using L = FwdLayout<D, DU, SAVE_M>;
+  using L = TcFwdLayout<D, DU, SAVE_M>;
+  using V = SweepVec<D, DU>;
   extern __shared__ __align__(128) float smem[];
   float* ops = smem;
   uint64_t* mbars = reinterpret_cast<uint64_t*>(smem + CF::kOps);
@@ -378,11 +369,8 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   }
   float* gs = groups + G.g * L::kGroup;
   float* vec = gs;
-  float* rows = vec + L::kVec;
-  float* cand = rows + L::kRows;
-  float* sh0 = cand + 2 * D;
-  float* sa = sh0 + D;
-  float* slam = sa + D;
+  float* sh0 = vec + 2 * V::kSize;
+  float* slam = sh0 + D;
 
   const int i = G.i;
   const int tiles = (nh * D + 127) / 128;
@@ -403,7 +391,6 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       }
     }
     sh0[i] = h0;
-    sa[i] = a;
     float y1[D], y2[D];
     const TIn* qf = Qf + (p * D + i) * D;
 #pragma unroll
@@ -411,14 +398,8 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       y1[k] = (k == i) ? 1.0f : 0.0f;
       y2[k] = valid ? ldf(qf + k) : 0.0f;
     }
-    bool swept;
-    if constexpr (SAVE_M) {
-      Y3ToRows<D, DU> y3{rows + 2 * D * D, i};
-      swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T);
-    } else {
-      Y3Discard y3;
-      swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T);
-    }
+    Y3Discard y3;  // M is formed from P below instead of from Y3
+    const bool swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T);
     // Uniform over the slot: a late timeout on the last product surfaces here too.
     if (slot_sync_or(X.bar_id, 128, X.timed_out || !swept)) {
       flags |= TTC_STATUS_MMA_TIMEOUT;
@@ -426,37 +407,51 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     }
     bool bad = false;
 #pragma unroll
-    for (int k = 0; k < D; ++k) {
-      bad |= unstable(y1[k]) | unstable(y2[k]);
-      rows[k * D + i] = y1[k];
-      rows[(D + k) * D + i] = y2[k];
-    }
+    for (int k = 0; k < D; ++k) bad |= unstable(y1[k]) | unstable(y2[k]);
     if (bad && valid) flags |= TTC_STATUS_FWD_UNSTABLE;
+    // P = Y1^-1 Y2 (fused_lqr.py:104-105): this thread ends up with row pc of P in y2.
     float piv;
-    const int pc = gauss_jordan<D, L::kNR>(G, rows, cand, piv);
+    const int pc = gauss_jordan_regs<D, D>(G, y1, y2, piv);
     bool lbad = unstable(piv);
     const float rpiv = recip(piv);
     float lam0 = 0.f;
+#pragma unroll
     for (int c = 0; c < D; ++c) {
-      const float x = rows[(D + c) * D + i] * rpiv;
-      lbad |= unstable(x);
-      lam0 = fmaf(x, sh0[c], lam0);
+      y2[c] *= rpiv;
+      lbad |= unstable(y2[c]);
+      lam0 = fmaf(y2[c], sh0[c], lam0);  // lambda0 = P h0 (symplectic_iter.py:437)
     }
     if (lbad && valid) flags |= TTC_STATUS_LU_UNSTABLE;
     if (valid && lam0_out != nullptr) lam0_out[p * D + pc] = lam0;
+    // The last sweep step had tau = 1: its vectors hold 1/A_1 and exp(lgB) R_inv.
+    const float* v1 = vec + ((T - 1) & 1) * V::kSize;
+    slam[pc] = lam0 * v1[V::kIA + pc];  // lambda1 = lambda0 / A_1 (:472-477)
     if constexpr (SAVE_M) {
+      // M = Y1^-1 Y3 with Y3 = -Y2_{T-1} B_1 R_inv and Y2 = Y2_{T-1} A_1 on the last step,
+      // so M = -(P A_1^-1) B diag(exp(lgB) R_inv): one more tensor-core product.
+      using CF2 = TcCfg<D, DU>;
+      const uint32_t o1 = tc::smem_u32(ops + CF2::kO1);
+      float w[D], m[DU];
+#pragma unroll
+      for (int k = 0; k < D; ++k) w[k] = y2[k] * v1[V::kIA + k];
+      if (!tile_product<D, DU, D>(X, w, m, tc::smem_desc(o1, DU * 16, 128),
+                                  tc::smem_desc(o1 + DU * D * 4, DU * 16, 128)) ||
+          slot_sync_or(X.bar_id, 128, X.timed_out)) {
+        flags |= TTC_STATUS_MMA_TIMEOUT;
+        break;
+      }
       if (valid) {
         float* mrow = M_out + (p * D + pc) * DU;
-        for (int j = 0; j < DU; ++j) mrow[j] = rows[(2 * D + j) * D + i] * rpiv;
+#pragma unroll
+        for (int j = 0; j < DU; ++j) mrow[j] = -m[j] * v1[V::kEBR + j];
       }
     }
-    slam[pc] = lam0 * recip(fmaf(sa[pc], exp_scaled(lgA2, 1.0f), 1.0f));
     G.sync();
     if (valid && i < DU) {
+      // u = -R_inv * (B diag(e^lgB))^T lambda1   (symplectic_iter.py:488-517)
       float acc = 0.f;
       for (int k = 0; k < D; ++k) {
-        // B[k][i] from the hi/lo operand O2 ((k, i) = B[k][i]).
-        const int idx = tc::canon(k, i, D);
+        const int idx = tc::canon(k, i, D);  // B[k][i] from the hi/lo operand O2
         acc = fmaf(ops[CF::kO2 + idx] + ops[CF::kO2 + D * DU + idx], slam[k], acc);
       }
       const float u = -(acc * exp_scaled(lgB2, 1.0f)) * rinv;
