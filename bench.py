@@ -167,9 +167,8 @@ def run_step(layer, x, dy, T, chunk, world):
         y = layer(x[:, s:s + chunk], T)
         y.backward(dy[:, s:s + chunk])
     if world > 1:
-        import torch.distributed as dist
-        for p in layer.parameters():
-            dist.all_reduce(p.grad)
+        from ttc_b200.parallel import allreduce_grads
+        allreduce_grads(layer)
 
 
 # ------------------------------------------------------------------------- CPU legs
@@ -329,9 +328,8 @@ def main(argv=None):
             y = layer(x[:, s:s + chunk], cfg.T)
             y.backward(dy[:, s:s + chunk])
         if world > 1:
-            import torch.distributed as dist
-            for p in layer.parameters():
-                dist.all_reduce(p.grad)
+            from ttc_b200.parallel import allreduce_grads
+            allreduce_grads(layer)
         dx_host.copy_(x.grad.view(cfg.rows, cfg.in_dim), non_blocking=True)
 
     e2e_step(0)

@@ -39,14 +39,29 @@ struct AdjLayout {
 // `valid`), and returns the head's grad_B row i (transposed into gB, pre-scaled by
 // exp(lgB t)) and grad_Q row i (gQ) for the caller's reduction over heads.  Returns true if
 // any written gradient is NaN, Inf or >= 1e6.
-template <int D, int DU, typename TIn>
+template <int D, int DU, typename TIn, bool kCache>
 __device__ __forceinline__ bool adjoint_head(
     const Group<D>& G, bool valid, int64_t p, int T, float a, float lgA2, float lgQ2, float lgB2,
     float rinv, float dUi, float h0i, float lam, float dlam, const float* sBp, const float* sQp,
     bool sym, float* adj, float* red, float (&gB)[DU], float (&gQ)[D], TIn* gA_out, TIn* gR_out,
     TIn* gQf_out, TIn* glgA_out, TIn* glgB_out, TIn* glgQ_out, TIn* gh0_out) {
   constexpr int kAdjB = AdjLayout<D, DU>::kBuf;
+  // kCache: the thread's row of Q, row of B and column of B (constant for the head) are
+  // held in registers (2d + du of them) instead of being re-read from shared memory every
+  // step; the caller decides whether its register budget allows it.
   const int i = G.i;
+  float qrow_r[kCache ? D : 1], brow_r[kCache ? DU : 1], bcol_r[kCache ? D : 1];
+  if constexpr (kCache) {
+#pragma unroll
+    for (int j = 0; j < D; ++j) qrow_r[j] = sQp[i * (D + 1) + j];
+#pragma unroll
+    for (int j = 0; j < DU; ++j) brow_r[j] = sBp[i * (DU + 1) + j];
+#pragma unroll
+    for (int r = 0; r < D; ++r) bcol_r[r] = i < DU ? sBp[r * (DU + 1) + i] : 0.f;
+  }
+  auto qrow = [&](int j) { if constexpr (kCache) return qrow_r[j]; else return sQp[i * (D + 1) + j]; };
+  auto brow = [&](int j) { if constexpr (kCache) return brow_r[j]; else return sBp[i * (DU + 1) + j]; };
+  auto bcol = [&](int r) { if constexpr (kCache) return bcol_r[r]; else return sBp[r * (DU + 1) + i]; };
   float hs = h0i, dh = 0.f;
   float gA = 0.f, glgA = 0.f, glgQ = 0.f, gR = 0.f, glgB = 0.f, gh0 = 0.f;
 #pragma unroll
@@ -74,26 +89,32 @@ __device__ __forceinline__ bool adjoint_head(
       const float* p_dhD = pb + 3 * D;
       const float4* h4 = reinterpret_cast<const float4*>(p_hD);
       const float4* dh4 = reinterpret_cast<const float4*>(p_dhD);
-      const float* qrow = sQp + i * (D + 1);
-      float qh = 0.f, qdh = 0.f, qth = 0.f, qtdh = 0.f;
+      // Four independent partial sums per dot product keep the FMA chains short.
+      float ph[4] = {0.f, 0.f, 0.f, 0.f}, pd[4] = {0.f, 0.f, 0.f, 0.f};
+      float pth[4] = {0.f, 0.f, 0.f, 0.f}, ptd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j4 = 0; j4 < D / 4; ++j4) {
         const float4 hv = h4[j4], dv = dh4[j4];  // broadcast 128-bit reads
-        const float q0 = qrow[4 * j4], q1 = qrow[4 * j4 + 1], q2 = qrow[4 * j4 + 2], q3 = qrow[4 * j4 + 3];
-        qh = fmaf(q0, hv.x, fmaf(q1, hv.y, fmaf(q2, hv.z, fmaf(q3, hv.w, qh))));
-        qdh = fmaf(q0, dv.x, fmaf(q1, dv.y, fmaf(q2, dv.z, fmaf(q3, dv.w, qdh))));
+        const float q[4] = {qrow(4 * j4), qrow(4 * j4 + 1), qrow(4 * j4 + 2), qrow(4 * j4 + 3)};
+        const float hh[4] = {hv.x, hv.y, hv.z, hv.w}, dd[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          ph[c] = fmaf(q[c], hh[c], ph[c]);
+          pd[c] = fmaf(q[c], dd[c], pd[c]);
+        }
         if (!sym) {
-          const int j = 4 * j4;
-          const float t0 = sQp[j * (D + 1) + i], t1 = sQp[(j + 1) * (D + 1) + i];
-          const float t2 = sQp[(j + 2) * (D + 1) + i], t3 = sQp[(j + 3) * (D + 1) + i];
-          qth = fmaf(t0, hv.x, fmaf(t1, hv.y, fmaf(t2, hv.z, fmaf(t3, hv.w, qth))));
-          qtdh = fmaf(t0, dv.x, fmaf(t1, dv.y, fmaf(t2, dv.z, fmaf(t3, dv.w, qtdh))));
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float qt = sQp[(4 * j4 + c) * (D + 1) + i];
+            pth[c] = fmaf(qt, hh[c], pth[c]);
+            ptd[c] = fmaf(qt, dd[c], ptd[c]);
+          }
         }
       }
-      if (sym) {
-        qth = qh;
-        qtdh = qdh;
-      }
+      const float qh = (ph[0] + ph[1]) + (ph[2] + ph[3]);
+      const float qdh = (pd[0] + pd[1]) + (pd[2] + pd[3]);
+      const float qth = sym ? qh : (pth[0] + pth[1]) + (pth[2] + pth[3]);
+      const float qtdh = sym ? qdh : (ptd[0] + ptd[1]) + (ptd[2] + ptd[3]);
       lam = fmaf(-dq_prev, qh, lam);
       dlam = fmaf(-dq_prev, qdh, dlam);
       glgQ = fmaf(0.5f * fmaf(dh, qh + qth, hs * (qdh + qtdh)), static_cast<float>(k) * dq_prev, glgQ);
@@ -114,16 +135,20 @@ __device__ __forceinline__ bool adjoint_head(
     if (i < DU) {
       const float4* l4 = reinterpret_cast<const float4*>(c_lam);
       const float4* dl4 = reinterpret_cast<const float4*>(c_dlam);
-      float bl = 0.f, bdl = 0.f;
+      float pl[4] = {0.f, 0.f, 0.f, 0.f}, pdl[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int r4 = 0; r4 < D / 4; ++r4) {
         const float4 lv = l4[r4], dv = dl4[r4];
-        const int r = 4 * r4;
-        const float b0 = sBp[r * (DU + 1) + i], b1 = sBp[(r + 1) * (DU + 1) + i];
-        const float b2 = sBp[(r + 2) * (DU + 1) + i], b3 = sBp[(r + 3) * (DU + 1) + i];
-        bl = fmaf(b0, lv.x, fmaf(b1, lv.y, fmaf(b2, lv.z, fmaf(b3, lv.w, bl))));
-        bdl = fmaf(b0, dv.x, fmaf(b1, dv.y, fmaf(b2, dv.z, fmaf(b3, dv.w, bdl))));
+        const float ll[4] = {lv.x, lv.y, lv.z, lv.w}, dd[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float b = bcol(4 * r4 + c);
+          pl[c] = fmaf(b, ll[c], pl[c]);
+          pdl[c] = fmaf(b, dd[c], pdl[c]);
+        }
       }
+      const float bl = (pl[0] + pl[1]) + (pl[2] + pl[3]);
+      const float bdl = (pdl[0] + pdl[1]) + (pdl[2] + pdl[3]);
       const float eB = exp_scaled(lgB2, ke);
       const float u = -(bl * eB) * rinv;
       float du = -(bdl * eB) * rinv;
@@ -136,19 +161,26 @@ __device__ __forceinline__ bool adjoint_head(
     G.sync();
     const float4* ue4 = reinterpret_cast<const float4*>(c_uE);
     const float4* due4 = reinterpret_cast<const float4*>(c_duE);
-    const float* brow = sBp + i * (DU + 1);
-    float bu = 0.f, bdu = 0.f;
+    float pu[4] = {0.f, 0.f, 0.f, 0.f}, pdu[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j4 = 0; j4 < DU / 4; ++j4) {
       const float4 uv = ue4[j4], dv = due4[j4];
-      const float b0 = brow[4 * j4], b1 = brow[4 * j4 + 1], b2 = brow[4 * j4 + 2], b3 = brow[4 * j4 + 3];
-      bu = fmaf(b0, uv.x, fmaf(b1, uv.y, fmaf(b2, uv.z, fmaf(b3, uv.w, bu))));
-      bdu = fmaf(b0, dv.x, fmaf(b1, dv.y, fmaf(b2, dv.z, fmaf(b3, dv.w, bdu))));
+      const float b0 = brow(4 * j4), b1 = brow(4 * j4 + 1), b2 = brow(4 * j4 + 2), b3 = brow(4 * j4 + 3);
+      pu[0] = fmaf(b0, uv.x, pu[0]);
+      pu[1] = fmaf(b1, uv.y, pu[1]);
+      pu[2] = fmaf(b2, uv.z, pu[2]);
+      pu[3] = fmaf(b3, uv.w, pu[3]);
+      pdu[0] = fmaf(b0, dv.x, pdu[0]);
+      pdu[1] = fmaf(b1, dv.y, pdu[1]);
+      pdu[2] = fmaf(b2, dv.z, pdu[2]);
+      pdu[3] = fmaf(b3, dv.w, pdu[3]);
       gB[4 * j4 + 0] = fmaf(lam, dv.x, fmaf(dlam, uv.x, gB[4 * j4 + 0]));
       gB[4 * j4 + 1] = fmaf(lam, dv.y, fmaf(dlam, uv.y, gB[4 * j4 + 1]));
       gB[4 * j4 + 2] = fmaf(lam, dv.z, fmaf(dlam, uv.z, gB[4 * j4 + 2]));
       gB[4 * j4 + 3] = fmaf(lam, dv.w, fmaf(dlam, uv.w, gB[4 * j4 + 3]));
     }
+    const float bu = (pu[0] + pu[1]) + (pu[2] + pu[3]);
+    const float bdu = (pdu[0] + pdu[1]) + (pdu[2] + pdu[3]);
     hs = fmaf(hs, At, bu);
     dh = fmaf(dh, At, bdu);
     const float dq = exp_scaled(lgQ2, ke);
@@ -171,17 +203,20 @@ __device__ __forceinline__ bool adjoint_head(
     } else {
       const float4* hD4 = reinterpret_cast<const float4*>(c_hD);
       const float4* dhD4 = reinterpret_cast<const float4*>(c_dhD);
+      // (h dh^T + dh h^T) scaled by Dq on both sides; the 1/2 is applied once at the end.
 #pragma unroll
       for (int j4 = 0; j4 < D / 4; ++j4) {
         const float4 hv = hD4[j4], dv = dhD4[j4];
-        gQ[4 * j4 + 0] = fmaf(0.5f, fmaf(hD, dv.x, dhD * hv.x), gQ[4 * j4 + 0]);
-        gQ[4 * j4 + 1] = fmaf(0.5f, fmaf(hD, dv.y, dhD * hv.y), gQ[4 * j4 + 1]);
-        gQ[4 * j4 + 2] = fmaf(0.5f, fmaf(hD, dv.z, dhD * hv.z), gQ[4 * j4 + 2]);
-        gQ[4 * j4 + 3] = fmaf(0.5f, fmaf(hD, dv.w, dhD * hv.w), gQ[4 * j4 + 3]);
+        gQ[4 * j4 + 0] = fmaf(hD, dv.x, fmaf(dhD, hv.x, gQ[4 * j4 + 0]));
+        gQ[4 * j4 + 1] = fmaf(hD, dv.y, fmaf(dhD, hv.y, gQ[4 * j4 + 1]));
+        gQ[4 * j4 + 2] = fmaf(hD, dv.z, fmaf(dhD, hv.z, gQ[4 * j4 + 2]));
+        gQ[4 * j4 + 3] = fmaf(hD, dv.w, fmaf(dhD, hv.w, gQ[4 * j4 + 3]));
       }
     }
     dq_prev = dq;
   }
+#pragma unroll
+  for (int j = 0; j < D; ++j) gQ[j] *= 0.5f;
   const float glgA_sum = group_sum<D>(G, glgA, red);
   if (valid) {
     bad |= unstable(gA) | unstable(glgQ) | unstable(gh0);
@@ -215,8 +250,19 @@ struct BwdLayout {
   static size_t bytes(int groups) { return sizeof(float) * (size_t)(kShared + groups * kGroup); }
 };
 
+// Resident CTAs per SM asked of ptxas for the saved-state backward (registers per thread
+// <= 65536 / (256 * n)).
+#ifndef TTC_BWD_MINB16
+#define TTC_BWD_MINB16 2
+#endif
+#ifndef TTC_BWD_MINB32
+#define TTC_BWD_MINB32 2
+#endif
+template <int D>
+constexpr int bwd_min_ctas() { return D <= 16 ? TTC_BWD_MINB16 : TTC_BWD_MINB32; }
+
 template <int D, int DU, typename TIn>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, bwd_min_ctas<D>())
 lqr_bwd_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
                const TIn* __restrict__ lgA, const TIn* __restrict__ lgB,
@@ -273,7 +319,7 @@ lqr_bwd_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     float dlam = 0.f;
     for (int j = 0; j < DU; ++j) dlam = fmaf(mrow[j], sdu[j], dlam);
     float gB[DU], gQ[D];
-    const bool bad = adjoint_head<D, DU, TIn>(G, true, p, T, a, lgA2, lgQ2, lgB2, rinv, dUi, h0i,
+    const bool bad = adjoint_head<D, DU, TIn, (D <= 16)>(G, true, p, T, a, lgA2, lgQ2, lgB2, rinv, dUi, h0i,
                                               lam, dlam, sBp, sQp, sym, adj, red, gB, gQ, gA_out,
                                               gR_out, gQf_out, glgA_out, glgB_out, glgQ_out, gh0_out);
 #pragma unroll

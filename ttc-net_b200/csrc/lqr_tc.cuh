@@ -620,7 +620,7 @@ lqr_bwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     G.sync();
     const float lam = sx[i], dlam = sdp[i];
     float gB[DU], gQ[D];
-    const bool bad = adjoint_head<D, DU, TIn>(G, valid, p, T, a, lgA2, lgQ2, lgB2, rinv, dUi, h0i,
+    const bool bad = adjoint_head<D, DU, TIn, false>(G, valid, p, T, a, lgA2, lgQ2, lgB2, rinv, dUi, h0i,
                                               lam, dlam, sBp, sQp, sym, adj, red, gB, gQ, gA_out,
                                               gR_out, gQf_out, glgA_out, glgB_out, glgQ_out,
                                               gh0_out);
