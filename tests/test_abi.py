@@ -45,7 +45,9 @@ def test_abi_version(lib):
 def test_supported_shapes(lib):
     assert lib.ttc_supported(16, 16) == 1
     assert lib.ttc_supported(32, 32) == 1
+    assert lib.ttc_supported(64, 64) == 1
     assert lib.ttc_supported(24, 24) == 0
+    assert lib.ttc_supported(32, 16) == 0
 
 
 def _fwd(lib, N=1, nh=1, d=16, du=16, T=4, dtype=0, null_inputs=False):
@@ -79,5 +81,5 @@ def test_bwd_rejects_bad_arguments_without_gpu(lib):
     assert bwd(M=None, Qf=None) == _lib.ERR_INVALID        # recompute needs Q_f
     assert bwd(lam0=None) == _lib.ERR_INVALID              # M without lam0
     assert bwd(grads=None) == _lib.ERR_INVALID
-    assert bwd(d=64, du=64) == _lib.ERR_UNSUPPORTED
+    assert bwd(d=48, du=48) == _lib.ERR_UNSUPPORTED
     assert bwd(N=0) == _lib.OK

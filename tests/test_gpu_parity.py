@@ -21,9 +21,9 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 GRAD_NAMES = ["g_" + n for n in SOLVER_ARG_NAMES]
 FWD_TOL_F32, FWD_TOL_BF16, GRAD_TOL_F32 = 1e-4, 2e-2, 1e-3
 
-# d = 64 has no kernel yet: its fixtures are not run here.
-SOLVER_CASES = ["solver_bench_d16", "solver_synth_d32", "solver_T1", "solver_T2",
-                "solver_growth", "prologue_cfg1", "prologue_cfg2", "prologue_cfg3"]
+SOLVER_CASES = ["solver_bench_d16", "solver_synth_d32", "solver_synth_d64", "solver_T1",
+                "solver_T2", "solver_growth", "prologue_cfg1", "prologue_cfg2", "prologue_cfg3",
+                "prologue_cfg4"]
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -66,7 +66,8 @@ def test_solver_matches_reference_golden(case, save_budget):
 
 
 @pytest.mark.parametrize("d,nh,N,T", [(16, 16, 24, 64), (16, 3, 7, 33), (16, 20, 5, 16),
-                                      (32, 32, 6, 128), (32, 5, 9, 40), (32, 1, 3, 7)])
+                                      (32, 32, 6, 128), (32, 5, 9, 40), (32, 1, 3, 7),
+                                      (64, 3, 2, 24), (64, 1, 3, 5)])
 def test_solver_matches_oracle_seeded(d, nh, N, T):
     """Seeded synthetic problems, head counts that leave CTA groups idle, odd sizes."""
     host = [torch.from_numpy(a) for a in solver_inputs_synthetic(N, nh, d, d, seed=100 + d + nh)]
@@ -188,7 +189,7 @@ def _layers(cfg, dtype=torch.float32):
     return cu.to("cuda", dtype)
 
 
-@pytest.mark.parametrize("case", ["layer_cfg1", "layer_cfg2", "layer_cfg3"])
+@pytest.mark.parametrize("case", ["layer_cfg1", "layer_cfg2", "layer_cfg3", "layer_cfg4"])
 def test_layer_matches_reference_golden(case):
     z = load(case)
     cfg = CONFIGS[int(z["cfg"])]

@@ -1,0 +1,5 @@
+// Kernel instantiations for h_dim = u_dim = 64, float activations.
+#define TTC_DEFINE_LAUNCHERS
+#include "lqr_launch.cuh"
+
+TTC_INSTANTIATE(64, 64, float)

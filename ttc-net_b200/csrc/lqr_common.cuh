@@ -35,8 +35,7 @@ __device__ __forceinline__ float exp_scaled(float lg2, float t) { return exp2f(l
 
 // A group of D threads owns one LQR problem (one head of one row); thread i of the
 // group holds row i of the d x d state.  D = 16 packs two groups in a warp; D = 64
-// spans two warps and synchronises with a named barrier (ids 1..15, 0 is
-// __syncthreads).
+// spans two warps and synchronises with a named barrier (0 is __syncthreads).
 template <int D>
 struct Group {
   int g;          // group index in the CTA
@@ -49,11 +48,13 @@ struct Group {
       mask = 0xffffffffu;
     }
   }
+  // D > 32: named barrier 8 + g (the tensor-core kernels use ids 1..4 for their tile
+  // slots; a CTA has at most 8 such groups).
   __device__ __forceinline__ void sync() const {
     if constexpr (D <= 32) {
       __syncwarp(mask);
     } else {
-      asm volatile("bar.sync %0, %1;" ::"r"(g + 1), "r"(D) : "memory");
+      asm volatile("bar.sync %0, %1;" ::"r"(g + 8), "r"(D) : "memory");
     }
   }
 };

@@ -259,7 +259,7 @@ struct BwdLayout {
 #define TTC_BWD_MINB32 2
 #endif
 template <int D>
-constexpr int bwd_min_ctas() { return D <= 16 ? TTC_BWD_MINB16 : TTC_BWD_MINB32; }
+constexpr int bwd_min_ctas() { return D <= 16 ? TTC_BWD_MINB16 : (D <= 32 ? TTC_BWD_MINB32 : 1); }
 
 template <int D, int DU, typename TIn>
 __global__ void __launch_bounds__(kThreads, bwd_min_ctas<D>())

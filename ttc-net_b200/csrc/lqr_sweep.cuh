@@ -64,4 +64,89 @@ __device__ __forceinline__ int gauss_jordan_regs(const Group<D>& G, float (&y1)[
   return pc;
 }
 
+// The same elimination for a group spanning several warps (D = 64): the pivot search
+// combines the warps' shuffle results through shared memory and the pivot row is published
+// in a double-buffered shared row.  pbuf holds GjBcast<D, NR>::kSize floats.
+template <int D, int NR>
+struct GjBcast {
+  static constexpr int kRow = D + NR;
+  static constexpr int kSize = 2 * kRow + 4 * (D / 32);
+};
+
+template <int D, int NR>
+__device__ __forceinline__ int gauss_jordan_bcast(const Group<D>& G, float (&y1)[D], float (&rhs)[NR],
+                                                  float& piv, float* pbuf) {
+  constexpr int kWarps = D / 32;
+  const int i = G.i, w = i >> 5;
+  float* cbuf = pbuf + 2 * GjBcast<D, NR>::kRow;
+  bool done = false;
+  int pc = 0;
+  piv = 1.0f;
+#pragma unroll
+  for (int k = 0; k < D; ++k) {
+    float bv = done ? -1.0f : fmaxf(fabsf(y1[k]), 0.0f);
+    int bi = i;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    float* cb = cbuf + (k & 1) * 2 * kWarps;
+    if ((i & 31) == 0) {
+      cb[2 * w] = bv;
+      cb[2 * w + 1] = __int_as_float(bi);
+    }
+    G.sync();
+    bv = cb[0];
+    bi = __float_as_int(cb[1]);
+#pragma unroll
+    for (int ww = 1; ww < kWarps; ++ww) {
+      const float ov = cb[2 * ww];
+      const int oi = __float_as_int(cb[2 * ww + 1]);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    const bool me = (i == bi);
+    float* pr = pbuf + (k & 1) * GjBcast<D, NR>::kRow;
+    if (me) {
+#pragma unroll
+      for (int c = k; c < D; ++c) pr[c] = y1[c];
+#pragma unroll
+      for (int c = 0; c < NR; ++c) pr[D + c] = rhs[c];
+      done = true;
+      pc = k;
+      piv = y1[k];
+    }
+    G.sync();
+    if (!me) {
+      const float f = y1[k] * recip(pr[k]);
+      y1[k] = 0.0f;
+#pragma unroll
+      for (int c = k + 1; c < D; ++c) y1[c] = fmaf(-f, pr[c], y1[c]);
+#pragma unroll
+      for (int c = 0; c < NR; ++c) rhs[c] = fmaf(-f, pr[D + c], rhs[c]);
+    }
+  }
+  G.sync();
+  return pc;
+}
+
+// Register Gauss-Jordan for any supported D; pbuf (GjBcast<D, NR>::kSize floats of group
+// shared memory) is only touched when the group spans several warps.
+template <int D, int NR>
+__device__ __forceinline__ int gauss_jordan_group(const Group<D>& G, float (&y1)[D], float (&rhs)[NR],
+                                                  float& piv, float* pbuf) {
+  if constexpr (D <= 32) {
+    return gauss_jordan_regs<D, NR>(G, y1, rhs, piv);
+  } else {
+    return gauss_jordan_bcast<D, NR>(G, y1, rhs, piv, pbuf);
+  }
+}
+
 }  // namespace ttc

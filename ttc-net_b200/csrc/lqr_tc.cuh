@@ -39,9 +39,11 @@ struct TcCfg {
 // Launch shape: at d = 16 a thread needs ~80 registers, so 256-thread CTAs with three
 // resident per SM (6 tiles in flight) beat 512-thread CTAs at 128 registers (measured
 // 14 % on config 2); at d = 32 the 128-register budget of 4 tiles per SM is needed.
+// At d = 64 a thread holds two 64-wide state rows plus a product row (~220 registers):
+// 256-thread CTAs, one per SM.
 template <int D>
 struct TcLaunch {
-  static constexpr int kMaxThreads = D <= 16 ? 256 : 512;
+  static constexpr int kMaxThreads = D == 32 ? 512 : 256;
   static constexpr int kMinBlocks = D <= 16 ? 3 : 1;
   static constexpr int kMaxSlots = kMaxThreads / 128;
 };
@@ -49,8 +51,10 @@ struct TcLaunch {
 template <int D, int DU, bool SAVE_M>
 struct TcFwdLayout {
   using C = TcCfg<D, DU>;
-  // per head: sweep vectors (double-buffered), h0, A_diag, lambda1 hand-over
-  static constexpr int kGroup = round4(2 * SweepVec<D, DU>::kSize + 3 * D);
+  // per head: sweep vectors (double-buffered), h0, lambda1 hand-over, spare, and the
+  // pivot-row buffer of the cross-warp Gauss-Jordan (d = 64 only)
+  static constexpr int kPb = D > 32 ? GjBcast<D, D>::kSize : 0;
+  static constexpr int kGroup = round4(2 * SweepVec<D, DU>::kSize + 3 * D + kPb);
   static size_t bytes(int slots) {
     return sizeof(float) * (size_t)(C::kOps + C::kHeader + slots * C::kHeadsPerTile * kGroup);
   }
@@ -371,6 +375,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   float* vec = gs;
   float* sh0 = vec + 2 * V::kSize;
   float* slam = sh0 + D;
+  float* pbuf = sh0 + 3 * D;
 
   const int i = G.i;
   const int tiles = (nh * D + 127) / 128;
@@ -411,7 +416,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     if (bad && valid) flags |= TTC_STATUS_FWD_UNSTABLE;
     // P = Y1^-1 Y2 (fused_lqr.py:104-105): this thread ends up with row pc of P in y2.
     float piv;
-    const int pc = gauss_jordan_regs<D, D>(G, y1, y2, piv);
+    const int pc = gauss_jordan_group<D, D>(G, y1, y2, piv, pbuf);
     bool lbad = unstable(piv);
     const float rpiv = recip(piv);
     float lam0 = 0.f;
@@ -476,7 +481,9 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
 template <int D, int DU>
 struct TcBwdLayout {
   using CF = TcCfg<D, DU>;
-  static constexpr int kGroup = round4(2 * SweepVec<D, DU>::kSize + AdjLayout<D, DU>::kSize + 4 * D + 4);
+  static constexpr int kPb = D > 32 ? GjBcast<D, 2>::kSize : 0;
+  static constexpr int kGroup =
+      round4(2 * SweepVec<D, DU>::kSize + AdjLayout<D, DU>::kSize + 4 * D + 4 + kPb);
   static constexpr int kAcc = D * DU + D * D;  // per slot
   static constexpr int kBp = round4(D * (DU + 1));
   static constexpr int kQp = round4(D * (D + 1));
@@ -523,6 +530,7 @@ lqr_bwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   float* sx = sdu + D;
   float* sdp = sx + D;
   float* red = sdp + D;
+  float* pbuf = red + 4;
 
   bool sym_local = true;
   for (int e = tid; e < D * DU; e += blockDim.x) {
@@ -613,7 +621,7 @@ lqr_bwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
 #pragma unroll
     for (int j = 0; j < D; ++j) rhs[0] = fmaf(y2[j], sh0[j], rhs[0]);
     float piv;
-    const int pc = gauss_jordan_regs<D, 2>(G, y1, rhs, piv);
+    const int pc = gauss_jordan_group<D, 2>(G, y1, rhs, piv, pbuf);
     const float rp = recip(piv);
     sx[pc] = rhs[0] * rp;   // lambda0 = P h0        (symplectic_iter.py:437)
     sdp[pc] = rhs[1] * rp;  // d_p = Y1^-1 (Y3 d_u)  (fused_lqr.py:185-187)

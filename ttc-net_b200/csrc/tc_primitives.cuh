@@ -127,7 +127,13 @@ __device__ __forceinline__ void tmem_st<32>(uint32_t taddr, const float (&v)[32]
       : "memory");
 }
 
-// 8 columns starting at element `off` of v.
+template <>
+__device__ __forceinline__ void tmem_st<64>(uint32_t taddr, const float (&v)[64]) {
+  tmem_st<32>(taddr, *reinterpret_cast<const float(*)[32]>(&v[0]));
+  tmem_st<32>(taddr + 32, *reinterpret_cast<const float(*)[32]>(&v[32]));
+}
+
+// 8 consecutive columns.
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, float v0, float v1, float v2, float v3,
                                          float v4, float v5, float v6, float v7) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
@@ -166,6 +172,11 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<64>(uint32_t taddr, float (&v)[64]) {
+  tmem_ld<32>(taddr, *reinterpret_cast<float(*)[32]>(&v[0]));
+  tmem_ld<32>(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 

@@ -15,7 +15,7 @@ char g_err[512] = "";
 
 int fail(int code, const char* msg) { return ttc::set_error(code, msg); }
 
-bool supported(int d, int du) { return (d == 16 && du == 16) || (d == 32 && du == 32); }
+bool supported(int d, int du) { return du == d && (d == 16 || d == 32 || d == 64); }
 
 int check_common(int64_t N, int nh, int d, int du, int T, int dtype) {
   if (N < 0 || N > 0x7fffffffLL) return fail(TTC_ERR_INVALID, "N (rows) must be in [0, 2^31)");
@@ -62,10 +62,12 @@ int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_
                                  log_gamma_Q, h0, N, nh, T, u, lam0, M, status, st)
   if (dtype == TTC_DTYPE_F32) {
     if (d == 16) TTC_FWD(16, 16, float);
-    TTC_FWD(32, 32, float);
+    if (d == 32) TTC_FWD(32, 32, float);
+    TTC_FWD(64, 64, float);
   } else {
     if (d == 16) TTC_FWD(16, 16, __nv_bfloat16);
-    TTC_FWD(32, 32, __nv_bfloat16);
+    if (d == 32) TTC_FWD(32, 32, __nv_bfloat16);
+    TTC_FWD(64, 64, __nv_bfloat16);
   }
 #undef TTC_FWD
 }
@@ -95,10 +97,12 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
                                  log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, st)
   if (dtype == TTC_DTYPE_F32) {
     if (d == 16) TTC_BWD(16, 16, float);
-    TTC_BWD(32, 32, float);
+    if (d == 32) TTC_BWD(32, 32, float);
+    TTC_BWD(64, 64, float);
   } else {
     if (d == 16) TTC_BWD(16, 16, __nv_bfloat16);
-    TTC_BWD(32, 32, __nv_bfloat16);
+    if (d == 32) TTC_BWD(32, 32, __nv_bfloat16);
+    TTC_BWD(64, 64, __nv_bfloat16);
   }
 #undef TTC_BWD
 }
