@@ -243,3 +243,43 @@ def test_layer_4d_input_convention():
     y3 = layer(x.reshape(2, 3 * cfg.H, cfg.in_dim), T=8).reshape(2, 3, cfg.H, -1)
     assert y4.shape == (2, 3, cfg.H, cfg.out_dim)
     assert torch.equal(y4, y3)
+
+
+@pytest.mark.parametrize("kw", [{"bias": True}, {"gamma_bias": True},
+                                {"gamma_bias": True, "gamma_bias_init": "zero"},
+                                {"q_reparam": "cholesky"}, {"rescale": "h0_norm"},
+                                {"rescale": "none"}], ids=lambda kw: "-".join(f"{k}={v}" for k, v in kw.items()))
+def test_layer_options_match_oracle(kw):
+    """Non-default TTCLayer options (ttc_layer.py:56-68,121-123,129-130,144-147) through the
+    CUDA solver against the oracle layer (fused restatement, fp64)."""
+    from ttc_b200 import TTCLayer
+    torch.manual_seed(11)
+    cu = TTCLayer(24, 20, 16, 4, 8, 16, **kw)
+    ref = O.TTCLayerOracle(24, 20, 16, 4, 8, 16, solver_impl="fused", **kw).double()
+    with torch.no_grad():
+        if cu.bias_gamma is not None:
+            cu.bias_gamma.uniform_(-1.0, 0.5)
+        if cu.in_proj.bias is not None:
+            cu.in_proj.bias.normal_(0.0, 0.1)
+    ref.load_state_dict({k: v.double() for k, v in cu.state_dict().items()})
+    cu = cu.cuda()
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(2, 5, 24, generator=g)
+    dy = torch.randn(2, 5, 20, generator=g)
+    xc = x.cuda().requires_grad_(True)
+    y = cu(xc, T=24)
+    y.backward(dy.cuda())
+    xr = x.double().requires_grad_(True)
+    yr = ref(xr, T=24)
+    yr.backward(dy.double())
+    assert O.max_rel(y.detach().cpu(), yr) < FWD_TOL_F32
+    assert O.max_rel(xc.grad.cpu(), xr.grad) < GRAD_TOL_F32
+    for (n1, p1), (n2, p2) in zip(cu.named_parameters(), ref.named_parameters()):
+        assert O.max_rel(p1.grad.cpu(), p2.grad) < GRAD_TOL_F32, n1
+
+
+def test_unsupported_state_dims_raise():
+    from ttc_b200 import TTCLayer
+    layer = TTCLayer(8, 8, 16, 2, 16, 16, u_dim=8).cuda()
+    with pytest.raises(NotImplementedError, match="u_dim=8"):
+        layer(torch.randn(1, 2, 8, device="cuda"), T=4)
