@@ -75,8 +75,8 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu: str):
+        self.gpu = gpu
         self.proc = None
         self.lines = []
 
@@ -124,6 +124,21 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_selector(local: int) -> str:
+    """nvidia-smi -i argument for this process's GPU: its UUID (immune to
+    CUDA_VISIBLE_DEVICES renumbering), else the visible-device entry, else the index."""
+    try:
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        if u:
+            return u if u.startswith("GPU-") else "GPU-" + u
+    except (AttributeError, RuntimeError):
+        pass
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        return vis.split(",")[local].strip()
+    return str(local)
 
 
 # ------------------------------------------------------------------------- setup
@@ -291,8 +306,7 @@ def main(argv=None):
 
     # ---- device-resident timed region
     timer = KernelTimer()
-    phys = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
-        if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    phys = gpu_selector(local)
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(phys) as clocks:
