@@ -75,19 +75,25 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu: str):
+    def __init__(self, gpu: str, startup_s: float = 30.0):
         self.gpu = gpu
+        self.startup_s = startup_s
         self.proc = None
         self.lines = []
+        self.err = ""
+        self.first = threading.Event()
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200", "-i", str(self.gpu)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi needs up to seconds to initialise on a many-GPU box; the timed
+            # region starts only after its first sample so that short runs are covered.
+            self.first.wait(self.startup_s)
         except (OSError, ValueError):
             self.proc = None
         return self
@@ -95,6 +101,8 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+            self.first.set()
+        self.first.set()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -104,10 +112,16 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.thread.join(timeout=2)
+            try:
+                self.err = (self.proc.stderr.read() or "").strip().splitlines()[-1:]
+            except (OSError, ValueError):
+                self.err = []
 
     def summary(self):
         if not self.lines:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            why = "; ".join(self.err) if self.err else "no sample"
+            return {"sm_mhz": None, "sm_max_mhz": None,
+                    "reasons": [f"nvidia-smi unavailable ({why}, -i {self.gpu})"]}
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
@@ -307,9 +321,9 @@ def main(argv=None):
     # ---- device-resident timed region
     timer = KernelTimer()
     phys = gpu_selector(local)
-    barrier()
-    torch.cuda.synchronize()
     with ClockSampler(phys) as clocks:
+        barrier()
+        torch.cuda.synchronize()
         set_kernel_timer(timer)
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
@@ -321,6 +335,14 @@ def main(argv=None):
         set_kernel_timer(None)
     barrier()
     ms = max_over_ranks(start.elapsed_time(end))
+    clock_summary = clocks.summary()
+    if world > 1:
+        import torch.distributed as dist
+        every = [None] * world
+        dist.all_gather_object(every, clock_summary)
+        clock_summary = dict(clock_summary)
+        clock_summary["reasons"] = sorted({r for c in every for r in c["reasons"]})
+        clock_summary["sm_mhz_per_rank"] = [c["sm_mhz"] for c in every]
     tokens_per_step = cfg.tokens * world
     value = tokens_per_step * args.steps / (ms / 1000.0)
     kern = timer.durations_ms()
@@ -369,7 +391,7 @@ def main(argv=None):
         bwd_ms = kern.get("ttc_lqr_bwd", [float("nan")])
         calls_per_step = math.ceil(rows / chunk)
         probs_per_launch = cfg.problems / calls_per_step
-        sm_max = clocks.summary().get("sm_max_mhz") or 1965.0
+        sm_max = clock_summary.get("sm_max_mhz") or 1965.0
         fp32_peak = SM_COUNT_B200 * FP32_LANES_PER_SM * 2 * sm_max * 1e6 / 1e12
         fwd_tflops = fwd_f * probs_per_launch / (statistics.mean(fwd_ms) / 1e3) / 1e12
         bwd_tflops = bwd_f * probs_per_launch / (statistics.mean(bwd_ms) / 1e3) / 1e12
@@ -397,7 +419,7 @@ def main(argv=None):
                                 "tflops": bwd_tflops,
                                 "frac_fp32_peak": bwd_tflops / fp32_peak},
             },
-            "clocks": clocks.summary(),
+            "clocks": clock_summary,
             "e2e": {"value": tokens_per_step * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches * world,
