@@ -30,6 +30,49 @@ __device__ __forceinline__ float recip(float x) {
   return fmaf(r, fmaf(-x, r, 1.0f), r);
 }
 
+// Paired fp32 arithmetic (PTX `fma/add/mul.rn.f32x2`, sm_100a): one instruction performs
+// two independent fp32 operations, each rounded exactly like its scalar counterpart, so a
+// kernel written with pairs gives bitwise the results of the scalar code in the same order
+// while issuing half the instructions.  A pair lives in one 64-bit register (x = low half).
+using f2 = unsigned long long;
+__device__ __forceinline__ f2 pk2(float x, float y) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ f2 dup2(float x) { return pk2(x, x); }
+__device__ __forceinline__ void up2(f2 v, float& x, float& y) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v));
+}
+__device__ __forceinline__ float sum2(f2 v) {
+  float x, y;
+  up2(v, x, y);
+  return x + y;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// The two halves of a float4 (broadcast shared-memory reads come as float4).
+__device__ __forceinline__ f2 lo2(const float4& v) { return pk2(v.x, v.y); }
+__device__ __forceinline__ f2 hi2(const float4& v) { return pk2(v.z, v.w); }
+
 // exp(lg * t) as exp2(lg * log2(e) * t); lg2 is lg pre-multiplied by log2(e).
 __device__ __forceinline__ float exp_scaled(float lg2, float t) { return exp2f(lg2 * t); }
 

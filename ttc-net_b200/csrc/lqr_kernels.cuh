@@ -45,29 +45,39 @@ __device__ __forceinline__ bool adjoint_head(
     float rinv, float dUi, float h0i, float lam, float dlam, const float* sBp, const float* sQp,
     bool sym, float* adj, float* red, float (&gB)[DU], float (&gQ)[D], TIn* gA_out, TIn* gR_out,
     TIn* gQf_out, TIn* glgA_out, TIn* glgB_out, TIn* glgQ_out, TIn* gh0_out) {
+  static_assert(D % 4 == 0 && DU % 4 == 0, "dimensions must be multiples of 4");
   constexpr int kAdjB = AdjLayout<D, DU>::kBuf;
+  // The matrix-vector products and the rank-2 gradient updates run on fp32 pairs (two
+  // columns per instruction) in the summation order of four interleaved partial sums.
   // kCache: the thread's row of Q, row of B and column of B (constant for the head) are
   // held in registers (2d + du of them) instead of being re-read from shared memory every
   // step; the caller decides whether its register budget allows it.
   const int i = G.i;
-  float qrow_r[kCache ? D : 1], brow_r[kCache ? DU : 1], bcol_r[kCache ? D : 1];
+  f2 qrow_r[kCache ? D / 2 : 1], brow_r[kCache ? DU / 2 : 1], bcol_r[kCache ? D / 2 : 1];
+  auto ld_qrow = [&](int j2) { return pk2(sQp[i * (D + 1) + 2 * j2], sQp[i * (D + 1) + 2 * j2 + 1]); };
+  auto ld_brow = [&](int j2) { return pk2(sBp[i * (DU + 1) + 2 * j2], sBp[i * (DU + 1) + 2 * j2 + 1]); };
+  auto ld_bcol = [&](int r2) {
+    return i < DU ? pk2(sBp[2 * r2 * (DU + 1) + i], sBp[(2 * r2 + 1) * (DU + 1) + i]) : f2(0);
+  };
   if constexpr (kCache) {
 #pragma unroll
-    for (int j = 0; j < D; ++j) qrow_r[j] = sQp[i * (D + 1) + j];
+    for (int j2 = 0; j2 < D / 2; ++j2) qrow_r[j2] = ld_qrow(j2);
 #pragma unroll
-    for (int j = 0; j < DU; ++j) brow_r[j] = sBp[i * (DU + 1) + j];
+    for (int j2 = 0; j2 < DU / 2; ++j2) brow_r[j2] = ld_brow(j2);
 #pragma unroll
-    for (int r = 0; r < D; ++r) bcol_r[r] = i < DU ? sBp[r * (DU + 1) + i] : 0.f;
+    for (int r2 = 0; r2 < D / 2; ++r2) bcol_r[r2] = ld_bcol(r2);
   }
-  auto qrow = [&](int j) { if constexpr (kCache) return qrow_r[j]; else return sQp[i * (D + 1) + j]; };
-  auto brow = [&](int j) { if constexpr (kCache) return brow_r[j]; else return sBp[i * (DU + 1) + j]; };
-  auto bcol = [&](int r) { if constexpr (kCache) return bcol_r[r]; else return sBp[r * (DU + 1) + i]; };
+  auto qrow = [&](int j2) { if constexpr (kCache) return qrow_r[j2]; else return ld_qrow(j2); };
+  auto brow = [&](int j2) { if constexpr (kCache) return brow_r[j2]; else return ld_brow(j2); };
+  auto bcol = [&](int r2) { if constexpr (kCache) return bcol_r[r2]; else return ld_bcol(r2); };
+  auto qcol = [&](int r2) { return pk2(sQp[2 * r2 * (D + 1) + i], sQp[(2 * r2 + 1) * (D + 1) + i]); };
   float hs = h0i, dh = 0.f;
   float gA = 0.f, glgA = 0.f, glgQ = 0.f, gR = 0.f, glgB = 0.f, gh0 = 0.f;
+  f2 gB2[DU / 2], gQ2[D / 2];
 #pragma unroll
-  for (int j = 0; j < DU; ++j) gB[j] = 0.f;
+  for (int j2 = 0; j2 < DU / 2; ++j2) gB2[j2] = 0;
 #pragma unroll
-  for (int k = 0; k < D; ++k) gQ[k] = 0.f;
+  for (int k2 = 0; k2 < D / 2; ++k2) gQ2[k2] = 0;
   float dq_prev = 1.0f;  // exp(lgQ * k) at the top of step k
   bool bad = false;
   for (int k = 0; k < T; ++k) {
@@ -85,36 +95,29 @@ __device__ __forceinline__ bool adjoint_head(
     if (k > 0) {
       // lambda -= Q_k h, dlambda -= Q_k dh with Q_k = Dq Q Dq (symplectic_iter.py:766-775);
       // the same products give the log_gamma_Q gradient of step k-1 (:871-877).
-      const float* p_hD = pb + 2 * D;
-      const float* p_dhD = pb + 3 * D;
-      const float4* h4 = reinterpret_cast<const float4*>(p_hD);
-      const float4* dh4 = reinterpret_cast<const float4*>(p_dhD);
-      // Four independent partial sums per dot product keep the FMA chains short.
-      float ph[4] = {0.f, 0.f, 0.f, 0.f}, pd[4] = {0.f, 0.f, 0.f, 0.f};
-      float pth[4] = {0.f, 0.f, 0.f, 0.f}, ptd[4] = {0.f, 0.f, 0.f, 0.f};
+      const float4* h4 = reinterpret_cast<const float4*>(pb + 2 * D);
+      const float4* dh4 = reinterpret_cast<const float4*>(pb + 3 * D);
+      f2 ph0 = 0, ph1 = 0, pd0 = 0, pd1 = 0, pth0 = 0, pth1 = 0, ptd0 = 0, ptd1 = 0;
 #pragma unroll
       for (int j4 = 0; j4 < D / 4; ++j4) {
         const float4 hv = h4[j4], dv = dh4[j4];  // broadcast 128-bit reads
-        const float q[4] = {qrow(4 * j4), qrow(4 * j4 + 1), qrow(4 * j4 + 2), qrow(4 * j4 + 3)};
-        const float hh[4] = {hv.x, hv.y, hv.z, hv.w}, dd[4] = {dv.x, dv.y, dv.z, dv.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          ph[c] = fmaf(q[c], hh[c], ph[c]);
-          pd[c] = fmaf(q[c], dd[c], pd[c]);
-        }
+        const f2 qa = qrow(2 * j4), qb = qrow(2 * j4 + 1);
+        ph0 = fma2(qa, lo2(hv), ph0);
+        ph1 = fma2(qb, hi2(hv), ph1);
+        pd0 = fma2(qa, lo2(dv), pd0);
+        pd1 = fma2(qb, hi2(dv), pd1);
         if (!sym) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float qt = sQp[(4 * j4 + c) * (D + 1) + i];
-            pth[c] = fmaf(qt, hh[c], pth[c]);
-            ptd[c] = fmaf(qt, dd[c], ptd[c]);
-          }
+          const f2 ta = qcol(2 * j4), tb = qcol(2 * j4 + 1);
+          pth0 = fma2(ta, lo2(hv), pth0);
+          pth1 = fma2(tb, hi2(hv), pth1);
+          ptd0 = fma2(ta, lo2(dv), ptd0);
+          ptd1 = fma2(tb, hi2(dv), ptd1);
         }
       }
-      const float qh = (ph[0] + ph[1]) + (ph[2] + ph[3]);
-      const float qdh = (pd[0] + pd[1]) + (pd[2] + pd[3]);
-      const float qth = sym ? qh : (pth[0] + pth[1]) + (pth[2] + pth[3]);
-      const float qtdh = sym ? qdh : (ptd[0] + ptd[1]) + (ptd[2] + ptd[3]);
+      const float qh = sum2(ph0) + sum2(ph1);
+      const float qdh = sum2(pd0) + sum2(pd1);
+      const float qth = sym ? qh : sum2(pth0) + sum2(pth1);
+      const float qtdh = sym ? qdh : sum2(ptd0) + sum2(ptd1);
       lam = fmaf(-dq_prev, qh, lam);
       dlam = fmaf(-dq_prev, qdh, dlam);
       glgQ = fmaf(0.5f * fmaf(dh, qh + qth, hs * (qdh + qtdh)), static_cast<float>(k) * dq_prev, glgQ);
@@ -135,20 +138,18 @@ __device__ __forceinline__ bool adjoint_head(
     if (i < DU) {
       const float4* l4 = reinterpret_cast<const float4*>(c_lam);
       const float4* dl4 = reinterpret_cast<const float4*>(c_dlam);
-      float pl[4] = {0.f, 0.f, 0.f, 0.f}, pdl[4] = {0.f, 0.f, 0.f, 0.f};
+      f2 pl0 = 0, pl1 = 0, pdl0 = 0, pdl1 = 0;
 #pragma unroll
       for (int r4 = 0; r4 < D / 4; ++r4) {
         const float4 lv = l4[r4], dv = dl4[r4];
-        const float ll[4] = {lv.x, lv.y, lv.z, lv.w}, dd[4] = {dv.x, dv.y, dv.z, dv.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float b = bcol(4 * r4 + c);
-          pl[c] = fmaf(b, ll[c], pl[c]);
-          pdl[c] = fmaf(b, dd[c], pdl[c]);
-        }
+        const f2 ba = bcol(2 * r4), bb = bcol(2 * r4 + 1);
+        pl0 = fma2(ba, lo2(lv), pl0);
+        pl1 = fma2(bb, hi2(lv), pl1);
+        pdl0 = fma2(ba, lo2(dv), pdl0);
+        pdl1 = fma2(bb, hi2(dv), pdl1);
       }
-      const float bl = (pl[0] + pl[1]) + (pl[2] + pl[3]);
-      const float bdl = (pdl[0] + pdl[1]) + (pdl[2] + pdl[3]);
+      const float bl = sum2(pl0) + sum2(pl1);
+      const float bdl = sum2(pdl0) + sum2(pdl1);
       const float eB = exp_scaled(lgB2, ke);
       const float u = -(bl * eB) * rinv;
       float du = -(bdl * eB) * rinv;
@@ -161,26 +162,21 @@ __device__ __forceinline__ bool adjoint_head(
     G.sync();
     const float4* ue4 = reinterpret_cast<const float4*>(c_uE);
     const float4* due4 = reinterpret_cast<const float4*>(c_duE);
-    float pu[4] = {0.f, 0.f, 0.f, 0.f}, pdu[4] = {0.f, 0.f, 0.f, 0.f};
+    const f2 lam2 = dup2(lam), dlam2 = dup2(dlam);
+    f2 pu0 = 0, pu1 = 0, pdu0 = 0, pdu1 = 0;
 #pragma unroll
     for (int j4 = 0; j4 < DU / 4; ++j4) {
       const float4 uv = ue4[j4], dv = due4[j4];
-      const float b0 = brow(4 * j4), b1 = brow(4 * j4 + 1), b2 = brow(4 * j4 + 2), b3 = brow(4 * j4 + 3);
-      pu[0] = fmaf(b0, uv.x, pu[0]);
-      pu[1] = fmaf(b1, uv.y, pu[1]);
-      pu[2] = fmaf(b2, uv.z, pu[2]);
-      pu[3] = fmaf(b3, uv.w, pu[3]);
-      pdu[0] = fmaf(b0, dv.x, pdu[0]);
-      pdu[1] = fmaf(b1, dv.y, pdu[1]);
-      pdu[2] = fmaf(b2, dv.z, pdu[2]);
-      pdu[3] = fmaf(b3, dv.w, pdu[3]);
-      gB[4 * j4 + 0] = fmaf(lam, dv.x, fmaf(dlam, uv.x, gB[4 * j4 + 0]));
-      gB[4 * j4 + 1] = fmaf(lam, dv.y, fmaf(dlam, uv.y, gB[4 * j4 + 1]));
-      gB[4 * j4 + 2] = fmaf(lam, dv.z, fmaf(dlam, uv.z, gB[4 * j4 + 2]));
-      gB[4 * j4 + 3] = fmaf(lam, dv.w, fmaf(dlam, uv.w, gB[4 * j4 + 3]));
+      const f2 ba = brow(2 * j4), bb = brow(2 * j4 + 1);
+      pu0 = fma2(ba, lo2(uv), pu0);
+      pu1 = fma2(bb, hi2(uv), pu1);
+      pdu0 = fma2(ba, lo2(dv), pdu0);
+      pdu1 = fma2(bb, hi2(dv), pdu1);
+      gB2[2 * j4] = fma2(lam2, lo2(dv), fma2(dlam2, lo2(uv), gB2[2 * j4]));
+      gB2[2 * j4 + 1] = fma2(lam2, hi2(dv), fma2(dlam2, hi2(uv), gB2[2 * j4 + 1]));
     }
-    const float bu = (pu[0] + pu[1]) + (pu[2] + pu[3]);
-    const float bdu = (pdu[0] + pdu[1]) + (pdu[2] + pdu[3]);
+    const float bu = sum2(pu0) + sum2(pu1);
+    const float bdu = sum2(pdu0) + sum2(pdu1);
     hs = fmaf(hs, At, bu);
     dh = fmaf(dh, At, bdu);
     const float dq = exp_scaled(lgQ2, ke);
@@ -193,30 +189,31 @@ __device__ __forceinline__ bool adjoint_head(
     if (k == T - 1) {
       // grad_Qf = (h dh^T + dh h^T) / 2 at the final state (symplectic_iter.py:855-857).
       if (valid) {
-        TIn* qrow = gQf_out + (p * D + i) * D;
+        TIn* qrow_out = gQf_out + (p * D + i) * D;
         for (int j = 0; j < D; ++j) {
           const float v = 0.5f * fmaf(hs, c_dh[j], dh * c_h[j]);
           bad |= unstable(v);
-          stf(qrow + j, v);
+          stf(qrow_out + j, v);
         }
       }
     } else {
       const float4* hD4 = reinterpret_cast<const float4*>(c_hD);
       const float4* dhD4 = reinterpret_cast<const float4*>(c_dhD);
+      const f2 hD2 = dup2(hD), dhD2 = dup2(dhD);
       // (h dh^T + dh h^T) scaled by Dq on both sides; the 1/2 is applied once at the end.
 #pragma unroll
       for (int j4 = 0; j4 < D / 4; ++j4) {
         const float4 hv = hD4[j4], dv = dhD4[j4];
-        gQ[4 * j4 + 0] = fmaf(hD, dv.x, fmaf(dhD, hv.x, gQ[4 * j4 + 0]));
-        gQ[4 * j4 + 1] = fmaf(hD, dv.y, fmaf(dhD, hv.y, gQ[4 * j4 + 1]));
-        gQ[4 * j4 + 2] = fmaf(hD, dv.z, fmaf(dhD, hv.z, gQ[4 * j4 + 2]));
-        gQ[4 * j4 + 3] = fmaf(hD, dv.w, fmaf(dhD, hv.w, gQ[4 * j4 + 3]));
+        gQ2[2 * j4] = fma2(hD2, lo2(dv), fma2(dhD2, lo2(hv), gQ2[2 * j4]));
+        gQ2[2 * j4 + 1] = fma2(hD2, hi2(dv), fma2(dhD2, hi2(hv), gQ2[2 * j4 + 1]));
       }
     }
     dq_prev = dq;
   }
 #pragma unroll
-  for (int j = 0; j < D; ++j) gQ[j] *= 0.5f;
+  for (int j2 = 0; j2 < DU / 2; ++j2) up2(gB2[j2], gB[2 * j2], gB[2 * j2 + 1]);
+#pragma unroll
+  for (int k2 = 0; k2 < D / 2; ++k2) up2(mul2(gQ2[k2], dup2(0.5f)), gQ[2 * k2], gQ[2 * k2 + 1]);
   const float glgA_sum = group_sum<D>(G, glgA, red);
   if (valid) {
     bad |= unstable(gA) | unstable(glgQ) | unstable(gh0);

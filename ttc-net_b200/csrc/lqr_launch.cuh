@@ -6,6 +6,7 @@
 
 #include <cstdio>
 
+#include "lqr_adjoint_mma.cuh"
 #include "lqr_tc.cuh"
 
 namespace ttc {
@@ -41,6 +42,11 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
 
 #ifdef TTC_DEFINE_LAUNCHERS
 constexpr size_t kMaxSmem = 227 * 1024;
+
+// Largest d whose saved-state backward runs on the warp-MMA adjoint.
+#ifndef TTC_ADJ_MMA_MAXD
+#define TTC_ADJ_MMA_MAXD 16
+#endif
 
 // Tile slots per CTA for the tensor-core forward: one per 128-row tile of a row, at most
 // TcLaunch<D>::kMaxSlots (TMEM: 4 x 96 columns at d = 32), fewer if the shared-memory
@@ -95,11 +101,34 @@ int launch_fwd(const void* A, const void* B, const void* Q, const void* R, const
                                           nullptr, status, st);
 }
 
+// Saved-state backward on the warp-MMA adjoint: R rows x ceil(nh / 8) warps per CTA.
+template <int D, typename TIn, bool FROM_M>
+int launch_bwd_mma(const void* A, const void* B, const void* Q, const void* R, const void* lA,
+                   const void* lB, const void* lQ, const void* h0, const float* lam0,
+                   const float* M_or_dp, const void* dU, int64_t N, int nh, int T, void* const* g,
+                   int* status, cudaStream_t st) {
+  using C = AdjMma<D>;
+  const int rpc = C::rows_per_cta(nh);
+  const size_t smem = C::bytes(nh);
+  auto k = ttc::lqr_bwd_mma_kernel<D, TIn, FROM_M>;
+  if (int rc = set_smem(k, smem)) return rc;
+  const int64_t grid = (N + rpc - 1) / rpc;
+  k<<<dim3((unsigned)grid), dim3(32 * C::warps(nh)), smem, st>>>(
+      (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)lA, (const TIn*)lB,
+      (const TIn*)lQ, (const TIn*)h0, lam0, M_or_dp, (const TIn*)dU, N, nh, T, rpc, (TIn*)g[0],
+      (TIn*)g[1], (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6], (TIn*)g[7],
+      (TIn*)g[8], status);
+  return cuda_check(cudaGetLastError(), "lqr_bwd_mma_kernel launch");
+}
+
 template <int D, int DU, typename TIn>
 int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
                const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
                int* status, cudaStream_t st) {
+  if constexpr (D == DU && D <= TTC_ADJ_MMA_MAXD) {
+    if (M != nullptr && nh <= 8 * AdjMma<D>::kMaxWarps) return launch_bwd_mma<D, TIn, true>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status, st);
+  }
   if (M != nullptr) {
     // The forward saved lambda0 and M: adjoint only, on the CUDA cores.
     const int G = groups_for(nh, D);
