@@ -14,8 +14,9 @@
 // 8kk + 2t + 1).  Each product runs in 3xTF32 (A_lo B_hi + A_hi B_lo + A_hi B_hi), close to
 // the fp32 sums of the reference.  grad_B and grad_Q sum over heads, i.e. contract over the
 // MMA's M rows: the vectors go through a small shared staging matrix and a second MMA with
-// K = the 16 (head, primal / tangent) rows accumulates them in registers over all steps.
-// Per-row partial sums of the warps meet in shared memory in warp order: deterministic.
+// K = the 16 (head, primal / tangent) rows accumulates them in registers over all steps;
+// the output tiles are shared out among the row's warps, each summing every warp's staged
+// vectors in warp order: deterministic.
 #pragma once
 
 #include "lqr_kernels.cuh"
@@ -44,23 +45,41 @@ struct AdjMma {
   static_assert(D % 16 == 0, "d must be a multiple of 16");
   static constexpr int NT = D / 8;             // n-tiles of an output = k-steps of an input
   static constexpr int MT = D / 16;            // m-tiles of grad_B / grad_Q
+  static constexpr int kUnits = 2 * MT;        // (grad_B | grad_Q, m-tile) units of NT tiles
   static constexpr int kFrag = NT * NT * 128;  // floats of one constant operand (hi + lo)
   static constexpr int SS = D + 8;             // staging row stride (bank-conflict free)
   static constexpr int kStage = 16 * SS;
-  // per row: operands Q^T, B, B^T, Q and a symmetry flag; per warp: 3 staging matrices
+  // per row: operands Q^T, B, B^T, Q and a symmetry flag; per warp: 3 staging matrices,
+  // double-buffered by step parity
   static constexpr int kRow = 4 * kFrag + 4;
-  static constexpr int kWarp = 3 * kStage;
+  static constexpr int kWarp = 2 * 3 * kStage;
   static constexpr int kMaxWarps = 8;
-  static int rows_per_cta(int nh) {
-    const int wpr = (nh + 7) / 8;
-    return wpr >= kMaxWarps ? 1 : kMaxWarps / wpr;
+  // OWN (d = 16): every warp accumulates all units from its own heads and the row's warps
+  // add their partial sums at the end.  Shared (d >= 32, where all units would not fit in
+  // registers): the units are dealt out to the row's warps, which meet at a named barrier
+  // every step and sum all the row's staged vectors.
+  static constexpr bool kOwn = D <= 16;
+  static constexpr size_t kSmemLimit = 227 * 1024;
+  static int warps_per_row(int nh) { return (nh + 7) / 8; }
+  static size_t bytes_for(int rows, int wpr) {
+    return sizeof(float) * ((size_t)rows * kRow + (size_t)rows * wpr * kWarp);
   }
-  static int warps(int nh) { return ((nh + 7) / 8) * rows_per_cta(nh); }
-  static size_t bytes(int nh) {
-    const int w = warps(nh), r = rows_per_cta(nh);
-    // the final grad_B / grad_Q exchange reuses the staging area: 2 D^2 floats per warp
-    const int per_warp = kWarp > 2 * D * D ? kWarp : 2 * D * D;
-    return sizeof(float) * ((size_t)r * kRow + (size_t)w * per_warp);
+  static int rows_per_cta(int nh) {
+    const int wpr = warps_per_row(nh);
+    int r = wpr >= kMaxWarps ? 1 : kMaxWarps / wpr;
+    while (r > 1 && bytes_for(r, wpr) > kSmemLimit) --r;
+    return r;
+  }
+  static int warps(int nh) { return warps_per_row(nh) * rows_per_cta(nh); }
+  // grad_B / grad_Q units each warp of a row accumulates
+  static int units_per_warp(int nh) {
+    if (kOwn) return kUnits;
+    const int wpr = warps_per_row(nh);
+    return (kUnits + wpr - 1) / wpr;
+  }
+  static size_t bytes(int nh) { return bytes_for(rows_per_cta(nh), warps_per_row(nh)); }
+  static bool fits(int nh) {
+    return warps_per_row(nh) <= kMaxWarps && bytes(nh) <= kSmemLimit && units_per_warp(nh) <= 2;
   }
 };
 
@@ -82,34 +101,29 @@ __device__ __forceinline__ void build_operand(float* dst, Get get, int tid, int 
 
 // out (16 x D, output-fragment order) = in (16 x D, output-fragment order) * W, 3xTF32.
 // in[j] = {row g e0, row g e1, row g+8 e0, row g+8 e1} with e0/e1 = entries 8j+2t, 8j+2t+1.
+// k-steps outer, n-tiles inner: one A fragment live at a time and NT independent chains.
 template <int D>
 __device__ __forceinline__ void frag_product(const float (&in)[D / 8][4], float (&out)[D / 8][4],
                                              const float4* W, int lane) {
   constexpr int NT = D / 8;
-  uint32_t ah[NT][4], al[NT][4];
+#pragma unroll
+  for (int nj = 0; nj < NT; ++nj)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) out[nj][r] = 0.f;
 #pragma unroll
   for (int kk = 0; kk < NT; ++kk) {
-    wmma::split(in[kk][0], ah[kk][0], al[kk][0]);  // a0: row g,   slot t     <- entry 8kk+2t
-    wmma::split(in[kk][2], ah[kk][1], al[kk][1]);  // a1: row g+8, slot t
-    wmma::split(in[kk][1], ah[kk][2], al[kk][2]);  // a2: row g,   slot t + 4 <- entry 8kk+2t+1
-    wmma::split(in[kk][3], ah[kk][3], al[kk][3]);  // a3: row g+8, slot t + 4
-  }
+    uint32_t ah[4], al[4];
+    wmma::split(in[kk][0], ah[0], al[0]);  // a0: row g,   slot t     <- entry 8kk+2t
+    wmma::split(in[kk][2], ah[1], al[1]);  // a1: row g+8, slot t
+    wmma::split(in[kk][1], ah[2], al[2]);  // a2: row g,   slot t + 4 <- entry 8kk+2t+1
+    wmma::split(in[kk][3], ah[3], al[3]);  // a3: row g+8, slot t + 4
 #pragma unroll
-  for (int nj = 0; nj < NT; ++nj) {
-    float4 w[NT];
-#pragma unroll
-    for (int kk = 0; kk < NT; ++kk) w[kk] = W[(kk * NT + nj) * 32 + lane];
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kk = 0; kk < NT; ++kk) {
-      wmma::m16n8k8(c, al[kk], __float_as_uint(w[kk].x), __float_as_uint(w[kk].y));
-      wmma::m16n8k8(c, ah[kk], __float_as_uint(w[kk].z), __float_as_uint(w[kk].w));
+    for (int nj = 0; nj < NT; ++nj) {
+      const float4 w = W[(kk * NT + nj) * 32 + lane];
+      wmma::m16n8k8(out[nj], al, __float_as_uint(w.x), __float_as_uint(w.y));
+      wmma::m16n8k8(out[nj], ah, __float_as_uint(w.z), __float_as_uint(w.w));
+      wmma::m16n8k8(out[nj], ah, __float_as_uint(w.x), __float_as_uint(w.y));
     }
-#pragma unroll
-    for (int kk = 0; kk < NT; ++kk)
-      wmma::m16n8k8(c, ah[kk], __float_as_uint(w[kk].x), __float_as_uint(w[kk].y));
-#pragma unroll
-    for (int r = 0; r < 4; ++r) out[nj][r] = c[r];
   }
 }
 
@@ -124,44 +138,42 @@ __device__ __forceinline__ void stage_rows(float* S, const float (&v)[D / 8][4],
   }
 }
 
-// acc[m][n] += sum_r SX[r][m] * SY[(r + 8) % 16][n]  (K = the 16 staged rows), 3xTF32.
+// acc[n-tile][.] += sum_r SX[r][16 mi + m] * SY[(r + 8) % 16][n]  over the 16 staged rows
+// (K) for one m-tile of the output, 3xTF32.
 template <int D>
-__device__ __forceinline__ void accumulate_outer(float (&acc)[D / 16][D / 8][4], const float* SX,
-                                                 const float* SY, int g, int t) {
-  constexpr int SS = AdjMma<D>::SS, NT = D / 8, MT = D / 16;
+__device__ __forceinline__ void accumulate_unit(float (&acc)[D / 8][4], const float* SX, const float* SY,
+                                                int mi, int g, int t) {
+  constexpr int SS = AdjMma<D>::SS, NT = D / 8;
 #pragma unroll
   for (int kk = 0; kk < 2; ++kk) {
-    uint32_t bh[NT][2], bl[NT][2];
+    const float* x0 = SX + (8 * kk + t) * SS + 16 * mi;
+    const float* x1 = SX + (8 * kk + t + 4) * SS + 16 * mi;
+    uint32_t ah[4], al[4];
+    wmma::split(x0[g], ah[0], al[0]);
+    wmma::split(x0[g + 8], ah[1], al[1]);
+    wmma::split(x1[g], ah[2], al[2]);
+    wmma::split(x1[g + 8], ah[3], al[3]);
     const float* y0 = SY + ((8 * kk + t + 8) & 15) * SS;
     const float* y1 = SY + ((8 * kk + t + 12) & 15) * SS;
 #pragma unroll
     for (int nj = 0; nj < NT; ++nj) {
-      wmma::split(y0[8 * nj + g], bh[nj][0], bl[nj][0]);
-      wmma::split(y1[8 * nj + g], bh[nj][1], bl[nj][1]);
-    }
-    const float* x0 = SX + (8 * kk + t) * SS;
-    const float* x1 = SX + (8 * kk + t + 4) * SS;
-#pragma unroll
-    for (int mi = 0; mi < MT; ++mi) {
-      uint32_t ah[4], al[4];
-      wmma::split(x0[16 * mi + g], ah[0], al[0]);
-      wmma::split(x0[16 * mi + g + 8], ah[1], al[1]);
-      wmma::split(x1[16 * mi + g], ah[2], al[2]);
-      wmma::split(x1[16 * mi + g + 8], ah[3], al[3]);
-#pragma unroll
-      for (int nj = 0; nj < NT; ++nj) {
-        wmma::m16n8k8(acc[mi][nj], al, bh[nj][0], bh[nj][1]);
-        wmma::m16n8k8(acc[mi][nj], ah, bl[nj][0], bl[nj][1]);
-        wmma::m16n8k8(acc[mi][nj], ah, bh[nj][0], bh[nj][1]);
-      }
+      uint32_t bh0, bl0, bh1, bl1;
+      wmma::split(y0[8 * nj + g], bh0, bl0);
+      wmma::split(y1[8 * nj + g], bh1, bl1);
+      wmma::m16n8k8(acc[nj], al, bh0, bh1);
+      wmma::m16n8k8(acc[nj], ah, bl0, bl1);
+      wmma::m16n8k8(acc[nj], ah, bh0, bh1);
     }
   }
 }
 
 // Backward from the forward's lambda0 and either M (d_p = M d_u per head, fused_lqr.py:
-// 185-187) or d_p itself.  Grid: ceil(N / R) CTAs of R rows x ceil(nh / 8) warps.
-template <int D, typename TIn, bool FROM_M>
-__global__ void __launch_bounds__(256, 2)
+// 185-187) or d_p itself.  Grid: ceil(N / R) CTAs of R rows x W = ceil(nh / 8) warps; the W
+// warps of a row meet at one named barrier per step (id 1 + row), after which warp w
+// accumulates grad_B / grad_Q units w, w + W, ... (UPW at most) over all W warps' staged
+// vectors of that step, in warp order.
+template <int D, typename TIn, bool FROM_M, int UPW>
+__global__ void __launch_bounds__(256, D <= 16 ? 2 : 1)
 lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                    const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
                    const TIn* __restrict__ lgA, const TIn* __restrict__ lgB,
@@ -185,13 +197,11 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   const bool row_ok = n < N;
   float* rows_s = smem;
   float* warp_s = smem + (size_t)rows_per_cta * C::kRow;
-  const int per_warp = C::kWarp > 2 * D * D ? C::kWarp : 2 * D * D;
-  float* stg = warp_s + warp * per_warp;
+  float* row_stage = warp_s + (size_t)(rloc * wpr) * C::kWarp;  // warp 0 of this row
+  float* stg = warp_s + (size_t)warp * C::kWarp;
 
   // The CTA's rows: constant operands Q^T, B, B^T, Q in fragment order, symmetry flag.
-  for (int r = 0; r < rows_per_cta; ++r) {
-    if (tid == 0) reinterpret_cast<int*>(rows_s + r * C::kRow + 4 * C::kFrag)[0] = 1;
-  }
+  if (tid < rows_per_cta) reinterpret_cast<int*>(rows_s + tid * C::kRow + 4 * C::kFrag)[0] = 1;
   __syncthreads();
   for (int r = 0; r < rows_per_cta; ++r) {
     const int64_t nr = n0 + r;
@@ -209,7 +219,7 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   }
   __syncthreads();
 
-  const float* rbase = rows_s + (row_ok ? rloc : 0) * C::kRow;
+  const float* rbase = rows_s + rloc * C::kRow;
   const float4* Wqt = reinterpret_cast<const float4*>(rbase);
   const float4* Wb = reinterpret_cast<const float4*>(rbase + C::kFrag);
   const float4* Wbt = reinterpret_cast<const float4*>(rbase + 2 * C::kFrag);
@@ -219,10 +229,10 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   const int h = hb * 8 + g;
   const bool valid = row_ok && h < nh;
   const int64_t p = valid ? n * nh + h : 0;
-  // entry of slot (j, s): 8j + 2t + s
-  float a[NT][2], lgQ2[NT][2], lgB2[NT][2], rinv[NT][2], rinv2[NT][2], dUi[NT][2];
+  // slot (j, s) of a thread is entry 8j + 2t + s; index 2 + s of a pair array is the tangent
+  float a[NT][2], lgQ2[NT][2], lgB2[NT][2], rinv[NT][2];
   float L[NT][4], H[NT][4];
-  float lgA2 = valid ? ldf(lgA + p) * kLog2e : 0.f;
+  const float lgA2 = valid ? ldf(lgA + p) * kLog2e : 0.f;
 #pragma unroll
   for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -232,8 +242,6 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       lgQ2[j][s] = valid ? ldf(lgQ + p * D + e) * kLog2e : 0.f;
       lgB2[j][s] = valid ? ldf(lgB + p * D + e) * kLog2e : 0.f;
       rinv[j][s] = valid ? ldf(Rinv + p * D + e) : 1.f;
-      rinv2[j][s] = recip(rinv[j][s] * rinv[j][s]);
-      dUi[j][s] = valid ? ldf(dU + p * D + e) : 0.f;
       H[j][s] = valid ? ldf(H0 + p * D + e) : 0.f;
       H[j][2 + s] = 0.f;
       L[j][s] = valid ? lam0_in[p * D + e] : 0.f;
@@ -250,41 +258,39 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     }
   }
 
-  float gA[NT][2], glgQ[NT][2], gR[NT][2], glgB[NT][2], dqp[NT][2], At[NT][2];
-  float HD[NT][4];
+  float gA[NT][2], glgQ[NT][2], gR[NT][2], glgB[NT][2], dqp[NT][2];
   float glgA = 0.f;
 #pragma unroll
-  for (int j = 0; j < NT; ++j) {
+  for (int j = 0; j < NT; ++j)
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       gA[j][s] = glgQ[j][s] = gR[j][s] = glgB[j][s] = 0.f;
       dqp[j][s] = 1.0f;
     }
+  float acc[UPW][NT][4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) HD[j][r] = 0.f;
-  }
-  float accB[MT][NT][4], accQ[MT][NT][4];
-#pragma unroll
-  for (int mi = 0; mi < MT; ++mi)
+  for (int q = 0; q < UPW; ++q)
 #pragma unroll
     for (int nj = 0; nj < NT; ++nj)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) accB[mi][nj][r] = accQ[mi][nj][r] = 0.f;
+      for (int r = 0; r < 4; ++r) acc[q][nj][r] = 0.f;
 
-  float* S0 = stg;                 // [lambda; dlambda]
-  float* S1 = stg + C::kStage;     // [u e^lgB; du e^lgB]
-  float* S2 = stg + 2 * C::kStage; // [h Dq; dh Dq]
   bool bad = false;
   for (int k = 0; k < T; ++k) {
     const float ke = static_cast<float>(k + 1);
+    float* S0 = stg + (k & 1) * 3 * C::kStage;  // [lambda; dlambda]
+    float* S1 = S0 + C::kStage;                 // [u e^lgB; du e^lgB]
+    float* S2 = S0 + 2 * C::kStage;             // [h Dq; dh Dq]
     if (k > 0) {
       // lambda -= Q_k h, dlambda -= Q_k dh with Q_k = Dq Q Dq (symplectic_iter.py:766-775)
       // and the log_gamma_Q gradient of step k-1 (:871-877).
-      float QH[NT][4], QTH[NT][4];
+      float HD[NT][4], QH[NT][4], QTH[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r & 1];
       frag_product<D>(HD, QH, Wqt, lane);
-      if (!sym) {
-        frag_product<D>(HD, QTH, Wq, lane);
-      }
+      if (!sym) frag_product<D>(HD, QTH, Wq, lane);
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -307,6 +313,7 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         }
     }
     const float eA = exp_scaled(lgA2, ke);
+    float At[NT][2];
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -320,6 +327,7 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         glgA = fmaf(dA * a[j][s], ke * eA, glgA);
       }
     }
+    stage_rows<D>(S0, L, g, t);
     // u = -R_inv (B e^lgB)^T lambda and its tangent (symplectic_iter.py:800-830)
     float UE[NT][4];
     {
@@ -333,16 +341,14 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
           const float bl = BL[j][s], bdl = BL[j][2 + s];
           const float u = -(bl * eB) * rinv[j][s];
           float du = -(bdl * eB) * rinv[j][s];
-          if (k == 0) du = fmaf(dUi[j][s], -rinv[j][s], du);
+          if (k == 0 && valid) du = fmaf(ldf(dU + p * D + 8 * j + 2 * t + s), -rinv[j][s], du);
           glgB[j][s] = fmaf(fmaf(du, bl, u * bdl), ke * eB, glgB[j][s]);
-          gR[j][s] = fmaf(-(u * du), rinv2[j][s], gR[j][s]);
+          gR[j][s] = fmaf(-(u * du), recip(rinv[j][s] * rinv[j][s]), gR[j][s]);
           UE[j][s] = u * eB;
           UE[j][2 + s] = du * eB;
         }
       }
     }
-    __syncwarp();
-    stage_rows<D>(S0, L, g, t);
     stage_rows<D>(S1, UE, g, t);
     // h <- A h + B e^lgB u (symplectic_iter.py:832-850)
     {
@@ -354,33 +360,63 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         for (int s = 0; s < 2; ++s) {
           H[j][s] = fmaf(H[j][s], At[j][s], BU[j][s]);
           H[j][2 + s] = fmaf(H[j][2 + s], At[j][s], BU[j][2 + s]);
-          const float dq = exp_scaled(lgQ2[j][s], ke);
-          HD[j][s] = H[j][s] * dq;
-          HD[j][2 + s] = H[j][2 + s] * dq;
-          dqp[j][s] = dq;
+          dqp[j][s] = exp_scaled(lgQ2[j][s], ke);
         }
       }
     }
-    if (k < T - 1) stage_rows<D>(S2, HD, g, t);
-    __syncwarp();
+    if (k < T - 1) {
+      float HD[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r & 1];
+      stage_rows<D>(S2, HD, g, t);
+    }
+    // Every warp of the row has staged step k (and finished reading step k - 1's buffer).
+    if (!C::kOwn && wpr > 1) {
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + rloc), "r"(32 * wpr) : "memory");
+    } else {
+      __syncwarp();
+    }
     // grad_B += lambda (du e^lgB)^T + dlambda (u e^lgB)^T ;
     // grad_Q += (h Dq)(dh Dq)^T + (dh Dq)(h Dq)^T  (the 1/2 is applied at the end)
-    accumulate_outer<D>(accB, S0, S1, g, t);
-    if (k < T - 1) accumulate_outer<D>(accQ, S2, S2, g, t);
+#pragma unroll
+    for (int q = 0; q < UPW; ++q) {
+      const int unit = C::kOwn ? q : hb + q * wpr;
+      if (unit < C::kUnits) {
+        const bool isq = unit >= MT;
+        if (!isq || k < T - 1) {
+          const int mi = isq ? unit - MT : unit;
+          const int off = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : 0);
+          const int offy = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : C::kStage);
+          if constexpr (C::kOwn) {
+            accumulate_unit<D>(acc[q], stg + off, stg + offy, mi, g, t);
+          } else {
+            for (int w = 0; w < wpr; ++w) {
+              const float* base = row_stage + (size_t)w * C::kWarp;
+              accumulate_unit<D>(acc[q], base + off, base + offy, mi, g, t);
+            }
+          }
+        }
+      }
+    }
   }
 
-  // grad_Qf = (h dh^T + dh h^T) / 2 at the final state (symplectic_iter.py:855-857).
-  __syncwarp();
-  stage_rows<D>(S0, H, g, t);
-  __syncwarp();
-  for (int e = lane; e < 8 * D * D; e += 32) {
-    const int hh = e / (D * D), i = (e / D) % D, jj = e % D;
-    const int h2 = hb * 8 + hh;
-    if (row_ok && h2 < nh) {
-      const float v = 0.5f * fmaf(S0[hh * C::SS + i], S0[(hh + 8) * C::SS + jj],
-                                  S0[(hh + 8) * C::SS + i] * S0[hh * C::SS + jj]);
-      bad |= unstable(v);
-      stf(gQf_out + ((n * nh + h2) * D + i) * D + jj, v);
+  // grad_Qf = (h dh^T + dh h^T) / 2 at the final state (symplectic_iter.py:855-857), from
+  // the staging buffer of step T (unused by the row's other warps).
+  {
+    float* S = stg + (T & 1) * 3 * C::kStage;
+    stage_rows<D>(S, H, g, t);
+    __syncwarp();
+    for (int e = lane; e < 8 * D * D; e += 32) {
+      const int hh = e / (D * D), i = (e / D) % D, jj = e % D;
+      const int h2 = hb * 8 + hh;
+      if (row_ok && h2 < nh) {
+        const float v = 0.5f * fmaf(S[hh * C::SS + i], S[(hh + 8) * C::SS + jj],
+                                    S[(hh + 8) * C::SS + i] * S[hh * C::SS + jj]);
+        bad |= unstable(v);
+        stf(gQf_out + ((n * nh + h2) * D + i) * D + jj, v);
+      }
     }
   }
   // Per-head outputs.
@@ -405,35 +441,54 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       stf(glgA_out + p, glgA_sum);
     }
   }
-  // grad_B / grad_Q of the row: the warps' partial sums in warp order.
-  __syncthreads();
-  float* red = stg;  // [D][D] grad_B then [D][D] grad_Q, row-major
+  if constexpr (C::kOwn) {
+    // The row's warps add their partial sums in warp order (staging area reused).
+    static_assert(!C::kOwn || 2 * D * D <= C::kWarp, "reduction area");
+    __syncthreads();
 #pragma unroll
-  for (int mi = 0; mi < MT; ++mi)
+    for (int q = 0; q < UPW; ++q) {
+      const bool isq = q >= MT;
+      const int mi = isq ? q - MT : q;
+      float* red = stg + (isq ? D * D : 0);
 #pragma unroll
-    for (int nj = 0; nj < NT; ++nj) {
-      const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
-      red[r0 * D + c0] = accB[mi][nj][0];
-      red[r0 * D + c0 + 1] = accB[mi][nj][1];
-      red[(r0 + 8) * D + c0] = accB[mi][nj][2];
-      red[(r0 + 8) * D + c0 + 1] = accB[mi][nj][3];
-      red[D * D + r0 * D + c0] = 0.5f * accQ[mi][nj][0];
-      red[D * D + r0 * D + c0 + 1] = 0.5f * accQ[mi][nj][1];
-      red[D * D + (r0 + 8) * D + c0] = 0.5f * accQ[mi][nj][2];
-      red[D * D + (r0 + 8) * D + c0 + 1] = 0.5f * accQ[mi][nj][3];
+      for (int nj = 0; nj < NT; ++nj) {
+        const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
+        *reinterpret_cast<float2*>(red + r0 * D + c0) = make_float2(acc[q][nj][0], acc[q][nj][1]);
+        *reinterpret_cast<float2*>(red + (r0 + 8) * D + c0) = make_float2(acc[q][nj][2], acc[q][nj][3]);
+      }
     }
-  __syncthreads();
-  for (int r = 0; r < rows_per_cta; ++r) {
-    const int64_t nr = n0 + r;
-    if (nr >= N) break;
-    for (int e = tid; e < 2 * D * D; e += nthreads) {
-      float s = 0.f;
-      for (int w = 0; w < wpr; ++w) s += warp_s[(r * wpr + w) * per_warp + e];
-      bad |= unstable(s);
-      if (e < D * D) {
-        stf(gB_out + nr * (D * D) + e, s);
-      } else {
-        stf(gQ_out + nr * (D * D) + (e - D * D), s);
+    __syncthreads();
+    for (int r = 0; r < rows_per_cta; ++r) {
+      const int64_t nr = n0 + r;
+      if (nr >= N) break;
+      for (int e = tid; e < 2 * D * D; e += nthreads) {
+        float v = 0.f;
+        for (int w = 0; w < wpr; ++w) v += warp_s[(size_t)(r * wpr + w) * C::kWarp + e];
+        if (e >= D * D) v *= 0.5f;
+        bad |= unstable(v);
+        stf((e < D * D ? gB_out : gQ_out) + nr * (D * D) + (e % (D * D)), v);
+      }
+    }
+  } else if (row_ok) {
+    // Each unit holds the sum over all the row's heads.
+#pragma unroll
+    for (int q = 0; q < UPW; ++q) {
+      const int unit = hb + q * wpr;
+      if (unit < C::kUnits) {
+        const bool isq = unit >= MT;
+        const int mi = isq ? unit - MT : unit;
+        const float sc = isq ? 0.5f : 1.0f;
+        TIn* out = (isq ? gQ_out : gB_out) + n * (D * D);
+#pragma unroll
+        for (int nj = 0; nj < NT; ++nj) {
+          const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
+          const float v[4] = {sc * acc[q][nj][0], sc * acc[q][nj][1], sc * acc[q][nj][2], sc * acc[q][nj][3]};
+          bad |= unstable(v[0]) | unstable(v[1]) | unstable(v[2]) | unstable(v[3]);
+          stf(out + r0 * D + c0, v[0]);
+          stf(out + r0 * D + c0 + 1, v[1]);
+          stf(out + (r0 + 8) * D + c0, v[2]);
+          stf(out + (r0 + 8) * D + c0 + 1, v[3]);
+        }
       }
     }
   }

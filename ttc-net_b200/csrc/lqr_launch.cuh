@@ -45,7 +45,7 @@ constexpr size_t kMaxSmem = 227 * 1024;
 
 // Largest d whose saved-state backward runs on the warp-MMA adjoint.
 #ifndef TTC_ADJ_MMA_MAXD
-#define TTC_ADJ_MMA_MAXD 16
+#define TTC_ADJ_MMA_MAXD 32
 #endif
 
 // Tile slots per CTA for the tensor-core forward: one per 128-row tile of a row, at most
@@ -110,7 +110,9 @@ int launch_bwd_mma(const void* A, const void* B, const void* Q, const void* R, c
   using C = AdjMma<D>;
   const int rpc = C::rows_per_cta(nh);
   const size_t smem = C::bytes(nh);
-  auto k = ttc::lqr_bwd_mma_kernel<D, TIn, FROM_M>;
+  constexpr int kU = C::kOwn ? C::kUnits : 1;
+  auto k = C::units_per_warp(nh) == kU ? ttc::lqr_bwd_mma_kernel<D, TIn, FROM_M, kU>
+                                       : ttc::lqr_bwd_mma_kernel<D, TIn, FROM_M, 2>;
   if (int rc = set_smem(k, smem)) return rc;
   const int64_t grid = (N + rpc - 1) / rpc;
   k<<<dim3((unsigned)grid), dim3(32 * C::warps(nh)), smem, st>>>(
@@ -127,7 +129,8 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
                const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
                int* status, cudaStream_t st) {
   if constexpr (D == DU && D <= TTC_ADJ_MMA_MAXD) {
-    if (M != nullptr && nh <= 8 * AdjMma<D>::kMaxWarps) return launch_bwd_mma<D, TIn, true>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status, st);
+    if (M != nullptr && AdjMma<D>::fits(nh))
+      return launch_bwd_mma<D, TIn, true>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status, st);
   }
   if (M != nullptr) {
     // The forward saved lambda0 and M: adjoint only, on the CUDA cores.
