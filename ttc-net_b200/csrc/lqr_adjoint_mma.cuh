@@ -186,7 +186,7 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                    int* __restrict__ status) {
   using C = AdjMma<D>;
   constexpr int NT = C::NT, MT = C::MT;
-  extern __shared__ __align__(16) float smem[];
+  extern __shared__ __align__(128) float smem[];
   const int tid = threadIdx.x, nthreads = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;

@@ -270,7 +270,7 @@ lqr_bwd_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                TIn* __restrict__ gQf_out, TIn* __restrict__ glgA_out, TIn* __restrict__ glgB_out,
                TIn* __restrict__ glgQ_out, TIn* __restrict__ gh0_out, int* __restrict__ status) {
   using L = BwdLayout<D, DU>;
-  extern __shared__ __align__(16) float smem[];
+  extern __shared__ __align__(128) float smem[];
   float* sBp = smem;            // [D][DU+1]
   float* sQp = sBp + L::kBp;    // [D][D+1]
   const int ngroups = blockDim.x / D;
