@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define TTC_ABI_VERSION 1
+#define TTC_ABI_VERSION 2
 
 #define TTC_DTYPE_F32 0
 #define TTC_DTYPE_BF16 1
@@ -101,6 +101,27 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
                 void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_Q_f,
                 void* grad_lgA, void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status,
                 void* stream);
+
+/* Elementwise layer prologue (replaces the PyTorch ops of ttc/layers/ttc_layer.py:106-133
+ * between in_proj and the low-rank einsums; the einsums stay with the caller).
+ * Z [N, W] row-major in the activation dtype, W = nh*(4d + 2du + 1) + rB + rQ: per row nh
+ * head slices [h0 d | A_diag d | R_inv du | coeff_Qf d | lgA 1 | lgB du | lgQ d], then
+ * coeff_B (rB) and coeff_Q (rQ).  Outputs (activation dtype, contiguous):
+ *   A_diag = l2norm(.) [N,nh,d], R_inv = clamp(l2norm(softplus(.)), 1e-6) [N,nh,du],
+ *   coeff_Qf = l2norm(softplus(.)) [N,nh,d], lgA = -softplus(.) [N,nh], lgB [N,nh,du],
+ *   lgQ [N,nh,d], h0 [N,nh,d], coeff_B = l2norm(.) [N,rB], coeff_Q = l2norm(softplus(.)) [N,rQ]
+ * with l2norm(x) = x * rsqrt(sum(x^2) + 1e-6) in fp32 and torch's softplus (threshold 20).
+ * d, du, rB, rQ <= 64. */
+int ttc_prologue_fwd(const void* Z, int64_t N, int nh, int d, int du, int rB, int rQ, int dtype,
+                     void* A_diag, void* R_inv, void* coeff_Qf, void* lgA, void* lgB, void* lgQ,
+                     void* h0, void* coeff_B, void* coeff_Q, void* stream);
+
+/* Backward of ttc_prologue_fwd: dZ [N, W] from the gradients of its nine outputs (same
+ * shapes and dtype; any of them may be NULL, read as zero).  Z is the forward's input. */
+int ttc_prologue_bwd(const void* Z, int64_t N, int nh, int d, int du, int rB, int rQ, int dtype,
+                     const void* g_A_diag, const void* g_R_inv, const void* g_coeff_Qf,
+                     const void* g_lgA, const void* g_lgB, const void* g_lgQ, const void* g_h0,
+                     const void* g_coeff_B, const void* g_coeff_Q, void* dZ, void* stream);
 
 #ifdef __cplusplus
 }

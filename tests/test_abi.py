@@ -26,7 +26,8 @@ def declared_functions():
 
 def test_header_declares_expected_entry_points():
     names = declared_functions()
-    for n in ("ttc_lqr_fwd", "ttc_lqr_bwd", "ttc_abi_version", "ttc_supported", "ttc_last_error"):
+    for n in ("ttc_lqr_fwd", "ttc_lqr_bwd", "ttc_prologue_fwd", "ttc_prologue_bwd", "ttc_abi_version",
+              "ttc_supported", "ttc_last_error"):
         assert n in names
 
 
@@ -82,4 +83,27 @@ def test_bwd_rejects_bad_arguments_without_gpu(lib):
     assert bwd(lam0=None) == _lib.ERR_INVALID              # M without lam0
     assert bwd(grads=None) == _lib.ERR_INVALID
     assert bwd(d=48, du=48) == _lib.ERR_UNSUPPORTED
+    assert bwd(N=0) == _lib.OK
+
+
+def test_prologue_rejects_bad_arguments_without_gpu(lib):
+    from ttc_b200 import _lib
+    P = 16  # never dereferenced: rejected before any launch
+
+    def fwd(N=1, nh=1, d=16, du=16, rB=16, rQ=16, dtype=0, outs=P):
+        return lib.ttc_prologue_fwd(P, N, nh, d, du, rB, rQ, dtype, *([outs] * 9), None)
+
+    def bwd(N=1, nh=1, d=16, du=16, rB=16, rQ=16, dtype=0, dZ=P):
+        return lib.ttc_prologue_bwd(P, N, nh, d, du, rB, rQ, dtype, *([None] * 9), dZ, None)
+
+    assert fwd(N=-1) == _lib.ERR_INVALID
+    assert fwd(nh=0) == _lib.ERR_INVALID
+    assert fwd(rB=0) == _lib.ERR_INVALID
+    assert fwd(dtype=5) == _lib.ERR_INVALID
+    assert fwd(d=65) == _lib.ERR_UNSUPPORTED
+    assert b"<= 64" in lib.ttc_last_error()
+    assert fwd(outs=None) == _lib.ERR_INVALID
+    assert fwd(N=0) == _lib.OK
+    assert bwd(dZ=None) == _lib.ERR_INVALID
+    assert bwd(rQ=100) == _lib.ERR_UNSUPPORTED
     assert bwd(N=0) == _lib.OK

@@ -1,8 +1,10 @@
 """CPU tests of the host-side mirror of the reference interface (no GPU needed).
 
-The product's prologue / epilogue (ttc_b200.TTCLayer) runs in PyTorch; here it is
-exercised on the CPU with the oracle's solver put in place of the CUDA one, and compared
-with the reference's golden layer outputs."""
+The product layer (ttc_b200.TTCLayer) runs its elementwise prologue as a CUDA kernel and
+the LQR solve in the CUDA library; here its remaining host code (einsums, gamma bias,
+epilogue, shapes) is exercised on the CPU with the PyTorch prologue of prologue_ref.py and
+the oracle's solver put in their places, and compared with the reference's golden layer
+outputs.  The GPU tests cover the kernels themselves."""
 import os
 
 import numpy as np
@@ -10,9 +12,25 @@ import pytest
 import torch
 
 from oracle import ttc_oracle as O
+from prologue_ref import prologue_torch
 from ttc_cases import CONFIGS, layer_weights
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture
+def cpu_prologue(monkeypatch):
+    """Swap the layer's CUDA prologue for the PyTorch one (test-only)."""
+    import ttc_b200.layer as L
+    monkeypatch.setattr(L, "prologue", prologue_torch)
+
+
+def test_product_layer_has_no_cpu_path():
+    """Without the stand-ins the product layer refuses CPU tensors instead of falling back."""
+    from ttc_b200 import TTCLayer
+    layer = TTCLayer(8, 6, 16, 2, 16, 16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        layer(torch.randn(1, 3, 8), T=2)
 
 
 def test_registry_and_unknown_solver():
@@ -72,7 +90,7 @@ def test_solver_shape_contract():
 
 
 @pytest.mark.parametrize("case", ["layer_cfg2", "layer_cfg3"])
-def test_product_prologue_epilogue_against_reference(case):
+def test_product_prologue_epilogue_against_reference(case, cpu_prologue):
     """ttc_b200.TTCLayer's own prologue/epilogue code with the oracle fused solver in the
     solver slot reproduces the reference layer's y and gradients."""
     from ttc_b200 import TTCLayer
@@ -91,7 +109,7 @@ def test_product_prologue_epilogue_against_reference(case):
         assert O.max_rel(p.grad[::s], torch.from_numpy(z["g_" + pn])) < 1e-3, pn
 
 
-def test_four_dim_input_convention():
+def test_four_dim_input_convention(cpu_prologue):
     from ttc_b200 import TTCLayer
     layer = TTCLayer(8, 6, 16, 3, 16, 16)
     layer.solver = O.fused_solve

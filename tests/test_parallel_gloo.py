@@ -18,6 +18,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _use_cpu_prologue(setattr_fn=setattr):
+    import ttc_b200.layer as L
+    from prologue_ref import prologue_torch
+    setattr_fn(L, "prologue", prologue_torch)  # CPU stand-in for the CUDA prologue
+
+
 def _layer():
     from oracle import ttc_oracle as O
     from ttc_b200 import TTCLayer
@@ -43,6 +49,7 @@ def _worker(rank, world, port, out_dir, fail_rank):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=20))
+    _use_cpu_prologue()
     layer = _layer()
     x, dy = _data()
     xs, dys = shard_rows(x, rank, world), shard_rows(dy, rank, world)
@@ -72,7 +79,8 @@ def _run(world, tmp_path, fail_rank=-1):
     return [p.exitcode for p in procs]
 
 
-def test_sharded_gradients_equal_full_batch(tmp_path):
+def test_sharded_gradients_equal_full_batch(tmp_path, monkeypatch):
+    _use_cpu_prologue(monkeypatch.setattr)
     codes = _run(2, tmp_path)
     assert codes == [0, 0]
     layer = _layer()

@@ -2,9 +2,10 @@
 (ttc/layers/ttc_layer.py:24-153): same constructor signature, parameter names, shapes
 and initialisation, so a reference ``state_dict`` loads 1:1.
 
-The prologue (in_proj, split, l2norm / softplus, low-rank B / Q / Q_f mixtures,
-ttc_layer.py:104-135) and epilogue (l2norm, out_proj, :142-150) run as PyTorch ops on
-the GPU; the LQR solve runs in libttc_b200.so through ``LQR_SOLVER_IMPL_MAP``.
+The prologue's elementwise part (split, l2norm / softplus / clamp, ttc_layer.py:106-133)
+runs as one CUDA kernel each way (``prologue.py``); in_proj, the low-rank B / Q / Q_f
+mixtures and the epilogue (l2norm, out_proj, :142-150) are PyTorch / cuBLAS ops on the GPU;
+the LQR solve runs in libttc_b200.so through ``LQR_SOLVER_IMPL_MAP``.
 """
 from __future__ import annotations
 
@@ -14,6 +15,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .prologue import prologue
 from .solver import LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_with_status
 from . import _lib
 
@@ -74,16 +76,12 @@ class TTCLayer(nn.Module):
                     module.bias_gamma.data.fill_(0.0)
 
     def solver_inputs(self, x2d: torch.Tensor):
-        """Prologue (ttc_layer.py:104-135): rows [N, in_dim] -> the nine solver inputs."""
+        """Prologue (ttc_layer.py:104-135): rows [N, in_dim] -> the nine solver inputs.  The
+        elementwise part (split, l2norm, softplus, clamp, negation) is one CUDA kernel each way
+        (``prologue``); the low-rank B / Q / Q_f mixtures are cuBLAS einsums."""
         nh, d, du = self.num_heads, self.h_dim, self.u_dim
-        gamma_split = [1, du, d]
-        head_split = [d, d, du, d, sum(gamma_split)]
-        heads, coeff_B, coeff_Q = torch.split(
-            self.in_proj(x2d), [sum(head_split) * nh, self.b_rank, self.q_rank], dim=-1)
-        h0, A_diag, R_inv_diag, coeff_Qf, log_gammas = torch.split(
-            heads.view(-1, nh, sum(head_split)), head_split, dim=-1)
-        A_diag = l2norm(A_diag)
-        coeff_B, coeff_Q, coeff_Qf = l2norm(coeff_B), l2norm(F.softplus(coeff_Q)), l2norm(F.softplus(coeff_Qf))
+        A_diag, R_inv_diag, coeff_Qf, log_gamma_A, log_gamma_B, log_gamma_Q, h0, coeff_B, coeff_Q = \
+            prologue(self.in_proj(x2d), nh, d, du, self.b_rank, self.q_rank)
         B = torch.einsum("...r,rmn->...mn", coeff_B, self.Bs)
         if self.q_reparam == "plain":
             Q = torch.einsum("...r,rmn->...mn", coeff_Q, self.Qs)
@@ -91,14 +89,13 @@ class TTCLayer(nn.Module):
         else:
             Q = torch.einsum("...r,rmn,rkn->...mk", coeff_Q, self.Qs, self.Qs) / math.sqrt(d)
             Q_f = torch.einsum("...r,rmn,rkn->...mk", coeff_Qf, self.Qs, self.Qs) / math.sqrt(d)
-        R_inv_diag = torch.clamp(l2norm(F.softplus(R_inv_diag)), min=1e-6)
         if self.bias_gamma is not None:
-            log_gammas = -F.softplus(log_gammas) - F.relu(-self.bias_gamma[None, None, :])
-        else:
-            log_gammas = -F.softplus(log_gammas)
-        log_gamma_A, log_gamma_B, log_gamma_Q = torch.split(log_gammas, gamma_split, dim=-1)
-        return (A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A.squeeze(-1), log_gamma_B,
-                log_gamma_Q, h0)
+            # log_gammas = -softplus(.) - relu(-bias_gamma), split as [1, du, d] (:129-133)
+            bg = F.relu(-self.bias_gamma)
+            log_gamma_A = log_gamma_A - bg[0]
+            log_gamma_B = log_gamma_B - bg[1:1 + du]
+            log_gamma_Q = log_gamma_Q - bg[1 + du:]
+        return (A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0)
 
     def forward(self, h0: torch.Tensor, T: int) -> torch.Tensor:
         """y = layer(x, T).  x is [bs, seq, in_dim] as in the reference; a 4-D

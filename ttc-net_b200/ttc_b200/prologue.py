@@ -1,0 +1,55 @@
+"""The layer's elementwise prologue on the GPU: one CUDA kernel forward, one backward.
+
+Between in_proj and the low-rank einsums, TTCLayer.forward (ttc/layers/ttc_layer.py:106-133)
+splits the projection Z into per-head and per-row pieces and applies l2norm / softplus /
+clamp / negation to them.  As separate PyTorch ops that is ~20 launches forward and ~30
+backward (plus the concatenation of the split's gradient), all reading and writing Z-sized
+tensors.  ``prologue`` does the same arithmetic in ``ttc_prologue_fwd`` and its chain rule in
+``ttc_prologue_bwd`` (include/ttc_b200.h), with the reference's roundings in bf16.  No
+fallback: without the CUDA library these raise.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .solver import _DTYPES, _launch, _ptr
+
+
+class PrologueFunction(torch.autograd.Function):
+    """Z [N, W] -> (A_diag, R_inv, coeff_Qf, lgA, lgB, lgQ, h0, coeff_B, coeff_Q)."""
+
+    @staticmethod
+    def forward(ctx, Z, nh, d, du, rB, rQ):
+        if Z.dtype not in _DTYPES:
+            raise TypeError(f"ttc_b200 prologue: unsupported dtype {Z.dtype}")
+        if not Z.is_cuda:
+            raise RuntimeError("ttc_b200 prologue needs a CUDA tensor")
+        Z = Z.contiguous()
+        N = Z.shape[0]
+        assert Z.shape[1] == nh * (4 * d + 2 * du + 1) + rB + rQ, "in_proj width mismatch"
+        kw = dict(device=Z.device, dtype=Z.dtype)
+        outs = (torch.empty(N, nh, d, **kw), torch.empty(N, nh, du, **kw), torch.empty(N, nh, d, **kw),
+                torch.empty(N, nh, **kw), torch.empty(N, nh, du, **kw), torch.empty(N, nh, d, **kw),
+                torch.empty(N, nh, d, **kw), torch.empty(N, rB, **kw), torch.empty(N, rQ, **kw))
+        lib = _lib.load()
+        _launch("ttc_prologue_fwd", Z.device, lib.ttc_prologue_fwd, _ptr(Z), N, nh, d, du, rB, rQ,
+                _DTYPES[Z.dtype], *[_ptr(o) for o in outs])
+        ctx.save_for_backward(Z)
+        ctx.dims = (nh, d, du, rB, rQ)
+        return outs
+
+    @staticmethod
+    def backward(ctx, *grads):
+        (Z,) = ctx.saved_tensors
+        nh, d, du, rB, rQ = ctx.dims
+        gs = [None if g is None else g.to(Z.dtype).contiguous() for g in grads]
+        dZ = torch.empty_like(Z)
+        lib = _lib.load()
+        _launch("ttc_prologue_bwd", Z.device, lib.ttc_prologue_bwd, _ptr(Z), Z.shape[0], nh, d, du, rB,
+                rQ, _DTYPES[Z.dtype], *[_ptr(g) for g in gs], _ptr(dZ))
+        return dZ, None, None, None, None, None
+
+
+def prologue(Z: torch.Tensor, nh: int, d: int, du: int, rB: int, rQ: int):
+    return PrologueFunction.apply(Z, nh, d, du, rB, rQ)
