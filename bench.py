@@ -6,7 +6,9 @@
 One step = TTCLayer forward + backward on one batch of the chosen config (default:
 config 2, fp32, x[4,1024,16,64], h_dim 16, T 64), rows read as [B, L*H, in_dim].  At N > 1
 (torchrun) every rank runs the same per-GPU batch on its own data and the parameter
-gradients are all-reduced (NCCL) inside the step: weak scaling.  Rank 0 prints one JSON line.
+gradients are all-reduced (NCCL) inside the step: weak scaling -- except config 5, whose
+global batch of 64 sequences is split over the N GPUs (strong scaling, as BASELINE.json
+defines it).  Rank 0 prints one JSON line.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle's restatement of the
 ``riccati`` solver with autograd backward, all host threads) on a row sample of the same
@@ -256,6 +258,9 @@ def reference_arm(args, cfg):
     }), flush=True)
 
 
+STRONG_SCALING = {5}
+
+
 def workload_config(cfg, world, args, chunk):
     return {
         "workload": f"{cfg.name}: TTCLayer fwd+bwd, x[{cfg.B},{cfg.L},{cfg.H},{cfg.in_dim}] per GPU "
@@ -283,6 +288,14 @@ def main(argv=None):
 
     world, rank, local = dist_setup(args.gpus)
     device = torch.device("cuda", local)
+    # Config 5 is defined at a fixed global batch (64 sequences split over the GPUs):
+    # strong scaling.  The other configs keep their per-GPU batch (weak scaling).
+    strong = args.config in STRONG_SCALING and not args.batch
+    if strong:
+        import dataclasses
+        if cfg.B % world:
+            raise SystemExit(f"global batch {cfg.B} of config {args.config} does not split over {world} GPUs")
+        cfg = dataclasses.replace(cfg, B=cfg.B // world)
     torch.cuda.set_device(device)
     dtype = torch.bfloat16 if cfg.dtype == "bfloat16" else torch.float32
 
@@ -399,7 +412,7 @@ def main(argv=None):
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
             "dtype": "f32" if dtype == torch.float32 else "bf16 activations, f32 solver",
             "data": "synthetic (seeded N(0,1) x and dy, reference init distributions)",
             "config": workload_config(cfg, world, args, chunk),

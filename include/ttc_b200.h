@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define TTC_ABI_VERSION 2
+#define TTC_ABI_VERSION 3
 
 #define TTC_DTYPE_F32 0
 #define TTC_DTYPE_BF16 1
@@ -101,6 +101,37 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
                 void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_Q_f,
                 void* grad_lgA, void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status,
                 void* stream);
+
+/* ttc_lqr_fwd with Q_f given as the layer's rank-rQ mixture (ttc_layer.py:119-123,
+ * Q_f[n,h] = sum_r coeff_Qf[n,h,r] Q_basis[r]) instead of the [N,nh,d,d] tensor:
+ * coeff_Qf [N,nh,rQ], Q_basis [rQ,d,d], both in the activation dtype; each kernel mixes the
+ * rows of Q_f it needs.  Everything else as ttc_lqr_fwd. */
+int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                    const void* coeff_Qf, const void* Q_basis, int rQ, const void* log_gamma_A,
+                    const void* log_gamma_B, const void* log_gamma_Q, const void* h0, int64_t N, int nh,
+                    int d, int du, int T, int dtype, void* u, float* lam0, float* M, int* status,
+                    void* stream);
+
+/* Number of grad_basis_partial slices ttc_lqr_bwd_mix writes for this shape on the current
+ * device (it runs one wave of CTAs, each summing into its own slice); 0 if the mixed path is
+ * not available for the shape and rank (it needs d = du <= 32, at most 64 heads, a forward
+ * that saved M, and the rQ x d x d basis in the forward's shared memory), or minus an error
+ * code. */
+int64_t ttc_lqr_bwd_mix_slices(int64_t N, int nh, int d, int du, int rQ, int dtype);
+
+/* Backward of ttc_lqr_fwd_mix (saved lam0 and M required).  In place of grad_Q_f it writes
+ * grad_coeff_Qf [N,nh,rQ] (activation dtype) = <gQf, Q_basis[r]> per head, and
+ * grad_basis_partial [slices,rQ,d,d] (fp32; slices from ttc_lqr_bwd_mix_slices, every slice
+ * written): S = sum over slices of sum_heads coeff_Qf[r] h_T dh_T^T, so that the basis
+ * gradient is (S + S^T) / 2, the symmetrised convention of grad_Q_f.  Other outputs as
+ * ttc_lqr_bwd. */
+int ttc_lqr_bwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                    const void* coeff_Qf, const void* Q_basis, int rQ, const void* log_gamma_A,
+                    const void* log_gamma_B, const void* log_gamma_Q, const void* h0, const float* lam0,
+                    const float* M, const void* d_u, int64_t N, int nh, int d, int du, int T, int dtype,
+                    void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_coeff_Qf,
+                    float* grad_basis_partial, int64_t slices, void* grad_lgA, void* grad_lgB,
+                    void* grad_lgQ, void* grad_h0, int* status, void* stream);
 
 /* Elementwise layer prologue (replaces the PyTorch ops of ttc/layers/ttc_layer.py:106-133
  * between in_proj and the low-rank einsums; the einsums stay with the caller).

@@ -167,6 +167,135 @@ __device__ __forceinline__ void accumulate_unit(float (&acc)[D / 8][4], const fl
   }
 }
 
+// The layer's Q_f mixture on the backward side (Q_f = sum_r coeff_Qf[r] basis[r],
+// ttc_layer.py:119-123) for all heads of a CTA's row group, from every warp's final state
+// (h, dh) staged at `stage_off` of its staging area (rows 0-7 h, rows 8-15 dh of its 8 heads,
+// output-fragment positions) and its heads' coeff_Qf at `coeff_off` ([8][rQ], zero for
+// padding heads).  The Q_f gradient of a head is the rank-2
+// gQf = (h dh^T + dh h^T) / 2 (symplectic_iter.py:855-857), so
+//   grad_coeff_Qf[r] = <gQf, basis[r]> = ((h basis[r]) . dh + (dh basis[r]) . h) / 2,
+//   slice[r] += sum_heads coeff_Qf[r] h dh^T   (the caller forms (S + S^T) / 2 from the sum
+//   of all CTAs' slices).
+// Basis index r belongs to warp r mod W, which loads basis[r] in fragment order once, runs
+// over the staged warps in order and read-modify-writes slice[r] once: deterministic.
+template <int D, typename TIn>
+__device__ __forceinline__ bool qmix_cta(const float* warp_s, int stage_off, int coeff_off, int nwarps, int wpr,
+                                         int64_t n0,
+                                         int64_t N, int nh, const TIn* __restrict__ basis, int rQ,
+                                         const TIn* __restrict__ coeff, TIn* __restrict__ gcoeff,
+                                         float* __restrict__ slice, int warp, int g, int t) {
+  constexpr int SS = AdjMma<D>::SS, NT = D / 8, MT = D / 16, kWarp = AdjMma<D>::kWarp;
+  bool bad = false;
+  for (int r = warp; r < rQ; r += nwarps) {
+    // basis[r] as the constant operand: W[k][n] = basis[r][k][n], K rows permuted as the
+    // other products (slot t <-> entry 8kk + 2t, slot t + 4 <-> 8kk + 2t + 1).
+    uint32_t wh[NT][NT][2], wl[NT][NT][2];
+    const TIn* Wr = basis + (int64_t)r * D * D;
+#pragma unroll
+    for (int kk = 0; kk < NT; ++kk)
+#pragma unroll
+      for (int nj = 0; nj < NT; ++nj) {
+        wmma::split(ldf(Wr + (8 * kk + 2 * t) * D + 8 * nj + g), wh[kk][nj][0], wl[kk][nj][0]);
+        wmma::split(ldf(Wr + (8 * kk + 2 * t + 1) * D + 8 * nj + g), wh[kk][nj][1], wl[kk][nj][1]);
+      }
+    float acc[MT][NT][4];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int nj = 0; nj < NT; ++nj)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[mi][nj][e] = 0.f;
+    for (int sw = 0; sw < nwarps; ++sw) {
+      const float* S = warp_s + (size_t)sw * kWarp + stage_off;
+      const int64_t ns = n0 + sw / wpr;
+      const int hb = sw % wpr;
+      const bool rowv = ns < N;
+      const int64_t prow = ns * nh;
+      // grad_coeff_Qf of the staged warp's heads: [h; dh] basis[r]
+      float Hs[NT][4], P[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const float2 a = *reinterpret_cast<const float2*>(S + g * SS + 8 * j + 2 * t);
+        const float2 b = *reinterpret_cast<const float2*>(S + (g + 8) * SS + 8 * j + 2 * t);
+        Hs[j][0] = a.x;
+        Hs[j][1] = a.y;
+        Hs[j][2] = b.x;
+        Hs[j][3] = b.y;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) P[j][e] = 0.f;
+      }
+#pragma unroll
+      for (int kk = 0; kk < NT; ++kk) {
+        uint32_t ah[4], al[4];
+        wmma::split(Hs[kk][0], ah[0], al[0]);
+        wmma::split(Hs[kk][2], ah[1], al[1]);
+        wmma::split(Hs[kk][1], ah[2], al[2]);
+        wmma::split(Hs[kk][3], ah[3], al[3]);
+#pragma unroll
+        for (int nj = 0; nj < NT; ++nj) {
+          wmma::m16n8k8(P[nj], al, wh[kk][nj][0], wh[kk][nj][1]);
+          wmma::m16n8k8(P[nj], ah, wl[kk][nj][0], wl[kk][nj][1]);
+          wmma::m16n8k8(P[nj], ah, wh[kk][nj][0], wh[kk][nj][1]);
+        }
+      }
+      float sdot = 0.f;
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) sdot = fmaf(P[j][e], Hs[j][2 + e], fmaf(P[j][2 + e], Hs[j][e], sdot));
+      sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+      sdot += __shfl_xor_sync(0xffffffffu, sdot, 2);
+      sdot *= 0.5f;
+      const int hg = hb * 8 + g;
+      if (rowv && hg < nh && t == 0) {
+        bad |= unstable(sdot);
+        stf(gcoeff + (prow + hg) * rQ + r, sdot);
+      }
+      // slice[r] += sum over the staged heads of coeff[r] h dh^T (MMA with K = the 8 heads):
+      // A[i][k] = h_k[i], B[k][j] = coeff_k[r] dh_k[j].
+      // coeff[r] of the heads in k-slots t and t + 4, staged by warp sw as [8][rQ]
+      const float* Cs = warp_s + (size_t)sw * kWarp + coeff_off;
+      const float c0 = Cs[t * rQ + r], c1 = Cs[(t + 4) * rQ + r];
+      uint32_t xh[MT][4], xl[MT][4];
+#pragma unroll
+      for (int mi = 0; mi < MT; ++mi) {
+        wmma::split(S[t * SS + 16 * mi + g], xh[mi][0], xl[mi][0]);
+        wmma::split(S[t * SS + 16 * mi + g + 8], xh[mi][1], xl[mi][1]);
+        wmma::split(S[(t + 4) * SS + 16 * mi + g], xh[mi][2], xl[mi][2]);
+        wmma::split(S[(t + 4) * SS + 16 * mi + g + 8], xh[mi][3], xl[mi][3]);
+      }
+#pragma unroll
+      for (int nj = 0; nj < NT; ++nj) {
+        uint32_t bh0, bl0, bh1, bl1;
+        wmma::split(c0 * S[(8 + t) * SS + 8 * nj + g], bh0, bl0);
+        wmma::split(c1 * S[(12 + t) * SS + 8 * nj + g], bh1, bl1);
+#pragma unroll
+        for (int mi = 0; mi < MT; ++mi) {
+          wmma::m16n8k8(acc[mi][nj], xl[mi], bh0, bh1);
+          wmma::m16n8k8(acc[mi][nj], xh[mi], bl0, bl1);
+          wmma::m16n8k8(acc[mi][nj], xh[mi], bh0, bh1);
+        }
+      }
+    }
+    float* sr = slice + (int64_t)r * D * D;
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int nj = 0; nj < NT; ++nj) {
+        float2* q0 = reinterpret_cast<float2*>(sr + (16 * mi + g) * D + 8 * nj + 2 * t);
+        float2* q1 = reinterpret_cast<float2*>(sr + (16 * mi + g + 8) * D + 8 * nj + 2 * t);
+        float2 v0 = *q0, v1 = *q1;
+        v0.x += acc[mi][nj][0];
+        v0.y += acc[mi][nj][1];
+        v1.x += acc[mi][nj][2];
+        v1.y += acc[mi][nj][3];
+        *q0 = v0;
+        *q1 = v1;
+      }
+  }
+  return bad;
+}
+
 // Backward from the forward's lambda0 and either M (d_p = M d_u per head, fused_lqr.py:
 // 185-187) or d_p itself.  Grid: ceil(N / R) CTAs of R rows x W = ceil(nh / 8) warps; the W
 // warps of a row meet at one named barrier per step (id 1 + row), after which warp w
@@ -183,6 +312,8 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                    TIn* __restrict__ gA_out, TIn* __restrict__ gB_out, TIn* __restrict__ gQ_out,
                    TIn* __restrict__ gR_out, TIn* __restrict__ gQf_out, TIn* __restrict__ glgA_out,
                    TIn* __restrict__ glgB_out, TIn* __restrict__ glgQ_out, TIn* __restrict__ gh0_out,
+                   const TIn* __restrict__ Qbasis, int rQ, const TIn* __restrict__ cQf,
+                   TIn* __restrict__ gcQf_out, float* __restrict__ gQb_partial,
                    int* __restrict__ status) {
   using C = AdjMma<D>;
   constexpr int NT = C::NT, MT = C::MT;
@@ -192,305 +323,333 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   const int g = lane >> 2, t = lane & 3;
   const int wpr = (nh + 7) / 8;
   const int rloc = warp / wpr, hb = warp % wpr;
-  const int64_t n0 = (int64_t)blockIdx.x * rows_per_cta;
-  const int64_t n = n0 + rloc;
-  const bool row_ok = n < N;
   float* rows_s = smem;
   float* warp_s = smem + (size_t)rows_per_cta * C::kRow;
   float* row_stage = warp_s + (size_t)(rloc * wpr) * C::kWarp;  // warp 0 of this row
   float* stg = warp_s + (size_t)warp * C::kWarp;
-
-  // The CTA's rows: constant operands Q^T, B, B^T, Q in fragment order, symmetry flag.
-  if (tid < rows_per_cta) reinterpret_cast<int*>(rows_s + tid * C::kRow + 4 * C::kFrag)[0] = 1;
-  __syncthreads();
-  for (int r = 0; r < rows_per_cta; ++r) {
-    const int64_t nr = n0 + r;
-    if (nr >= N) break;
-    float* base = rows_s + r * C::kRow;
-    const TIn* Bn = Bm + nr * (D * D);
-    const TIn* Qn = Qm + nr * (D * D);
-    build_operand<D>(base, [&](int k, int c) { return ldf(Qn + c * D + k); }, tid, nthreads);
-    build_operand<D>(base + C::kFrag, [&](int k, int c) { return ldf(Bn + k * D + c); }, tid, nthreads);
-    build_operand<D>(base + 2 * C::kFrag, [&](int k, int c) { return ldf(Bn + c * D + k); }, tid, nthreads);
-    build_operand<D>(base + 3 * C::kFrag, [&](int k, int c) { return ldf(Qn + k * D + c); }, tid, nthreads);
-    bool asym = false;
-    for (int e = tid; e < D * D; e += nthreads) asym |= ldf(Qn + e) != ldf(Qn + (e % D) * D + e / D);
-    if (asym) reinterpret_cast<int*>(base + 4 * C::kFrag)[0] = 0;
+  // Q_f given as a mixture (Qbasis != NULL): this CTA's own [rQ][D][D] partial of the basis
+  // gradient, accumulated over every row group the CTA walks.
+  float* slice = nullptr;
+  if (Qbasis != nullptr) {
+    slice = gQb_partial + (int64_t)blockIdx.x * rQ * D * D;
+    for (int e = tid; e < rQ * D * D; e += nthreads) slice[e] = 0.f;
   }
-  __syncthreads();
-
-  const float* rbase = rows_s + rloc * C::kRow;
-  const float4* Wqt = reinterpret_cast<const float4*>(rbase);
-  const float4* Wb = reinterpret_cast<const float4*>(rbase + C::kFrag);
-  const float4* Wbt = reinterpret_cast<const float4*>(rbase + 2 * C::kFrag);
-  const float4* Wq = reinterpret_cast<const float4*>(rbase + 3 * C::kFrag);
-  const bool sym = reinterpret_cast<const int*>(rbase + 4 * C::kFrag)[0] != 0;
-
-  const int h = hb * 8 + g;
-  const bool valid = row_ok && h < nh;
-  const int64_t p = valid ? n * nh + h : 0;
-  // slot (j, s) of a thread is entry 8j + 2t + s; index 2 + s of a pair array is the tangent
-  float a[NT][2], lgQ2[NT][2], lgB2[NT][2], rinv[NT][2];
-  float L[NT][4], H[NT][4];
-  const float lgA2 = valid ? ldf(lgA + p) * kLog2e : 0.f;
-#pragma unroll
-  for (int j = 0; j < NT; ++j) {
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      const int e = 8 * j + 2 * t + s;
-      a[j][s] = valid ? ldf(A_diag + p * D + e) : 0.f;
-      lgQ2[j][s] = valid ? ldf(lgQ + p * D + e) * kLog2e : 0.f;
-      lgB2[j][s] = valid ? ldf(lgB + p * D + e) * kLog2e : 0.f;
-      rinv[j][s] = valid ? ldf(Rinv + p * D + e) : 1.f;
-      H[j][s] = valid ? ldf(H0 + p * D + e) : 0.f;
-      H[j][2 + s] = 0.f;
-      L[j][s] = valid ? lam0_in[p * D + e] : 0.f;
-      float dl = 0.f;
-      if (valid) {
-        if constexpr (FROM_M) {
-          const float* mrow = M_or_dp + (p * D + e) * D;
-          for (int c = 0; c < D; ++c) dl = fmaf(mrow[c], ldf(dU + p * D + c), dl);
-        } else {
-          dl = M_or_dp[p * D + e];
-        }
-      }
-      L[j][2 + s] = dl;
-    }
-  }
-
-  float gA[NT][2], glgQ[NT][2], gR[NT][2], glgB[NT][2], dqp[NT][2];
-  float glgA = 0.f;
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      gA[j][s] = glgQ[j][s] = gR[j][s] = glgB[j][s] = 0.f;
-      dqp[j][s] = 1.0f;
-    }
-  float acc[UPW][NT][4];
-#pragma unroll
-  for (int q = 0; q < UPW; ++q)
-#pragma unroll
-    for (int nj = 0; nj < NT; ++nj)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) acc[q][nj][r] = 0.f;
-
   bool bad = false;
-  for (int k = 0; k < T; ++k) {
-    const float ke = static_cast<float>(k + 1);
-    float* S0 = stg + (k & 1) * 3 * C::kStage;  // [lambda; dlambda]
-    float* S1 = S0 + C::kStage;                 // [u e^lgB; du e^lgB]
-    float* S2 = S0 + 2 * C::kStage;             // [h Dq; dh Dq]
-    if (k > 0) {
-      // lambda -= Q_k h, dlambda -= Q_k dh with Q_k = Dq Q Dq (symplectic_iter.py:766-775)
-      // and the log_gamma_Q gradient of step k-1 (:871-877).
-      float HD[NT][4], QH[NT][4], QTH[NT][4];
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r & 1];
-      frag_product<D>(HD, QH, Wqt, lane);
-      if (!sym) frag_product<D>(HD, QTH, Wq, lane);
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          const float qh = QH[j][s], qdh = QH[j][2 + s];
-          const float qth = sym ? qh : QTH[j][s], qtdh = sym ? qdh : QTH[j][2 + s];
-          L[j][s] = fmaf(-dqp[j][s], qh, L[j][s]);
-          L[j][2 + s] = fmaf(-dqp[j][s], qdh, L[j][2 + s]);
-          glgQ[j][s] = fmaf(0.5f * fmaf(H[j][2 + s], qh + qth, H[j][s] * (qdh + qtdh)),
-                            static_cast<float>(k) * dqp[j][s], glgQ[j][s]);
-        }
-      }
-    } else if (valid) {
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          bad |= unstable(L[j][2 + s]);
-          stf(gh0_out + p * D + 8 * j + 2 * t + s, L[j][2 + s]);  // dh_0 = dlambda_0
-        }
-    }
-    const float eA = exp_scaled(lgA2, ke);
-    float At[NT][2];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        At[j][s] = fmaf(a[j][s], eA, 1.0f);
-        const float rAt = recip(At[j][s]);
-        L[j][s] *= rAt;
-        L[j][2 + s] *= rAt;
-        const float dA = fmaf(L[j][s], H[j][2 + s], L[j][2 + s] * H[j][s]);
-        gA[j][s] = fmaf(dA, eA, gA[j][s]);
-        glgA = fmaf(dA * a[j][s], ke * eA, glgA);
-      }
-    }
-    stage_rows<D>(S0, L, g, t);
-    // u = -R_inv (B e^lgB)^T lambda and its tangent (symplectic_iter.py:800-830)
-    float UE[NT][4];
-    {
-      float BL[NT][4];
-      frag_product<D>(L, BL, Wb, lane);
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          const float eB = exp_scaled(lgB2[j][s], ke);
-          const float bl = BL[j][s], bdl = BL[j][2 + s];
-          const float u = -(bl * eB) * rinv[j][s];
-          float du = -(bdl * eB) * rinv[j][s];
-          if (k == 0 && valid) du = fmaf(ldf(dU + p * D + 8 * j + 2 * t + s), -rinv[j][s], du);
-          glgB[j][s] = fmaf(fmaf(du, bl, u * bdl), ke * eB, glgB[j][s]);
-          gR[j][s] = fmaf(-(u * du), recip(rinv[j][s] * rinv[j][s]), gR[j][s]);
-          UE[j][s] = u * eB;
-          UE[j][2 + s] = du * eB;
-        }
-      }
-    }
-    stage_rows<D>(S1, UE, g, t);
-    // h <- A h + B e^lgB u (symplectic_iter.py:832-850)
-    {
-      float BU[NT][4];
-      frag_product<D>(UE, BU, Wbt, lane);
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          H[j][s] = fmaf(H[j][s], At[j][s], BU[j][s]);
-          H[j][2 + s] = fmaf(H[j][2 + s], At[j][s], BU[j][2 + s]);
-          dqp[j][s] = exp_scaled(lgQ2[j][s], ke);
-        }
-      }
-    }
-    if (k < T - 1) {
-      float HD[NT][4];
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r & 1];
-      stage_rows<D>(S2, HD, g, t);
-    }
-    // Every warp of the row has staged step k (and finished reading step k - 1's buffer).
-    if (!C::kOwn && wpr > 1) {
-      asm volatile("bar.sync %0, %1;" ::"r"(1 + rloc), "r"(32 * wpr) : "memory");
-    } else {
-      __syncwarp();
-    }
-    // grad_B += lambda (du e^lgB)^T + dlambda (u e^lgB)^T ;
-    // grad_Q += (h Dq)(dh Dq)^T + (dh Dq)(h Dq)^T  (the 1/2 is applied at the end)
-#pragma unroll
-    for (int q = 0; q < UPW; ++q) {
-      const int unit = C::kOwn ? q : hb + q * wpr;
-      if (unit < C::kUnits) {
-        const bool isq = unit >= MT;
-        if (!isq || k < T - 1) {
-          const int mi = isq ? unit - MT : unit;
-          const int off = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : 0);
-          const int offy = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : C::kStage);
-          if constexpr (C::kOwn) {
-            accumulate_unit<D>(acc[q], stg + off, stg + offy, mi, g, t);
-          } else {
-            for (int w = 0; w < wpr; ++w) {
-              const float* base = row_stage + (size_t)w * C::kWarp;
-              accumulate_unit<D>(acc[q], base + off, base + offy, mi, g, t);
-            }
-          }
-        }
-      }
-    }
-  }
+  const int64_t ngroups = (N + rows_per_cta - 1) / rows_per_cta;
+  for (int64_t grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
+    const int64_t n0 = grp * rows_per_cta;
+    const int64_t n = n0 + rloc;
+    const bool row_ok = n < N;
 
-  // grad_Qf = (h dh^T + dh h^T) / 2 at the final state (symplectic_iter.py:855-857), from
-  // the staging buffer of step T (unused by the row's other warps).
-  {
-    float* S = stg + (T & 1) * 3 * C::kStage;
-    stage_rows<D>(S, H, g, t);
-    __syncwarp();
-    for (int e = lane; e < 8 * D * D; e += 32) {
-      const int hh = e / (D * D), i = (e / D) % D, jj = e % D;
-      const int h2 = hb * 8 + hh;
-      if (row_ok && h2 < nh) {
-        const float v = 0.5f * fmaf(S[hh * C::SS + i], S[(hh + 8) * C::SS + jj],
-                                    S[(hh + 8) * C::SS + i] * S[hh * C::SS + jj]);
-        bad |= unstable(v);
-        stf(gQf_out + ((n * nh + h2) * D + i) * D + jj, v);
-      }
+    // The CTA's rows: constant operands Q^T, B, B^T, Q in fragment order, symmetry flag.
+    if (tid < rows_per_cta) reinterpret_cast<int*>(rows_s + tid * C::kRow + 4 * C::kFrag)[0] = 1;
+    __syncthreads();
+    for (int r = 0; r < rows_per_cta; ++r) {
+      const int64_t nr = n0 + r;
+      if (nr >= N) break;
+      float* base = rows_s + r * C::kRow;
+      const TIn* Bn = Bm + nr * (D * D);
+      const TIn* Qn = Qm + nr * (D * D);
+      build_operand<D>(base, [&](int k, int c) { return ldf(Qn + c * D + k); }, tid, nthreads);
+      build_operand<D>(base + C::kFrag, [&](int k, int c) { return ldf(Bn + k * D + c); }, tid, nthreads);
+      build_operand<D>(base + 2 * C::kFrag, [&](int k, int c) { return ldf(Bn + c * D + k); }, tid, nthreads);
+      build_operand<D>(base + 3 * C::kFrag, [&](int k, int c) { return ldf(Qn + k * D + c); }, tid, nthreads);
+      bool asym = false;
+      for (int e = tid; e < D * D; e += nthreads) asym |= ldf(Qn + e) != ldf(Qn + (e % D) * D + e / D);
+      if (asym) reinterpret_cast<int*>(base + 4 * C::kFrag)[0] = 0;
     }
-  }
-  // Per-head outputs.
-  float glgA_sum = glgA;
-  glgA_sum += __shfl_xor_sync(0xffffffffu, glgA_sum, 1);
-  glgA_sum += __shfl_xor_sync(0xffffffffu, glgA_sum, 2);
-  if (valid) {
+    __syncthreads();
+
+    const float* rbase = rows_s + rloc * C::kRow;
+    const float4* Wqt = reinterpret_cast<const float4*>(rbase);
+    const float4* Wb = reinterpret_cast<const float4*>(rbase + C::kFrag);
+    const float4* Wbt = reinterpret_cast<const float4*>(rbase + 2 * C::kFrag);
+    const float4* Wq = reinterpret_cast<const float4*>(rbase + 3 * C::kFrag);
+    const bool sym = reinterpret_cast<const int*>(rbase + 4 * C::kFrag)[0] != 0;
+
+    const int h = hb * 8 + g;
+    const bool valid = row_ok && h < nh;
+    const int64_t p = valid ? n * nh + h : 0;
+    // slot (j, s) of a thread is entry 8j + 2t + s; index 2 + s of a pair array is the tangent
+    float a[NT][2], lgQ2[NT][2], lgB2[NT][2], rinv[NT][2];
+    float L[NT][4], H[NT][4];
+    const float lgA2 = valid ? ldf(lgA + p) * kLog2e : 0.f;
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
 #pragma unroll
       for (int s = 0; s < 2; ++s) {
         const int e = 8 * j + 2 * t + s;
-        bad |= unstable(gA[j][s]) | unstable(glgQ[j][s]) | unstable(gR[j][s]) | unstable(glgB[j][s]);
-        stf(gA_out + p * D + e, gA[j][s]);
-        stf(glgQ_out + p * D + e, glgQ[j][s]);
-        stf(gR_out + p * D + e, gR[j][s]);
-        stf(glgB_out + p * D + e, glgB[j][s]);
+        a[j][s] = valid ? ldf(A_diag + p * D + e) : 0.f;
+        lgQ2[j][s] = valid ? ldf(lgQ + p * D + e) * kLog2e : 0.f;
+        lgB2[j][s] = valid ? ldf(lgB + p * D + e) * kLog2e : 0.f;
+        rinv[j][s] = valid ? ldf(Rinv + p * D + e) : 1.f;
+        H[j][s] = valid ? ldf(H0 + p * D + e) : 0.f;
+        H[j][2 + s] = 0.f;
+        L[j][s] = valid ? lam0_in[p * D + e] : 0.f;
+        float dl = 0.f;
+        if (valid) {
+          if constexpr (FROM_M) {
+            const float* mrow = M_or_dp + (p * D + e) * D;
+            for (int c = 0; c < D; ++c) dl = fmaf(mrow[c], ldf(dU + p * D + c), dl);
+          } else {
+            dl = M_or_dp[p * D + e];
+          }
+        }
+        L[j][2 + s] = dl;
       }
     }
-    if (t == 0) {
-      bad |= unstable(glgA_sum);
-      stf(glgA_out + p, glgA_sum);
-    }
-  }
-  if constexpr (C::kOwn) {
-    // The row's warps add their partial sums in warp order (staging area reused).
-    static_assert(!C::kOwn || 2 * D * D <= C::kWarp, "reduction area");
-    __syncthreads();
+
+    float gA[NT][2], glgQ[NT][2], gR[NT][2], glgB[NT][2], dqp[NT][2];
+    float glgA = 0.f;
 #pragma unroll
-    for (int q = 0; q < UPW; ++q) {
-      const bool isq = q >= MT;
-      const int mi = isq ? q - MT : q;
-      float* red = stg + (isq ? D * D : 0);
+    for (int j = 0; j < NT; ++j)
 #pragma unroll
-      for (int nj = 0; nj < NT; ++nj) {
-        const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
-        *reinterpret_cast<float2*>(red + r0 * D + c0) = make_float2(acc[q][nj][0], acc[q][nj][1]);
-        *reinterpret_cast<float2*>(red + (r0 + 8) * D + c0) = make_float2(acc[q][nj][2], acc[q][nj][3]);
+      for (int s = 0; s < 2; ++s) {
+        gA[j][s] = glgQ[j][s] = gR[j][s] = glgB[j][s] = 0.f;
+        dqp[j][s] = 1.0f;
       }
-    }
-    __syncthreads();
-    for (int r = 0; r < rows_per_cta; ++r) {
-      const int64_t nr = n0 + r;
-      if (nr >= N) break;
-      for (int e = tid; e < 2 * D * D; e += nthreads) {
-        float v = 0.f;
-        for (int w = 0; w < wpr; ++w) v += warp_s[(size_t)(r * wpr + w) * C::kWarp + e];
-        if (e >= D * D) v *= 0.5f;
-        bad |= unstable(v);
-        stf((e < D * D ? gB_out : gQ_out) + nr * (D * D) + (e % (D * D)), v);
+    float acc[UPW][NT][4];
+#pragma unroll
+    for (int q = 0; q < UPW; ++q)
+#pragma unroll
+      for (int nj = 0; nj < NT; ++nj)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[q][nj][r] = 0.f;
+
+    for (int k = 0; k < T; ++k) {
+      const float ke = static_cast<float>(k + 1);
+      float* S0 = stg + (k & 1) * 3 * C::kStage;  // [lambda; dlambda]
+      float* S1 = S0 + C::kStage;                 // [u e^lgB; du e^lgB]
+      float* S2 = S0 + 2 * C::kStage;             // [h Dq; dh Dq]
+      if (k > 0) {
+        // lambda -= Q_k h, dlambda -= Q_k dh with Q_k = Dq Q Dq (symplectic_iter.py:766-775)
+        // and the log_gamma_Q gradient of step k-1 (:871-877).
+        float HD[NT][4], QH[NT][4], QTH[NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r & 1];
+        frag_product<D>(HD, QH, Wqt, lane);
+        if (!sym) frag_product<D>(HD, QTH, Wq, lane);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            const float qh = QH[j][s], qdh = QH[j][2 + s];
+            const float qth = sym ? qh : QTH[j][s], qtdh = sym ? qdh : QTH[j][2 + s];
+            L[j][s] = fmaf(-dqp[j][s], qh, L[j][s]);
+            L[j][2 + s] = fmaf(-dqp[j][s], qdh, L[j][2 + s]);
+            glgQ[j][s] = fmaf(0.5f * fmaf(H[j][2 + s], qh + qth, H[j][s] * (qdh + qtdh)),
+                              static_cast<float>(k) * dqp[j][s], glgQ[j][s]);
+          }
+        }
+      } else if (valid) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            bad |= unstable(L[j][2 + s]);
+            stf(gh0_out + p * D + 8 * j + 2 * t + s, L[j][2 + s]);  // dh_0 = dlambda_0
+          }
       }
-    }
-  } else if (row_ok) {
-    // Each unit holds the sum over all the row's heads.
+      const float eA = exp_scaled(lgA2, ke);
+      float At[NT][2];
 #pragma unroll
-    for (int q = 0; q < UPW; ++q) {
-      const int unit = hb + q * wpr;
-      if (unit < C::kUnits) {
-        const bool isq = unit >= MT;
-        const int mi = isq ? unit - MT : unit;
-        const float sc = isq ? 0.5f : 1.0f;
-        TIn* out = (isq ? gQ_out : gB_out) + n * (D * D);
+      for (int j = 0; j < NT; ++j) {
 #pragma unroll
-        for (int nj = 0; nj < NT; ++nj) {
-          const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
-          const float v[4] = {sc * acc[q][nj][0], sc * acc[q][nj][1], sc * acc[q][nj][2], sc * acc[q][nj][3]};
-          bad |= unstable(v[0]) | unstable(v[1]) | unstable(v[2]) | unstable(v[3]);
-          stf(out + r0 * D + c0, v[0]);
-          stf(out + r0 * D + c0 + 1, v[1]);
-          stf(out + (r0 + 8) * D + c0, v[2]);
-          stf(out + (r0 + 8) * D + c0 + 1, v[3]);
+        for (int s = 0; s < 2; ++s) {
+          At[j][s] = fmaf(a[j][s], eA, 1.0f);
+          const float rAt = recip(At[j][s]);
+          L[j][s] *= rAt;
+          L[j][2 + s] *= rAt;
+          const float dA = fmaf(L[j][s], H[j][2 + s], L[j][2 + s] * H[j][s]);
+          gA[j][s] = fmaf(dA, eA, gA[j][s]);
+          glgA = fmaf(dA * a[j][s], ke * eA, glgA);
+        }
+      }
+      stage_rows<D>(S0, L, g, t);
+      // u = -R_inv (B e^lgB)^T lambda and its tangent (symplectic_iter.py:800-830)
+      float UE[NT][4];
+      {
+        float BL[NT][4];
+        frag_product<D>(L, BL, Wb, lane);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            const float eB = exp_scaled(lgB2[j][s], ke);
+            const float bl = BL[j][s], bdl = BL[j][2 + s];
+            const float u = -(bl * eB) * rinv[j][s];
+            float du = -(bdl * eB) * rinv[j][s];
+            if (k == 0 && valid) du = fmaf(ldf(dU + p * D + 8 * j + 2 * t + s), -rinv[j][s], du);
+            glgB[j][s] = fmaf(fmaf(du, bl, u * bdl), ke * eB, glgB[j][s]);
+            gR[j][s] = fmaf(-(u * du), recip(rinv[j][s] * rinv[j][s]), gR[j][s]);
+            UE[j][s] = u * eB;
+            UE[j][2 + s] = du * eB;
+          }
+        }
+      }
+      stage_rows<D>(S1, UE, g, t);
+      // h <- A h + B e^lgB u (symplectic_iter.py:832-850)
+      {
+        float BU[NT][4];
+        frag_product<D>(UE, BU, Wbt, lane);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            H[j][s] = fmaf(H[j][s], At[j][s], BU[j][s]);
+            H[j][2 + s] = fmaf(H[j][2 + s], At[j][s], BU[j][2 + s]);
+            dqp[j][s] = exp_scaled(lgQ2[j][s], ke);
+          }
+        }
+      }
+      if (k < T - 1) {
+        float HD[NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r & 1];
+        stage_rows<D>(S2, HD, g, t);
+      }
+      // Every warp of the row has staged step k (and finished reading step k - 1's buffer).
+      if (!C::kOwn && wpr > 1) {
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + rloc), "r"(32 * wpr) : "memory");
+      } else {
+        __syncwarp();
+      }
+      // grad_B += lambda (du e^lgB)^T + dlambda (u e^lgB)^T ;
+      // grad_Q += (h Dq)(dh Dq)^T + (dh Dq)(h Dq)^T  (the 1/2 is applied at the end)
+#pragma unroll
+      for (int q = 0; q < UPW; ++q) {
+        const int unit = C::kOwn ? q : hb + q * wpr;
+        if (unit < C::kUnits) {
+          const bool isq = unit >= MT;
+          if (!isq || k < T - 1) {
+            const int mi = isq ? unit - MT : unit;
+            const int off = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : 0);
+            const int offy = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : C::kStage);
+            if constexpr (C::kOwn) {
+              accumulate_unit<D>(acc[q], stg + off, stg + offy, mi, g, t);
+            } else {
+              for (int w = 0; w < wpr; ++w) {
+                const float* base = row_stage + (size_t)w * C::kWarp;
+                accumulate_unit<D>(acc[q], base + off, base + offy, mi, g, t);
+              }
+            }
+          }
         }
       }
     }
+
+    // grad_Qf = (h dh^T + dh h^T) / 2 at the final state (symplectic_iter.py:855-857), from
+    // the staging buffer of step T (unused by the row's other warps); for a mixed Q_f its
+    // contractions with the basis instead.
+    if (Qbasis != nullptr) {
+      // final state into this step's staging buffer (the row's other warps last read it at
+      // step T - 2); after a CTA barrier, the heads' coeff_Qf into the other buffer
+      __syncwarp();
+      stage_rows<D>(stg + (T & 1) * 3 * C::kStage, H, g, t);
+      __syncthreads();
+      {
+        float* Cs = stg + ((T + 1) & 1) * 3 * C::kStage;
+        for (int e = lane; e < 8 * rQ; e += 32) {
+          const int hk = hb * 8 + e / rQ;
+          Cs[e] = (row_ok && hk < nh) ? ldf(cQf + (n * nh + hk) * rQ + e % rQ) : 0.f;
+        }
+      }
+      __syncthreads();
+      bad |= qmix_cta<D, TIn>(warp_s, (T & 1) * 3 * C::kStage, ((T + 1) & 1) * 3 * C::kStage, blockDim.x >> 5,
+                              wpr, n0, N, nh, Qbasis, rQ, cQf, gcQf_out, slice, warp, g, t);
+    } else {
+      float* S = stg + (T & 1) * 3 * C::kStage;
+      stage_rows<D>(S, H, g, t);
+      __syncwarp();
+      for (int e = lane; e < 8 * D * D; e += 32) {
+        const int hh = e / (D * D), i = (e / D) % D, jj = e % D;
+        const int h2 = hb * 8 + hh;
+        if (row_ok && h2 < nh) {
+          const float v = 0.5f * fmaf(S[hh * C::SS + i], S[(hh + 8) * C::SS + jj],
+                                      S[(hh + 8) * C::SS + i] * S[hh * C::SS + jj]);
+          bad |= unstable(v);
+          stf(gQf_out + ((n * nh + h2) * D + i) * D + jj, v);
+        }
+      }
+    }
+    // Per-head outputs.
+    float glgA_sum = glgA;
+    glgA_sum += __shfl_xor_sync(0xffffffffu, glgA_sum, 1);
+    glgA_sum += __shfl_xor_sync(0xffffffffu, glgA_sum, 2);
+    if (valid) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          const int e = 8 * j + 2 * t + s;
+          bad |= unstable(gA[j][s]) | unstable(glgQ[j][s]) | unstable(gR[j][s]) | unstable(glgB[j][s]);
+          stf(gA_out + p * D + e, gA[j][s]);
+          stf(glgQ_out + p * D + e, glgQ[j][s]);
+          stf(gR_out + p * D + e, gR[j][s]);
+          stf(glgB_out + p * D + e, glgB[j][s]);
+        }
+      }
+      if (t == 0) {
+        bad |= unstable(glgA_sum);
+        stf(glgA_out + p, glgA_sum);
+      }
+    }
+    if constexpr (C::kOwn) {
+      // The row's warps add their partial sums in warp order (staging area reused).
+      static_assert(!C::kOwn || 2 * D * D <= C::kWarp, "reduction area");
+      __syncthreads();
+#pragma unroll
+      for (int q = 0; q < UPW; ++q) {
+        const bool isq = q >= MT;
+        const int mi = isq ? q - MT : q;
+        float* red = stg + (isq ? D * D : 0);
+#pragma unroll
+        for (int nj = 0; nj < NT; ++nj) {
+          const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
+          *reinterpret_cast<float2*>(red + r0 * D + c0) = make_float2(acc[q][nj][0], acc[q][nj][1]);
+          *reinterpret_cast<float2*>(red + (r0 + 8) * D + c0) = make_float2(acc[q][nj][2], acc[q][nj][3]);
+        }
+      }
+      __syncthreads();
+      for (int r = 0; r < rows_per_cta; ++r) {
+        const int64_t nr = n0 + r;
+        if (nr >= N) break;
+        for (int e = tid; e < 2 * D * D; e += nthreads) {
+          float v = 0.f;
+          for (int w = 0; w < wpr; ++w) v += warp_s[(size_t)(r * wpr + w) * C::kWarp + e];
+          if (e >= D * D) v *= 0.5f;
+          bad |= unstable(v);
+          stf((e < D * D ? gB_out : gQ_out) + nr * (D * D) + (e % (D * D)), v);
+        }
+      }
+    } else if (row_ok) {
+      // Each unit holds the sum over all the row's heads.
+#pragma unroll
+      for (int q = 0; q < UPW; ++q) {
+        const int unit = hb + q * wpr;
+        if (unit < C::kUnits) {
+          const bool isq = unit >= MT;
+          const int mi = isq ? unit - MT : unit;
+          const float sc = isq ? 0.5f : 1.0f;
+          TIn* out = (isq ? gQ_out : gB_out) + n * (D * D);
+#pragma unroll
+          for (int nj = 0; nj < NT; ++nj) {
+            const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
+            const float v[4] = {sc * acc[q][nj][0], sc * acc[q][nj][1], sc * acc[q][nj][2], sc * acc[q][nj][3]};
+            bad |= unstable(v[0]) | unstable(v[1]) | unstable(v[2]) | unstable(v[3]);
+            stf(out + r0 * D + c0, v[0]);
+            stf(out + r0 * D + c0 + 1, v[1]);
+            stf(out + (r0 + 8) * D + c0, v[2]);
+            stf(out + (r0 + 8) * D + c0 + 1, v[3]);
+          }
+        }
+      }
+    }
+    __syncthreads();  // the next row group reuses the shared operands and staging
   }
   if (bad) atomicOr(status, TTC_STATUS_BWD_UNSTABLE);
 }

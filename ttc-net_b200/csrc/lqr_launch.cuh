@@ -29,16 +29,33 @@ inline int groups_for(int nh, int d) {
   return g < 1 ? 1 : g;
 }
 
+// Q_f given as the layer's rank-rQ mixture instead of [N, nh, d, d]: the Q_f argument then
+// holds coeff_Qf [N*nh, rQ] and `basis` [rQ, d, d] (activation dtype); the backward writes
+// grad_coeff [N*nh, rQ] in place of grad_Q_f and per-warp partial sums of the basis
+// gradient (`grad_basis_partial`, slices x [rQ, d, d] fp32).
+struct QMix {
+  const void* basis = nullptr;
+  int rank = 0;
+  void* grad_coeff = nullptr;
+  float* grad_basis_partial = nullptr;
+};
+
 template <int D, int DU, typename TIn>
 int launch_fwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N, int nh,
-               int T, void* u, float* lam0, float* M, int* status, cudaStream_t st);
+               int T, void* u, float* lam0, float* M, int* status, const QMix& mix, cudaStream_t st);
 
 template <int D, int DU, typename TIn>
 int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
                const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
-               int* status, cudaStream_t st);
+               int* status, const QMix& mix, cudaStream_t st);
+
+// Partial slices (one per CTA) the mixed-Q_f backward writes for (N, nh) on the current
+// device; 0 when the mixed path is not available for the shape and rank, -TTC_ERR_CUDA on
+// a CUDA error.
+template <int D, int DU, typename TIn>
+int64_t bwd_mix_slices(int64_t N, int nh, int rQ);
 
 #ifdef TTC_DEFINE_LAUNCHERS
 constexpr size_t kMaxSmem = 227 * 1024;
@@ -77,61 +94,120 @@ int set_smem(Kern k, size_t bytes) {
 template <int D, int DU, typename TIn, bool SAVE_M>
 int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                   const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N,
-                  int nh, int T, void* u, float* lam0, float* M, int* status, cudaStream_t st) {
+                  int nh, int T, void* u, float* lam0, float* M, int* status, const QMix& mix,
+                  cudaStream_t st) {
   using CF = TcCfg<D, DU>;
-  const int slots = tc_slots<D, DU, SAVE_M>(nh);
+  using L = TcFwdLayout<D, DU, SAVE_M>;
+  int slots = tc_slots<D, DU, SAVE_M>(nh);
+  const size_t extra = mix.basis != nullptr ? L::basis_bytes(mix.rank) : 0;
+  while (slots > 1 && L::bytes(slots) + extra > kMaxSmem) --slots;
+  if (L::bytes(slots) + extra > kMaxSmem)
+    return set_error(TTC_ERR_UNSUPPORTED, "the Q_f basis does not fit in shared memory");
   const uint32_t cols = tmem_cols_for(slots * CF::kSlotCols);
-  const size_t smem = TcFwdLayout<D, DU, SAVE_M>::bytes(slots);
+  const size_t smem = L::bytes(slots) + extra;
   auto k = ttc::lqr_fwd_tc_kernel<D, DU, TIn, SAVE_M>;
   if (int rc = set_smem(k, smem)) return rc;
   k<<<dim3((unsigned)N), dim3(slots * 128), smem, st>>>(
-      (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf, (const TIn*)lA,
-      (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0, nh, T, cols, (TIn*)u, lam0, M, status);
+      (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf,
+      (const TIn*)mix.basis, mix.rank, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0,
+      nh, T, cols, (TIn*)u, lam0, M, status);
   return cuda_check(cudaGetLastError(), "lqr_fwd_tc_kernel launch");
 }
 
 template <int D, int DU, typename TIn>
 int launch_fwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N, int nh,
-               int T, void* u, float* lam0, float* M, int* status, cudaStream_t st) {
+               int T, void* u, float* lam0, float* M, int* status, const QMix& mix, cudaStream_t st) {
   if (M != nullptr)
     return launch_fwd_tc<D, DU, TIn, true>(A, B, Q, R, Qf, lA, lB, lQ, h0, N, nh, T, u, lam0, M,
-                                           status, st);
+                                           status, mix, st);
   return launch_fwd_tc<D, DU, TIn, false>(A, B, Q, R, Qf, lA, lB, lQ, h0, N, nh, T, u, lam0,
-                                          nullptr, status, st);
+                                          nullptr, status, mix, st);
 }
 
 // Saved-state backward on the warp-MMA adjoint: R rows x ceil(nh / 8) warps per CTA.
 template <int D, typename TIn, bool FROM_M>
+auto bwd_mma_kernel_for(int nh) {
+  using C = AdjMma<D>;
+  constexpr int kU = C::kOwn ? C::kUnits : 1;
+  return C::units_per_warp(nh) == kU ? ttc::lqr_bwd_mma_kernel<D, TIn, FROM_M, kU>
+                                     : ttc::lqr_bwd_mma_kernel<D, TIn, FROM_M, 2>;
+}
+
+// Grid of the warp-MMA backward: one CTA per row group, or, with a mixed Q_f (whose basis
+// gradient is accumulated per warp over all the groups a CTA walks), at most one wave of
+// resident CTAs.  Returns 0 on a CUDA error (recorded).
+template <int D, typename TIn, bool FROM_M>
+int64_t bwd_mma_grid(int64_t N, int nh, bool mix) {
+  using C = AdjMma<D>;
+  const int64_t groups = (N + C::rows_per_cta(nh) - 1) / C::rows_per_cta(nh);
+  if (!mix) return groups;
+  auto k = bwd_mma_kernel_for<D, TIn, FROM_M>(nh);
+  const size_t smem = C::bytes(nh);
+  if (set_smem(k, smem)) return 0;
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cuda_check(cudaGetDevice(&dev), "cudaGetDevice") ||
+      cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute") ||
+      cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 32 * C::warps(nh), smem),
+                 "cudaOccupancyMaxActiveBlocksPerMultiprocessor"))
+    return 0;
+  const int64_t wave = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
+  return groups < wave ? groups : wave;
+}
+
+template <int D, typename TIn, bool FROM_M>
 int launch_bwd_mma(const void* A, const void* B, const void* Q, const void* R, const void* lA,
                    const void* lB, const void* lQ, const void* h0, const float* lam0,
                    const float* M_or_dp, const void* dU, int64_t N, int nh, int T, void* const* g,
-                   int* status, cudaStream_t st) {
+                   int* status, const QMix& mix, const void* coeff_Qf, cudaStream_t st) {
   using C = AdjMma<D>;
   const int rpc = C::rows_per_cta(nh);
   const size_t smem = C::bytes(nh);
-  constexpr int kU = C::kOwn ? C::kUnits : 1;
-  auto k = C::units_per_warp(nh) == kU ? ttc::lqr_bwd_mma_kernel<D, TIn, FROM_M, kU>
-                                       : ttc::lqr_bwd_mma_kernel<D, TIn, FROM_M, 2>;
+  auto k = bwd_mma_kernel_for<D, TIn, FROM_M>(nh);
   if (int rc = set_smem(k, smem)) return rc;
-  const int64_t grid = (N + rpc - 1) / rpc;
+  const int64_t grid = bwd_mma_grid<D, TIn, FROM_M>(N, nh, mix.basis != nullptr);
+  if (grid == 0) return TTC_ERR_CUDA;
   k<<<dim3((unsigned)grid), dim3(32 * C::warps(nh)), smem, st>>>(
       (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)lA, (const TIn*)lB,
       (const TIn*)lQ, (const TIn*)h0, lam0, M_or_dp, (const TIn*)dU, N, nh, T, rpc, (TIn*)g[0],
       (TIn*)g[1], (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6], (TIn*)g[7],
-      (TIn*)g[8], status);
+      (TIn*)g[8], (const TIn*)mix.basis, mix.rank, (const TIn*)coeff_Qf, (TIn*)mix.grad_coeff,
+      mix.grad_basis_partial, status);
   return cuda_check(cudaGetLastError(), "lqr_bwd_mma_kernel launch");
+}
+
+template <int D, int DU, typename TIn>
+int64_t bwd_mix_slices(int64_t N, int nh, int rQ) {
+  if constexpr (D == DU && D <= TTC_ADJ_MMA_MAXD) {
+    if (!AdjMma<D>::fits(nh)) return 0;
+    // the backward stages each warp's [8][rQ] coefficients in one staging buffer
+    if (8 * rQ > 3 * AdjMma<D>::kStage) return 0;
+    // the forward keeps the basis in shared memory next to one tile slot at least
+    if (TcFwdLayout<D, DU, true>::bytes(1) + TcFwdLayout<D, DU, true>::basis_bytes(rQ) > kMaxSmem) return 0;
+    const int64_t grid = bwd_mma_grid<D, TIn, true>(N, nh, true);
+    if (grid == 0) return -TTC_ERR_CUDA;
+    return grid;
+  } else {
+    (void)N;
+    (void)nh;
+    (void)rQ;
+    return 0;
+  }
 }
 
 template <int D, int DU, typename TIn>
 int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
                const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
-               int* status, cudaStream_t st) {
+               int* status, const QMix& mix, cudaStream_t st) {
   if constexpr (D == DU && D <= TTC_ADJ_MMA_MAXD) {
     if (M != nullptr && AdjMma<D>::fits(nh))
-      return launch_bwd_mma<D, TIn, true>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status, st);
+      return launch_bwd_mma<D, TIn, true>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status,
+                                          mix, Qf, st);
   }
+  if (mix.basis != nullptr)
+    return set_error(TTC_ERR_UNSUPPORTED,
+                     "a mixed Q_f needs the saved-state warp-MMA backward (d = du <= 32, <= 64 heads, M saved)");
   if (M != nullptr) {
     // The forward saved lambda0 and M: adjoint only, on the CUDA cores.
     const int G = groups_for(nh, D);
@@ -169,9 +245,10 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
   template int ttc::launch_fwd<D, DU, TIn>(const void*, const void*, const void*, const void*, \
                                            const void*, const void*, const void*, const void*, \
                                            const void*, int64_t, int, int, void*, float*,      \
-                                           float*, int*, cudaStream_t);                        \
+                                           float*, int*, const ttc::QMix&, cudaStream_t);      \
   template int ttc::launch_bwd<D, DU, TIn>(const void*, const void*, const void*, const void*, \
                                            const void*, const void*, const void*, const void*, \
                                            const void*, const float*, const float*,            \
                                            const void*, int64_t, int, int, void* const*, int*, \
-                                           cudaStream_t);
+                                           const ttc::QMix&, cudaStream_t);                    \
+  template int64_t ttc::bwd_mix_slices<D, DU, TIn>(int64_t, int, int);

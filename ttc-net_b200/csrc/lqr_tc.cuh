@@ -58,6 +58,10 @@ struct TcFwdLayout {
   static size_t bytes(int slots) {
     return sizeof(float) * (size_t)(C::kOps + C::kHeader + slots * C::kHeadsPerTile * kGroup);
   }
+  // A mixed Q_f keeps its rank-rQ basis in shared memory behind the groups, rows padded to
+  // D + 1 floats (conflict-free row reads by the D threads of a head).
+  __host__ __device__ static int basis_offset(int slots) { return C::kOps + C::kHeader + slots * C::kHeadsPerTile * kGroup; }
+  static size_t basis_bytes(int rQ) { return sizeof(float) * (size_t)rQ * D * (D + 1); }
 };
 
 // OR of `pred` over the `count` threads of named barrier `id` (also a barrier).
@@ -302,11 +306,54 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
   return true;
 }
 
+// This thread's row i of the terminal cost Q_f of problem p: read from Q_f [N*nh, D, D], or,
+// when `basis_s` is given, mixed from the rank-rQ basis as the layer does
+// (Q_f = sum_r coeff_Qf[r] basis[r], ttc_layer.py:119-123): `qf` is then coeff_Qf [N*nh, rQ],
+// basis_s the basis in shared memory (rows padded to D + 1), and the sum is rounded to the
+// activation dtype like the einsum it replaces.
+template <int D, typename TIn>
+__device__ __forceinline__ void load_qf_row(float (&y2)[D], bool valid, const TIn* __restrict__ qf,
+                                            const float* basis_s, int rQ, int64_t p, int i) {
+  if (!valid) {
+#pragma unroll
+    for (int k = 0; k < D; ++k) y2[k] = 0.0f;
+    return;
+  }
+  if (basis_s == nullptr) {
+    const TIn* row = qf + (p * D + i) * D;
+#pragma unroll
+    for (int k = 0; k < D; ++k) y2[k] = ldf(row + k);
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < D; ++k) y2[k] = 0.0f;
+  const TIn* c = qf + p * rQ;
+  for (int r = 0; r < rQ; ++r) {
+    const float cr = ldf(c + r);
+    const float* row = basis_s + (r * D + i) * (D + 1);
+#pragma unroll
+    for (int k = 0; k < D; ++k) y2[k] = fmaf(cr, row[k], y2[k]);
+  }
+  if constexpr (sizeof(TIn) == 2) {
+#pragma unroll
+    for (int k = 0; k < D; ++k) y2[k] = __bfloat162float(__float2bfloat16_rn(y2[k]));
+  }
+}
+
+// Cooperative copy of a rank-rQ basis [rQ, D, D] (activation dtype) into shared memory as
+// fp32 rows of D + 1.
+template <int D, typename TIn>
+__device__ __forceinline__ void stage_basis(float* basis_s, const TIn* __restrict__ basis, int rQ, int tid,
+                                            int nthreads) {
+  for (int e = tid; e < rQ * D * D; e += nthreads) basis_s[(e / D) * (D + 1) + e % D] = ldf(basis + e);
+}
+
 template <int D, int DU, typename TIn, bool SAVE_M>
 __global__ void __launch_bounds__(TcLaunch<D>::kMaxThreads, TcLaunch<D>::kMinBlocks)
 lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                   const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
-                  const TIn* __restrict__ Qf, const TIn* __restrict__ lgA,
+                  const TIn* __restrict__ Qf, const TIn* __restrict__ Qbasis, int rQ,
+                  const TIn* __restrict__ lgA,
                   const TIn* __restrict__ lgB, const TIn* __restrict__ lgQ,
                   const TIn* __restrict__ H0, int nh, int T, uint32_t tmem_cols,
                   TIn* __restrict__ u_out, float* __restrict__ lam0_out, float* __restrict__ M_out,
@@ -319,6 +366,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   uint64_t* mbars = reinterpret_cast<uint64_t*>(smem + CF::kOps);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + CF::kOps + 16);
   float* groups = smem + CF::kOps + CF::kHeader;
+  float* basis_s = Qbasis != nullptr ? smem + L::basis_offset(blockDim.x / 128) : nullptr;
 
   const int tid = threadIdx.x;
   const int nslots = blockDim.x / 128;
@@ -348,6 +396,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     for (int s = 0; s < nslots; ++s) tc::mbar_init(&mbars[s], 1);
     tc::mbar_init_fence();
   }
+  if (basis_s != nullptr) stage_basis<D, TIn>(basis_s, Qbasis, rQ, tid, blockDim.x);
   if (tid < 32) tc::tmem_alloc(tmem_base_s, tmem_cols);
   tc::fence_smem_to_async();
   tc::fence_before_sync();
@@ -397,12 +446,9 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     }
     sh0[i] = h0;
     float y1[D], y2[D];
-    const TIn* qf = Qf + (p * D + i) * D;
 #pragma unroll
-    for (int k = 0; k < D; ++k) {
-      y1[k] = (k == i) ? 1.0f : 0.0f;
-      y2[k] = valid ? ldf(qf + k) : 0.0f;
-    }
+    for (int k = 0; k < D; ++k) y1[k] = (k == i) ? 1.0f : 0.0f;
+    load_qf_row<D, TIn>(y2, valid, Qf, basis_s, rQ, p, i);
     Y3Discard y3;  // M is formed from P below instead of from Y3
     const bool swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T);
     // Uniform over the slot: a late timeout on the last product surfaces here too.

@@ -59,7 +59,7 @@ int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_FWD(DD, DDU, TT)                                                                 \
   return ttc::launch_fwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,        \
-                                 log_gamma_Q, h0, N, nh, T, u, lam0, M, status, st)
+                                 log_gamma_Q, h0, N, nh, T, u, lam0, M, status, ttc::QMix{}, st)
   if (dtype == TTC_DTYPE_F32) {
     if (d == 16) TTC_FWD(16, 16, float);
     if (d == 32) TTC_FWD(32, 32, float);
@@ -94,7 +94,100 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_BWD(DD, DDU, TT)                                                                  \
   return ttc::launch_bwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,         \
-                                 log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, st)
+                                 log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, ttc::QMix{}, st)
+  if (dtype == TTC_DTYPE_F32) {
+    if (d == 16) TTC_BWD(16, 16, float);
+    if (d == 32) TTC_BWD(32, 32, float);
+    TTC_BWD(64, 64, float);
+  } else {
+    if (d == 16) TTC_BWD(16, 16, __nv_bfloat16);
+    if (d == 32) TTC_BWD(32, 32, __nv_bfloat16);
+    TTC_BWD(64, 64, __nv_bfloat16);
+  }
+#undef TTC_BWD
+}
+
+int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                    const void* coeff_Qf, const void* Q_basis, int rQ, const void* log_gamma_A,
+                    const void* log_gamma_B, const void* log_gamma_Q, const void* h0, int64_t N, int nh,
+                    int d, int du, int T, int dtype, void* u, float* lam0, float* M, int* status,
+                    void* stream) {
+  if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (rQ < 1) return fail(TTC_ERR_INVALID, "rank of the Q_f mixture must be >= 1");
+  if (N == 0) return TTC_OK;
+  if (!A_diag || !B || !Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A || !log_gamma_B ||
+      !log_gamma_Q || !h0 || !u || !status)
+    return fail(TTC_ERR_INVALID, "null pointer argument");
+  ttc::QMix mix;
+  mix.basis = Q_basis;
+  mix.rank = rQ;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define TTC_FWD(DD, DDU, TT)                                                                 \
+  return ttc::launch_fwd<DD, DDU, TT>(A_diag, B, Q, R_inv, coeff_Qf, log_gamma_A, log_gamma_B,   \
+                                 log_gamma_Q, h0, N, nh, T, u, lam0, M, status, mix, st)
+  if (dtype == TTC_DTYPE_F32) {
+    if (d == 16) TTC_FWD(16, 16, float);
+    if (d == 32) TTC_FWD(32, 32, float);
+    TTC_FWD(64, 64, float);
+  } else {
+    if (d == 16) TTC_FWD(16, 16, __nv_bfloat16);
+    if (d == 32) TTC_FWD(32, 32, __nv_bfloat16);
+    TTC_FWD(64, 64, __nv_bfloat16);
+  }
+#undef TTC_FWD
+}
+
+int64_t ttc_lqr_bwd_mix_slices(int64_t N, int nh, int d, int du, int rQ, int dtype) {
+  if (int rc = check_common(N, nh, d, du, 1, dtype)) return -rc;
+  if (N == 0 || rQ < 1) return 0;
+#define TTC_SL(DD, TT) return ttc::bwd_mix_slices<DD, DD, TT>(N, nh, rQ)
+  if (dtype == TTC_DTYPE_F32) {
+    if (d == 16) TTC_SL(16, float);
+    if (d == 32) TTC_SL(32, float);
+    TTC_SL(64, float);
+  } else {
+    if (d == 16) TTC_SL(16, __nv_bfloat16);
+    if (d == 32) TTC_SL(32, __nv_bfloat16);
+    TTC_SL(64, __nv_bfloat16);
+  }
+#undef TTC_SL
+}
+
+int ttc_lqr_bwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                    const void* coeff_Qf, const void* Q_basis, int rQ, const void* log_gamma_A,
+                    const void* log_gamma_B, const void* log_gamma_Q, const void* h0, const float* lam0,
+                    const float* M, const void* d_u, int64_t N, int nh, int d, int du, int T, int dtype,
+                    void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_coeff_Qf,
+                    float* grad_basis_partial, int64_t slices, void* grad_lgA, void* grad_lgB,
+                    void* grad_lgQ, void* grad_h0, int* status, void* stream) {
+  if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (rQ < 1) return fail(TTC_ERR_INVALID, "rank of the Q_f mixture must be >= 1");
+  if (N == 0) return TTC_OK;
+  if (!A_diag || !B || !Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A || !log_gamma_B ||
+      !log_gamma_Q || !h0 || !d_u || !status || !lam0 || !M || !grad_basis_partial)
+    return fail(TTC_ERR_INVALID, "null pointer argument (the mixed-Q_f backward needs lam0 and M)");
+  void* g[9] = {grad_A, grad_B, grad_Q, grad_R_inv, nullptr, grad_lgA, grad_lgB, grad_lgQ, grad_h0};
+  for (int i = 0; i < 9; ++i)
+    if (i != 4 && !g[i]) return fail(TTC_ERR_INVALID, "null gradient pointer");
+  if (!grad_coeff_Qf) return fail(TTC_ERR_INVALID, "null gradient pointer");
+  const int64_t need = ttc_lqr_bwd_mix_slices(N, nh, d, du, rQ, dtype);
+  if (need < 0) return static_cast<int>(-need);
+  if (need == 0) return fail(TTC_ERR_UNSUPPORTED, "no mixed-Q_f backward for this shape");
+  if (slices != need) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "grad_basis_partial has %lld slices, this launch needs %lld",
+             (long long)slices, (long long)need);
+    return fail(TTC_ERR_INVALID, buf);
+  }
+  ttc::QMix mix;
+  mix.basis = Q_basis;
+  mix.rank = rQ;
+  mix.grad_coeff = grad_coeff_Qf;
+  mix.grad_basis_partial = grad_basis_partial;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define TTC_BWD(DD, DDU, TT)                                                                  \
+  return ttc::launch_bwd<DD, DDU, TT>(A_diag, B, Q, R_inv, coeff_Qf, log_gamma_A, log_gamma_B,    \
+                                 log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, mix, st)
   if (dtype == TTC_DTYPE_F32) {
     if (d == 16) TTC_BWD(16, 16, float);
     if (d == 32) TTC_BWD(32, 32, float);

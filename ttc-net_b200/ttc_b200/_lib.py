@@ -10,7 +10,7 @@ import os
 import threading
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libttc_b200.so")
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -36,6 +36,10 @@ SIGNATURES = {
     "ttc_last_error": (ctypes.c_char_p, []),
     "ttc_lqr_fwd": (_I, [_P] * 9 + [_I64, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
     "ttc_lqr_bwd": (_I, [_P] * 9 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I] + [_P] * 9 + [_P, _P]),
+    "ttc_lqr_fwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_I64, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
+    "ttc_lqr_bwd_mix_slices": (_I64, [_I64, _I, _I, _I, _I, _I]),
+    "ttc_lqr_bwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I]
+                        + [_P] * 5 + [_FP, _I64] + [_P] * 4 + [_P, _P]),
     "ttc_prologue_fwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P]),
     "ttc_prologue_bwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P, _P]),
 }

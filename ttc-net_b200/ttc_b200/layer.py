@@ -3,9 +3,11 @@
 and initialisation, so a reference ``state_dict`` loads 1:1.
 
 The prologue's elementwise part (split, l2norm / softplus / clamp, ttc_layer.py:106-133)
-runs as one CUDA kernel each way (``prologue.py``); in_proj, the low-rank B / Q / Q_f
-mixtures and the epilogue (l2norm, out_proj, :142-150) are PyTorch / cuBLAS ops on the GPU;
-the LQR solve runs in libttc_b200.so through ``LQR_SOLVER_IMPL_MAP``.
+runs as one CUDA kernel each way (``prologue.py``); the per-head Q_f mixture (:119-123) is
+done inside the solver kernels when the saved-state backward applies (``mix_available``),
+so no [N, nh, d, d] Q_f or grad_Q_f tensor exists; in_proj, the low-rank B / Q mixtures and
+the epilogue (l2norm, out_proj, :142-150) are PyTorch / cuBLAS ops on the GPU; the LQR solve
+runs in libttc_b200.so through ``LQR_SOLVER_IMPL_MAP``.
 """
 from __future__ import annotations
 
@@ -16,7 +18,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .prologue import prologue
-from .solver import LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_with_status
+from .solver import (LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_mix_with_status,
+                     lqr_solve_with_status, mix_available)
 from . import _lib
 
 
@@ -75,27 +78,40 @@ class TTCLayer(nn.Module):
                 else:
                     module.bias_gamma.data.fill_(0.0)
 
-    def solver_inputs(self, x2d: torch.Tensor):
-        """Prologue (ttc_layer.py:104-135): rows [N, in_dim] -> the nine solver inputs.  The
-        elementwise part (split, l2norm, softplus, clamp, negation) is one CUDA kernel each way
-        (``prologue``); the low-rank B / Q / Q_f mixtures are cuBLAS einsums."""
+    def mixed_inputs(self, x2d: torch.Tensor):
+        """Prologue (ttc_layer.py:104-135) up to, not including, the Q_f mixture: rows
+        [N, in_dim] -> (A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0) with
+        Q_f = sum_r coeff_Qf[..., r] Q_basis[r].  The elementwise part (split, l2norm,
+        softplus, clamp, negation) is one CUDA kernel each way (``prologue``); the low-rank
+        B / Q mixtures are cuBLAS einsums."""
         nh, d, du = self.num_heads, self.h_dim, self.u_dim
         A_diag, R_inv_diag, coeff_Qf, log_gamma_A, log_gamma_B, log_gamma_Q, h0, coeff_B, coeff_Q = \
             prologue(self.in_proj(x2d), nh, d, du, self.b_rank, self.q_rank)
         B = torch.einsum("...r,rmn->...mn", coeff_B, self.Bs)
         if self.q_reparam == "plain":
             Q = torch.einsum("...r,rmn->...mn", coeff_Q, self.Qs)
-            Q_f = torch.einsum("...r,rmn->...mn", coeff_Qf, self.Qs)
+            Q_basis = self.Qs
         else:
             Q = torch.einsum("...r,rmn,rkn->...mk", coeff_Q, self.Qs, self.Qs) / math.sqrt(d)
-            Q_f = torch.einsum("...r,rmn,rkn->...mk", coeff_Qf, self.Qs, self.Qs) / math.sqrt(d)
+            Q_basis = torch.einsum("rmn,rkn->rmk", self.Qs, self.Qs) / math.sqrt(d)
         if self.bias_gamma is not None:
             # log_gammas = -softplus(.) - relu(-bias_gamma), split as [1, du, d] (:129-133)
             bg = F.relu(-self.bias_gamma)
             log_gamma_A = log_gamma_A - bg[0]
             log_gamma_B = log_gamma_B - bg[1:1 + du]
             log_gamma_Q = log_gamma_Q - bg[1 + du:]
-        return (A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0)
+        return (A_diag, B, Q, R_inv_diag, coeff_Qf, Q_basis, log_gamma_A, log_gamma_B, log_gamma_Q, h0)
+
+    @staticmethod
+    def _materialise(parts):
+        A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0 = parts
+        Q_f = torch.einsum("...r,rmn->...mn", coeff_Qf, Q_basis)
+        return (A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0)
+
+    def solver_inputs(self, x2d: torch.Tensor):
+        """The nine inputs of the reference solver signature (ttc_layer.py:137), Q_f
+        materialised as [N, nh, d, d]."""
+        return self._materialise(self.mixed_inputs(x2d))
 
     def forward(self, h0: torch.Tensor, T: int) -> torch.Tensor:
         """y = layer(x, T).  x is [bs, seq, in_dim] as in the reference; a 4-D
@@ -107,19 +123,24 @@ class TTCLayer(nn.Module):
         if T == 0:
             return torch.zeros(h0.shape[0], h0.shape[1], self.out_dim, device=h0.device, dtype=h0.dtype)
         bs, seq_len, in_dim = h0.shape
-        args = self.solver_inputs(h0.reshape(-1, in_dim))
+        parts = self.mixed_inputs(h0.reshape(-1, in_dim))
         if self.solver is cuda_lqr_solve:
-            u, status = lqr_solve_with_status(*args, T)
+            N, nh, d = parts[0].shape
+            if mix_available(N, nh, d, self.u_dim, parts[5].shape[0], parts[2].dtype):
+                # Q_f mixed inside the kernels: no [N, nh, d, d] tensor either way.
+                u, status = lqr_solve_mix_with_status(*parts, T)
+            else:
+                u, status = lqr_solve_with_status(*self._materialise(parts), T)
             if status & _lib.STATUS_U_NAN:
                 raise RuntimeError(U_NAN_MSG)
         else:
-            u = self.solver(*args, T)
+            u = self.solver(*self._materialise(parts), T)
             if torch.isnan(u).any():
                 raise RuntimeError(U_NAN_MSG)
         if self.rescale == "l2_norm":
             u = l2norm(u)
         elif self.rescale == "h0_norm":
-            x0 = args[-1]
+            x0 = parts[-1]
             h0_norm = torch.linalg.norm(x0, dim=-1, ord=2).detach()
             u_norm = torch.linalg.norm(u, dim=-1, ord=2).detach()
             u = u / u_norm[..., None] * h0_norm[..., None]

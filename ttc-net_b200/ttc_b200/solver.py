@@ -161,6 +161,98 @@ class LQRSolveFunction(torch.autograd.Function):
         return (*grads, None, None)
 
 
+def mix_available(N: int, nh: int, d: int, du: int, rQ: int, dtype, save_budget: int | None = None) -> bool:
+    """Whether the solve can take Q_f as the layer's rank-r mixture (ttc_lqr_fwd_mix /
+    ttc_lqr_bwd_mix): needs the saved-state warp-MMA backward, i.e. M within the budget and a
+    supported shape.  Queries the current CUDA device."""
+    budget = SAVE_BUDGET_BYTES if save_budget is None else int(save_budget)
+    if dtype not in _DTYPES or N == 0 or N * nh * d * du * 4 > budget:
+        return False
+    return _lib.load().ttc_lqr_bwd_mix_slices(N, nh, d, du, rQ, _DTYPES[dtype]) > 0
+
+
+class LQRSolveMixFunction(torch.autograd.Function):
+    """LQRSolveFunction with Q_f = sum_r coeff_Qf[..., r] Q_basis[r] never materialised
+    (ttc_layer.py:119-123 fused into the solve): the forward mixes each head's Q_f rows in the
+    kernel, the backward returns grad_coeff_Qf and grad_Q_basis instead of grad_Q_f.  Always
+    saves M (callers check ``mix_available`` first)."""
+
+    @staticmethod
+    def forward(ctx, A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0, T):
+        T = int(T)
+        N, nh, d = A_diag.shape
+        du = B.shape[-1]
+        rQ = Q_basis.shape[0]
+        assert coeff_Qf.shape == (N, nh, rQ), f"coeff_Qf must be [{N},{nh},{rQ}]"
+        assert Q_basis.shape == (rQ, d, d), f"Q_basis must be [{rQ},{d},{d}]"
+        dtype = Q.dtype
+        if dtype not in _DTYPES:
+            raise TypeError(f"ttc_b200 'cuda' solver supports float32 and bfloat16, got {dtype}")
+        args = _prepare((A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0), dtype)
+        dev = Q.device
+        lib = _lib.load()
+        u = torch.empty(N, nh, du, device=dev, dtype=dtype)
+        lam0 = torch.empty(N, nh, d, device=dev, dtype=torch.float32)
+        M = torch.empty(N, nh, d, du, device=dev, dtype=torch.float32)
+        status = torch.zeros(1, device=dev, dtype=torch.int32)
+        A_c, B_c, Q_c, R_c, cQf_c, Qb_c, lA_c, lB_c, lQ_c, h0_c = args
+        with torch.cuda.device(dev), torch.profiler.record_function("fwd:ttc_lqr_fwd_mix"):
+            _launch("ttc_lqr_fwd", dev, lib.ttc_lqr_fwd_mix, _ptr(A_c), _ptr(B_c), _ptr(Q_c), _ptr(R_c),
+                    _ptr(cQf_c), _ptr(Qb_c), rQ, _ptr(lA_c), _ptr(lB_c), _ptr(lQ_c), _ptr(h0_c), N, nh, d,
+                    du, T, _DTYPES[dtype], _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
+        st = int(status.item())
+        if st & _lib.STATUS_FWD_UNSTABLE:
+            raise RuntimeError(FWD_UNSTABLE_MSG)
+        if st & _lib.STATUS_LU_UNSTABLE:
+            raise RuntimeError(LU_UNSTABLE_MSG)
+        ctx.save_for_backward(*args, lam0, M)
+        ctx.dims = (N, nh, d, du, rQ, T)
+        ctx.dtype = dtype
+        ctx.in_dtypes = [t.dtype for t in (A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0)]
+        status_cpu = torch.tensor([st], dtype=torch.int32)
+        ctx.mark_non_differentiable(status_cpu)
+        return u, status_cpu
+
+    @staticmethod
+    def backward(ctx, d_u, _d_status):
+        A, B, Q, R, cQf, Qb, lA, lB, lQ, h0, lam0, M = ctx.saved_tensors
+        N, nh, d, du, rQ, T = ctx.dims
+        dtype = ctx.dtype
+        dev = Q.device
+        lib = _lib.load()
+        d_u = d_u.to(dtype).contiguous()
+        with torch.cuda.device(dev):
+            slices = int(lib.ttc_lqr_bwd_mix_slices(N, nh, d, du, rQ, _DTYPES[dtype]))
+        if slices <= 0:
+            _lib.check(-slices if slices < 0 else _lib.ERR_UNSUPPORTED)
+        gA, gB, gQ, gR = [torch.empty_like(t) for t in (A, B, Q, R)]
+        gcQf = torch.empty_like(cQf)
+        partial = torch.empty(slices, rQ, d, d, device=dev, dtype=torch.float32)
+        glA, glB, glQ, gh0 = [torch.empty_like(t) for t in (lA, lB, lQ, h0)]
+        status = torch.zeros(1, device=dev, dtype=torch.int32)
+        with torch.cuda.device(dev), torch.profiler.record_function("bwd:ttc_lqr_bwd_mix"):
+            _launch("ttc_lqr_bwd", dev, lib.ttc_lqr_bwd_mix,
+                    *[_ptr(t) for t in (A, B, Q, R, cQf, Qb)], rQ,
+                    *[_ptr(t) for t in (lA, lB, lQ, h0)], _ptr(lam0), _ptr(M), _ptr(d_u), N, nh, d, du,
+                    T, _DTYPES[dtype], _ptr(gA), _ptr(gB), _ptr(gQ), _ptr(gR), _ptr(gcQf), _ptr(partial),
+                    slices, _ptr(glA), _ptr(glB), _ptr(glQ), _ptr(gh0), _ptr(status))
+        if int(status.item()) & _lib.STATUS_BWD_UNSTABLE:
+            raise RuntimeError(BWD_UNSTABLE_MSG)
+        S = partial.sum(0)
+        gQb = 0.5 * (S + S.transpose(-1, -2))
+        grads = [gA, gB, gQ, gR, gcQf, gQb, glA, glB, glQ, gh0]
+        grads = [g.to(dt) for g, dt in zip(grads, ctx.in_dtypes)]
+        return (*grads, None)
+
+
+def lqr_solve_mix_with_status(A_diag, B, Q, R_inv_diag, coeff_Qf, Q_basis, log_gamma_A, log_gamma_B,
+                              log_gamma_Q, h0, T):
+    """The solve with Q_f given as a mixture (see LQRSolveMixFunction); returns (u, status)."""
+    u, status = LQRSolveMixFunction.apply(A_diag, B, Q, R_inv_diag, coeff_Qf, Q_basis, log_gamma_A,
+                                          log_gamma_B, log_gamma_Q, h0, T)
+    return u, int(status.item())
+
+
 def lqr_solve_with_status(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q,
                           h0, T, save_budget: int | None = None):
     """Like ``cuda_lqr_solve`` but also returns the forward's status bits (host int)."""
