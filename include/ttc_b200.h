@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define TTC_ABI_VERSION 3
+#define TTC_ABI_VERSION 4
 
 #define TTC_DTYPE_F32 0
 #define TTC_DTYPE_BF16 1
@@ -47,6 +47,10 @@ extern "C" {
 #define TTC_STATUS_BWD_UNSTABLE 4 /* any of the nine gradients    (ttc/solvers/fused_lqr.py:243-246) */
 #define TTC_STATUS_U_NAN 8        /* NaN in u                     (ttc/layers/ttc_layer.py:139-140)  */
 #define TTC_STATUS_MMA_TIMEOUT 16 /* a tensor-core MMA did not complete within the kernel's poll limit */
+
+/* Option bits (`flags` argument). */
+#define TTC_FLAG_INV_GUARD 1 /* Y1 + 1e-6 I after the sweep, before the solve: the reference's
+                                inv_guard (fused_lqr.py:26-27,95-96; symplectic_iter.py:302-305) */
 
 /* ABI version of the loaded library (== TTC_ABI_VERSION it was built with). */
 int ttc_abi_version(void);
@@ -66,6 +70,8 @@ const char* ttc_last_error(void);
  * Inputs (activation dtype): A_diag [N,nh,d], B [N,d,du], Q [N,d,d], R_inv [N,nh,du],
  *   Q_f [N,nh,d,d], log_gamma_A [N,nh], log_gamma_B [N,nh,du], log_gamma_Q [N,nh,d],
  *   h0 [N,nh,d]  -- the solver signature of ttc_layer.py:137.
+ * flags: TTC_FLAG_* bits (TTC_FLAG_INV_GUARD); the backward takes the same flags (they
+ *   matter to it only when it recomputes the sweep).
  * Outputs: u [N,nh,du] (activation dtype);
  *   lam0 [N,nh,d] float32 = P h0 (may be NULL);
  *   M [N,nh,d,du] float32 = Y1^-1 Y3, what the backward needs to form
@@ -75,7 +81,7 @@ const char* ttc_last_error(void);
 int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                 const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
                 const void* log_gamma_Q, const void* h0, int64_t N, int nh, int d, int du,
-                int T, int dtype, void* u, float* lam0, float* M, int* status,
+                int T, int dtype, int flags, void* u, float* lam0, float* M, int* status,
                 void* stream);
 
 /*
@@ -97,7 +103,7 @@ int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_
 int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                 const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
                 const void* log_gamma_Q, const void* h0, const float* lam0, const float* M,
-                const void* d_u, int64_t N, int nh, int d, int du, int T, int dtype,
+                const void* d_u, int64_t N, int nh, int d, int du, int T, int dtype, int flags,
                 void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_Q_f,
                 void* grad_lgA, void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status,
                 void* stream);
@@ -109,8 +115,8 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
 int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                     const void* coeff_Qf, const void* Q_basis, int rQ, const void* log_gamma_A,
                     const void* log_gamma_B, const void* log_gamma_Q, const void* h0, int64_t N, int nh,
-                    int d, int du, int T, int dtype, void* u, float* lam0, float* M, int* status,
-                    void* stream);
+                    int d, int du, int T, int dtype, int flags, void* u, float* lam0, float* M,
+                    int* status, void* stream);
 
 /* Number of grad_basis_partial slices ttc_lqr_bwd_mix writes for this shape on the current
  * device (it runs one wave of CTAs, each summing into its own slice); 0 if the mixed path is

@@ -245,7 +245,7 @@ def kkt_solve(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h
 # Fused (symplectic) solver restatement
 # ---------------------------------------------------------------------------
 def fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
-                  normalize_threshold: float = 1e3):
+                  normalize_threshold: float = 1e3, inv_guard: bool = False):
     """Symplectic Riccati sweep + LU solve + first-step decode (fused_lqr.py:18-146).
 
     Y1 = I, Y2 = Q_f (fused_lqr.py:50-52); for s = 0..T-1 with tau = T-s (A/B
@@ -257,6 +257,7 @@ def fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_
         normalisation NORMALIZE_TYPE=2: divide Y1, Y2 (and Y3 at the last step) by the
         largest row abs-sum of Y1 or Y2 when it exceeds 1e3          (:286-300)
     The oracle normalises the whole d x d block (the reference's BY = d tiling).
+    inv_guard adds 1e-6 I to the final Y1 (INV_GUARD, symplectic_iter.py:302-305).
     P = Y1^-1 Y2 (LU, :104-105); lambda0 = P h0; lambda1 = lambda0 / (1 + A_diag e^lgA);
     u = -R_inv * (B diag(e^lgB))^T lambda1 (symplectic_iter.py:437,472-517).
     Returns u, lam0, Y1, Y2, Y3, P (all in the working dtype).
@@ -289,6 +290,8 @@ def fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_
         Y2 = Y2 / sc
         if s == T - 1:
             Y3 = Y3 / sc
+    if inv_guard:
+        Y1 = Y1 + 1e-6 * torch.eye(d, dtype=dt)
     P = torch.linalg.solve(Y1, Y2)
     lam0 = (P @ h0[..., None])[..., 0]
     lam1 = lam0 / (1.0 + A_diag * torch.exp(log_gamma_A)[..., None])
@@ -375,8 +378,9 @@ class _FusedFunc(torch.autograd.Function):
     """Autograd wrapper of the fused restatement (fused_lqr.py:255-291)."""
 
     @staticmethod
-    def forward(ctx, A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T):
-        u, lam0, Y1, _, Y3, _ = fused_forward(A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T)
+    def forward(ctx, A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T, inv_guard=False):
+        u, lam0, Y1, _, Y3, _ = fused_forward(A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T,
+                                              inv_guard=inv_guard)
         ctx.save_for_backward(A_diag, B, Q, R_inv, lgA, lgB, lgQ, h0, lam0, Y1, Y3)
         ctx.T = T
         return u
@@ -385,12 +389,14 @@ class _FusedFunc(torch.autograd.Function):
     def backward(ctx, d_u):
         A_diag, B, Q, R_inv, lgA, lgB, lgQ, h0, lam0, Y1, Y3 = ctx.saved_tensors
         g = fused_backward(A_diag, B, Q, R_inv, lgA, lgB, lgQ, h0, lam0, Y1, Y3, d_u, ctx.T)
-        return (*g, None)
+        return (*g, None, None)
 
 
-def fused_solve(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T):
+def fused_solve(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
+                inv_guard: bool = False):
     """The reference "fused" solver semantics on the CPU (fused_lqr.py:294-304)."""
-    return _FusedFunc.apply(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T)
+    return _FusedFunc.apply(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
+                            inv_guard)
 
 
 SOLVERS = {"riccati": riccati_solve, "kkt": kkt_solve, "fused": fused_solve}

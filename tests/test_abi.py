@@ -51,9 +51,9 @@ def test_supported_shapes(lib):
     assert lib.ttc_supported(32, 16) == 0
 
 
-def _fwd(lib, N=1, nh=1, d=16, du=16, T=4, dtype=0, null_inputs=False):
+def _fwd(lib, N=1, nh=1, d=16, du=16, T=4, dtype=0, null_inputs=False, flags=0):
     p = None if null_inputs else 16  # never dereferenced: rejected before any launch
-    return lib.ttc_lqr_fwd(*([p] * 9), N, nh, d, du, T, dtype, p, p, None, p, None)
+    return lib.ttc_lqr_fwd(*([p] * 9), N, nh, d, du, T, dtype, flags, p, p, None, p, None)
 
 
 def test_fwd_rejects_bad_arguments_without_gpu(lib):
@@ -66,6 +66,8 @@ def test_fwd_rejects_bad_arguments_without_gpu(lib):
     assert _fwd(lib, d=24, du=24) == _lib.ERR_UNSUPPORTED
     assert b"h_dim=24" in lib.ttc_last_error()
     assert _fwd(lib, null_inputs=True) == _lib.ERR_INVALID
+    assert _fwd(lib, flags=6) == _lib.ERR_INVALID
+    assert b"flag" in lib.ttc_last_error()
     assert _fwd(lib, N=0) == _lib.OK  # empty batch: nothing to launch
 
 
@@ -77,7 +79,7 @@ def test_bwd_rejects_bad_arguments_without_gpu(lib):
     def bwd(Qf=P, lam0=P, M=P, grads=P, **kw):
         a = {**base, **kw}
         return lib.ttc_lqr_bwd(P, P, P, P, Qf, P, P, P, P, lam0, M, P, a["N"], a["nh"], a["d"],
-                               a["du"], a["T"], a["dtype"], *([grads] * 9), P, None)
+                               a["du"], a["T"], a["dtype"], 0, *([grads] * 9), P, None)
 
     assert bwd(M=None, Qf=None) == _lib.ERR_INVALID        # recompute needs Q_f
     assert bwd(lam0=None) == _lib.ERR_INVALID              # M without lam0

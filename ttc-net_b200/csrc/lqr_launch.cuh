@@ -43,13 +43,14 @@ struct QMix {
 template <int D, int DU, typename TIn>
 int launch_fwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N, int nh,
-               int T, void* u, float* lam0, float* M, int* status, const QMix& mix, cudaStream_t st);
+               int T, void* u, float* lam0, float* M, int* status, const QMix& mix, int opts,
+               cudaStream_t st);
 
 template <int D, int DU, typename TIn>
 int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
                const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
-               int* status, const QMix& mix, cudaStream_t st);
+               int* status, const QMix& mix, int opts, cudaStream_t st);
 
 // Partial slices (one per CTA) the mixed-Q_f backward writes for (N, nh) on the current
 // device; 0 when the mixed path is not available for the shape and rank, -TTC_ERR_CUDA on
@@ -95,7 +96,7 @@ template <int D, int DU, typename TIn, bool SAVE_M>
 int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                   const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N,
                   int nh, int T, void* u, float* lam0, float* M, int* status, const QMix& mix,
-                  cudaStream_t st) {
+                  int opts, cudaStream_t st) {
   using CF = TcCfg<D, DU>;
   using L = TcFwdLayout<D, DU, SAVE_M>;
   int slots = tc_slots<D, DU, SAVE_M>(nh);
@@ -110,19 +111,20 @@ int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, co
   k<<<dim3((unsigned)N), dim3(slots * 128), smem, st>>>(
       (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf,
       (const TIn*)mix.basis, mix.rank, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0,
-      nh, T, cols, (TIn*)u, lam0, M, status);
+      nh, T, opts, cols, (TIn*)u, lam0, M, status);
   return cuda_check(cudaGetLastError(), "lqr_fwd_tc_kernel launch");
 }
 
 template <int D, int DU, typename TIn>
 int launch_fwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N, int nh,
-               int T, void* u, float* lam0, float* M, int* status, const QMix& mix, cudaStream_t st) {
+               int T, void* u, float* lam0, float* M, int* status, const QMix& mix, int opts,
+               cudaStream_t st) {
   if (M != nullptr)
     return launch_fwd_tc<D, DU, TIn, true>(A, B, Q, R, Qf, lA, lB, lQ, h0, N, nh, T, u, lam0, M,
-                                           status, mix, st);
+                                           status, mix, opts, st);
   return launch_fwd_tc<D, DU, TIn, false>(A, B, Q, R, Qf, lA, lB, lQ, h0, N, nh, T, u, lam0,
-                                          nullptr, status, mix, st);
+                                          nullptr, status, mix, opts, st);
 }
 
 // Saved-state backward on the warp-MMA adjoint: R rows x ceil(nh / 8) warps per CTA.
@@ -199,7 +201,7 @@ template <int D, int DU, typename TIn>
 int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
                const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
-               int* status, const QMix& mix, cudaStream_t st) {
+               int* status, const QMix& mix, int opts, cudaStream_t st) {
   if constexpr (D == DU && D <= TTC_ADJ_MMA_MAXD) {
     if (M != nullptr && AdjMma<D>::fits(nh))
       return launch_bwd_mma<D, TIn, true>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status,
@@ -231,7 +233,7 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
   if (int rc = set_smem(k, smem)) return rc;
   k<<<dim3((unsigned)N), dim3(slots * 128), smem, st>>>(
       (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf, (const TIn*)lA,
-      (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0, (const TIn*)dU, nh, T, cols, (TIn*)g[0],
+      (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0, (const TIn*)dU, nh, T, opts, cols, (TIn*)g[0],
       (TIn*)g[1], (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6], (TIn*)g[7],
       (TIn*)g[8], status);
   return cuda_check(cudaGetLastError(), "lqr_bwd_tc_kernel launch");
@@ -245,10 +247,10 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
   template int ttc::launch_fwd<D, DU, TIn>(const void*, const void*, const void*, const void*, \
                                            const void*, const void*, const void*, const void*, \
                                            const void*, int64_t, int, int, void*, float*,      \
-                                           float*, int*, const ttc::QMix&, cudaStream_t);      \
+                                           float*, int*, const ttc::QMix&, int, cudaStream_t); \
   template int ttc::launch_bwd<D, DU, TIn>(const void*, const void*, const void*, const void*, \
                                            const void*, const void*, const void*, const void*, \
                                            const void*, const float*, const float*,            \
                                            const void*, int64_t, int, int, void* const*, int*, \
-                                           const ttc::QMix&, cudaStream_t);                    \
+                                           const ttc::QMix&, int, cudaStream_t);               \
   template int64_t ttc::bwd_mix_slices<D, DU, TIn>(int64_t, int, int);

@@ -17,6 +17,11 @@ int fail(int code, const char* msg) { return ttc::set_error(code, msg); }
 
 bool supported(int d, int du) { return du == d && (d == 16 || d == 32 || d == 64); }
 
+int check_flags(int flags) {
+  if (flags & ~TTC_FLAG_INV_GUARD) return fail(TTC_ERR_INVALID, "unknown flag bits");
+  return TTC_OK;
+}
+
 int check_common(int64_t N, int nh, int d, int du, int T, int dtype) {
   if (N < 0 || N > 0x7fffffffLL) return fail(TTC_ERR_INVALID, "N (rows) must be in [0, 2^31)");
   if (nh < 1) return fail(TTC_ERR_INVALID, "num_heads must be >= 1");
@@ -50,8 +55,9 @@ const char* ttc_last_error(void) { return g_err; }
 int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                 const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
                 const void* log_gamma_Q, const void* h0, int64_t N, int nh, int d, int du,
-                int T, int dtype, void* u, float* lam0, float* M, int* status, void* stream) {
+                int T, int dtype, int flags, void* u, float* lam0, float* M, int* status, void* stream) {
   if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (int rc = check_flags(flags)) return rc;
   if (N == 0) return TTC_OK;
   if (!A_diag || !B || !Q || !R_inv || !Q_f || !log_gamma_A || !log_gamma_B || !log_gamma_Q ||
       !h0 || !u || !status)
@@ -59,7 +65,7 @@ int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_FWD(DD, DDU, TT)                                                                 \
   return ttc::launch_fwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,        \
-                                 log_gamma_Q, h0, N, nh, T, u, lam0, M, status, ttc::QMix{}, st)
+                                 log_gamma_Q, h0, N, nh, T, u, lam0, M, status, ttc::QMix{}, flags, st)
   if (dtype == TTC_DTYPE_F32) {
     if (d == 16) TTC_FWD(16, 16, float);
     if (d == 32) TTC_FWD(32, 32, float);
@@ -75,11 +81,12 @@ int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_
 int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                 const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
                 const void* log_gamma_Q, const void* h0, const float* lam0, const float* M,
-                const void* d_u, int64_t N, int nh, int d, int du, int T, int dtype,
+                const void* d_u, int64_t N, int nh, int d, int du, int T, int dtype, int flags,
                 void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_Q_f,
                 void* grad_lgA, void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status,
                 void* stream) {
   if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (int rc = check_flags(flags)) return rc;
   if (N == 0) return TTC_OK;
   if (!A_diag || !B || !Q || !R_inv || !log_gamma_A || !log_gamma_B || !log_gamma_Q || !h0 ||
       !d_u || !status)
@@ -94,7 +101,7 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_BWD(DD, DDU, TT)                                                                  \
   return ttc::launch_bwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,         \
-                                 log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, ttc::QMix{}, st)
+                                 log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, ttc::QMix{}, flags, st)
   if (dtype == TTC_DTYPE_F32) {
     if (d == 16) TTC_BWD(16, 16, float);
     if (d == 32) TTC_BWD(32, 32, float);
@@ -110,9 +117,10 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
 int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                     const void* coeff_Qf, const void* Q_basis, int rQ, const void* log_gamma_A,
                     const void* log_gamma_B, const void* log_gamma_Q, const void* h0, int64_t N, int nh,
-                    int d, int du, int T, int dtype, void* u, float* lam0, float* M, int* status,
+                    int d, int du, int T, int dtype, int flags, void* u, float* lam0, float* M, int* status,
                     void* stream) {
   if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (int rc = check_flags(flags)) return rc;
   if (rQ < 1) return fail(TTC_ERR_INVALID, "rank of the Q_f mixture must be >= 1");
   if (N == 0) return TTC_OK;
   if (!A_diag || !B || !Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A || !log_gamma_B ||
@@ -124,7 +132,7 @@ int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_FWD(DD, DDU, TT)                                                                 \
   return ttc::launch_fwd<DD, DDU, TT>(A_diag, B, Q, R_inv, coeff_Qf, log_gamma_A, log_gamma_B,   \
-                                 log_gamma_Q, h0, N, nh, T, u, lam0, M, status, mix, st)
+                                 log_gamma_Q, h0, N, nh, T, u, lam0, M, status, mix, flags, st)
   if (dtype == TTC_DTYPE_F32) {
     if (d == 16) TTC_FWD(16, 16, float);
     if (d == 32) TTC_FWD(32, 32, float);
@@ -187,7 +195,7 @@ int ttc_lqr_bwd_mix(const void* A_diag, const void* B, const void* Q, const void
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_BWD(DD, DDU, TT)                                                                  \
   return ttc::launch_bwd<DD, DDU, TT>(A_diag, B, Q, R_inv, coeff_Qf, log_gamma_A, log_gamma_B,    \
-                                 log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, mix, st)
+                                 log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, mix, 0, st)
   if (dtype == TTC_DTYPE_F32) {
     if (d == 16) TTC_BWD(16, 16, float);
     if (d == 32) TTC_BWD(32, 32, float);

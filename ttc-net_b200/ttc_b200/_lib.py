@@ -10,7 +10,7 @@ import os
 import threading
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libttc_b200.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -25,6 +25,8 @@ STATUS_LU_UNSTABLE = 2
 STATUS_BWD_UNSTABLE = 4
 STATUS_U_NAN = 8
 
+FLAG_INV_GUARD = 1
+
 # Every symbol include/ttc_b200.h declares, with (restype, argtypes).
 _P = ctypes.c_void_p
 _FP = ctypes.c_void_p      # float* passed as a raw address
@@ -34,9 +36,9 @@ SIGNATURES = {
     "ttc_abi_version": (_I, []),
     "ttc_supported": (_I, [_I, _I]),
     "ttc_last_error": (ctypes.c_char_p, []),
-    "ttc_lqr_fwd": (_I, [_P] * 9 + [_I64, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
-    "ttc_lqr_bwd": (_I, [_P] * 9 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I] + [_P] * 9 + [_P, _P]),
-    "ttc_lqr_fwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_I64, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
+    "ttc_lqr_fwd": (_I, [_P] * 9 + [_I64, _I, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
+    "ttc_lqr_bwd": (_I, [_P] * 9 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I, _I] + [_P] * 9 + [_P, _P]),
+    "ttc_lqr_fwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_I64, _I, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
     "ttc_lqr_bwd_mix_slices": (_I64, [_I64, _I, _I, _I, _I, _I]),
     "ttc_lqr_bwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I]
                         + [_P] * 5 + [_FP, _I64] + [_P] * 4 + [_P, _P]),

@@ -106,8 +106,9 @@ class LQRSolveFunction(torch.autograd.Function):
     tensor carrying the forward's TTC_STATUS_* bits."""
 
     @staticmethod
-    def forward(ctx, A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T, save_budget):
+    def forward(ctx, A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T, save_budget, flags=0):
         T = int(T)
+        flags = int(flags)
         N, nh, d, du = _check_shapes(A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T)
         dtype = Q.dtype
         if dtype not in _DTYPES:
@@ -122,7 +123,7 @@ class LQRSolveFunction(torch.autograd.Function):
         status = torch.zeros(1, device=dev, dtype=torch.int32)
         with torch.cuda.device(dev), torch.profiler.record_function("fwd:ttc_lqr_fwd"):
             _launch("ttc_lqr_fwd", dev, lib.ttc_lqr_fwd, *[_ptr(a) for a in args], N, nh, d, du,
-                    T, _DTYPES[dtype], _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
+                    T, _DTYPES[dtype], flags, _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
         st = int(status.item())
         if st & _lib.STATUS_FWD_UNSTABLE:
             raise RuntimeError(FWD_UNSTABLE_MSG)
@@ -132,6 +133,7 @@ class LQRSolveFunction(torch.autograd.Function):
         ctx.save_for_backward(A_c, B_c, Q_c, R_c, None if keep_m else Qf_c, lA_c, lB_c, lQ_c,
                               h0_c, lam0 if keep_m else None, M)
         ctx.dims = (N, nh, d, du, T)
+        ctx.flags = flags
         ctx.dtype = dtype
         ctx.in_dtypes = [t.dtype for t in (A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0)]
         status_cpu = torch.tensor([st], dtype=torch.int32)
@@ -153,12 +155,12 @@ class LQRSolveFunction(torch.autograd.Function):
         with torch.cuda.device(dev), torch.profiler.record_function("bwd:ttc_lqr_bwd"):
             _launch("ttc_lqr_bwd", dev, lib.ttc_lqr_bwd,
                     *[_ptr(t) for t in (A, B, Q, R, Qf, lA, lB, lQ, h0)], _ptr(lam0), _ptr(M),
-                    _ptr(d_u), N, nh, d, du, T, _DTYPES[dtype], *[_ptr(g) for g in grads],
+                    _ptr(d_u), N, nh, d, du, T, _DTYPES[dtype], ctx.flags, *[_ptr(g) for g in grads],
                     _ptr(status))
         if int(status.item()) & _lib.STATUS_BWD_UNSTABLE:
             raise RuntimeError(BWD_UNSTABLE_MSG)
         grads = [g.to(dt) for g, dt in zip(grads, ctx.in_dtypes)]
-        return (*grads, None, None)
+        return (*grads, None, None, None)
 
 
 def mix_available(N: int, nh: int, d: int, du: int, rQ: int, dtype, save_budget: int | None = None) -> bool:
@@ -199,7 +201,7 @@ class LQRSolveMixFunction(torch.autograd.Function):
         with torch.cuda.device(dev), torch.profiler.record_function("fwd:ttc_lqr_fwd_mix"):
             _launch("ttc_lqr_fwd", dev, lib.ttc_lqr_fwd_mix, _ptr(A_c), _ptr(B_c), _ptr(Q_c), _ptr(R_c),
                     _ptr(cQf_c), _ptr(Qb_c), rQ, _ptr(lA_c), _ptr(lB_c), _ptr(lQ_c), _ptr(h0_c), N, nh, d,
-                    du, T, _DTYPES[dtype], _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
+                    du, T, _DTYPES[dtype], 0, _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
         st = int(status.item())
         if st & _lib.STATUS_FWD_UNSTABLE:
             raise RuntimeError(FWD_UNSTABLE_MSG)
@@ -253,20 +255,38 @@ def lqr_solve_mix_with_status(A_diag, B, Q, R_inv_diag, coeff_Qf, Q_basis, log_g
     return u, int(status.item())
 
 
+def _flags(inv_guard: bool) -> int:
+    return _lib.FLAG_INV_GUARD if inv_guard else 0
+
+
 def lqr_solve_with_status(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q,
-                          h0, T, save_budget: int | None = None):
+                          h0, T, save_budget: int | None = None, inv_guard: bool = False):
     """Like ``cuda_lqr_solve`` but also returns the forward's status bits (host int)."""
     budget = SAVE_BUDGET_BYTES if save_budget is None else int(save_budget)
     u, status = LQRSolveFunction.apply(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B,
-                                       log_gamma_Q, h0, T, budget)
+                                       log_gamma_Q, h0, T, budget, _flags(inv_guard))
     return u, int(status.item())
 
 
 def cuda_lqr_solve(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
-                   save_budget: int | None = None):
-    """Drop-in for the reference solvers (ttc_layer.py:137): returns u [N, nh, du]."""
+                   save_budget: int | None = None, inv_guard: bool = False, num_chunks: int = 1):
+    """Drop-in for the reference solvers (ttc_layer.py:137): returns u [N, nh, du].
+
+    ``inv_guard`` adds 1e-6 I to Y1 before the solve, as the reference's fused solver
+    (fused_lqr.py:294-304).  ``num_chunks`` is the horizon split of fused_lqr_layer_fwd
+    (fused_lqr.py:26-35, T divisible by it); the kernels keep the recurrence state on chip for
+    the whole horizon with each step's own discount exponent, so every split gives the
+    unchunked result."""
+    assert T > 0 and T % num_chunks == 0, "T must be a positive multiple of num_chunks"
     return lqr_solve_with_status(A_diag, B, Q, R_inv_diag, Q_f, log_gamma_A, log_gamma_B,
-                                 log_gamma_Q, h0, T, save_budget)[0]
+                                 log_gamma_Q, h0, T, save_budget, inv_guard)[0]
+
+
+def fused_lqr_solve(A_diag, B, Q, R_inv_diag, Q_f, gamma_A, gamma_B, gamma_Q, h0, T,
+                    inv_guard: bool = False):
+    """The reference's public fused entry point (fused_lqr.py:294-304), same signature."""
+    return cuda_lqr_solve(A_diag, B, Q, R_inv_diag, Q_f, gamma_A, gamma_B, gamma_Q, h0, T,
+                          inv_guard=inv_guard)
 
 
 # The plug-in map of ttc_layer.py:18-22.  "fused" (the reference's default name) maps to
