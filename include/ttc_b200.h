@@ -55,7 +55,8 @@ extern "C" {
 /* ABI version of the loaded library (== TTC_ABI_VERSION it was built with). */
 int ttc_abi_version(void);
 
-/* 1 if kernels for state dim d and action dim du are compiled in, else 0. */
+/* 1 if kernels for state dim d and action dim du are compiled in, else 0: d in {16, 32, 64},
+ * du in {16, 32, 64} with du <= d (du is the N of a 128-row tcgen05 MMA: a multiple of 16). */
 int ttc_supported(int d, int du);
 
 /* Message of the last TTC_ERR_* returned by this library ("" if none). */

@@ -48,7 +48,11 @@ def test_supported_shapes(lib):
     assert lib.ttc_supported(32, 32) == 1
     assert lib.ttc_supported(64, 64) == 1
     assert lib.ttc_supported(24, 24) == 0
-    assert lib.ttc_supported(32, 16) == 0
+    assert lib.ttc_supported(32, 16) == 1   # u_dim < h_dim, multiples of 16
+    assert lib.ttc_supported(64, 32) == 1
+    assert lib.ttc_supported(64, 16) == 1
+    assert lib.ttc_supported(16, 32) == 0   # u_dim > h_dim
+    assert lib.ttc_supported(32, 8) == 0    # u_dim not a multiple of 16
 
 
 def _fwd(lib, N=1, nh=1, d=16, du=16, T=4, dtype=0, null_inputs=False, flags=0):

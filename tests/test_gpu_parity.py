@@ -278,6 +278,47 @@ def test_layer_options_match_oracle(kw):
         assert O.max_rel(p1.grad.cpu(), p2.grad) < GRAD_TOL_F32, n1
 
 
+@pytest.mark.parametrize("save_budget", [None, 0], ids=["saved", "recompute"])
+@pytest.mark.parametrize("d,du,nh,N,T", [(32, 16, 5, 4, 24), (64, 32, 2, 3, 16), (64, 16, 3, 2, 12)])
+def test_solver_udim_below_hdim_matches_oracle(d, du, nh, N, T, save_budget):
+    """u_dim < h_dim (TTCLayer's u_dim argument, ttc_layer.py:30-49): the same kernels with a
+    d x du B, against the oracle's fused restatement (grads) and riccati (u)."""
+    host = [torch.from_numpy(a) for a in solver_inputs_synthetic(N, nh, d, du, seed=500 + d + du)]
+    dy = torch.randn(N, nh, du, dtype=torch.float64, generator=torch.Generator().manual_seed(8))
+    leaves = [a.clone().requires_grad_(True) for a in host]
+    u_ref = O.fused_solve(*leaves, T)
+    (u_ref * dy).sum().backward()
+    u_ric = O.riccati_solve(*host, T, solve_dtype=None)
+    args = [a.to("cuda", torch.float32).requires_grad_(True) for a in host]
+    u, grads = run_cuda(args, T, dy.float().cuda(), save_budget)
+    assert u.shape == (N, nh, du)
+    assert O.max_rel(u.cpu(), u_ric) < FWD_TOL_F32
+    for name, g, leaf in zip(SOLVER_ARG_NAMES, grads, leaves):
+        assert O.max_rel(g.cpu(), leaf.grad) < GRAD_TOL_F32, name
+
+
+def test_layer_udim_below_hdim_matches_oracle():
+    from ttc_b200 import TTCLayer
+    torch.manual_seed(13)
+    cu = TTCLayer(24, 20, 32, 3, 8, 32, u_dim=16)
+    ref = O.TTCLayerOracle(24, 20, 32, 3, 8, 32, u_dim=16, solver_impl="fused").double()
+    ref.load_state_dict({k: v.double() for k, v in cu.state_dict().items()})
+    cu = cu.cuda()
+    g = torch.Generator().manual_seed(14)
+    x = torch.randn(2, 4, 24, generator=g)
+    dy = torch.randn(2, 4, 20, generator=g)
+    xc = x.cuda().requires_grad_(True)
+    y = cu(xc, T=20)
+    y.backward(dy.cuda())
+    xr = x.double().requires_grad_(True)
+    yr = ref(xr, T=20)
+    yr.backward(dy.double())
+    assert O.max_rel(y.detach().cpu(), yr) < FWD_TOL_F32
+    assert O.max_rel(xc.grad.cpu(), xr.grad) < GRAD_TOL_F32
+    for (n1, p1), (n2, p2) in zip(cu.named_parameters(), ref.named_parameters()):
+        assert O.max_rel(p1.grad.cpu(), p2.grad) < GRAD_TOL_F32, n1
+
+
 def test_unsupported_state_dims_raise():
     from ttc_b200 import TTCLayer
     layer = TTCLayer(8, 8, 16, 2, 16, 16, u_dim=8).cuda()

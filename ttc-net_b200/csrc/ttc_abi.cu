@@ -15,7 +15,22 @@ char g_err[512] = "";
 
 int fail(int code, const char* msg) { return ttc::set_error(code, msg); }
 
-bool supported(int d, int du) { return du == d && (d == 16 || d == 32 || d == 64); }
+// (h_dim, u_dim) pairs with kernels: u_dim <= h_dim, both multiples of 16 (the MMA N of a
+// 128-row tcgen05 tile), h_dim in {16, 32, 64}.
+bool supported(int d, int du) {
+  return (d == 16 || d == 32 || d == 64) && (du == 16 || du == 32 || du == 64) && du <= d;
+}
+
+// Expands X(D, DU, TIn) for the supported pair (d, du); callers checked supported() first.
+#define TTC_FOR_DIMS(X, TT)             \
+  do {                                  \
+    if (d == 16) X(16, 16, TT);         \
+    if (d == 32 && du == 32) X(32, 32, TT); \
+    if (d == 32) X(32, 16, TT);         \
+    if (d == 64 && du == 64) X(64, 64, TT); \
+    if (d == 64 && du == 32) X(64, 32, TT); \
+    X(64, 16, TT);                      \
+  } while (0)
 
 int check_flags(int flags) {
   if (flags & ~TTC_FLAG_INV_GUARD) return fail(TTC_ERR_INVALID, "unknown flag bits");
@@ -66,15 +81,8 @@ int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_
 #define TTC_FWD(DD, DDU, TT)                                                                 \
   return ttc::launch_fwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,        \
                                  log_gamma_Q, h0, N, nh, T, u, lam0, M, status, ttc::QMix{}, flags, st)
-  if (dtype == TTC_DTYPE_F32) {
-    if (d == 16) TTC_FWD(16, 16, float);
-    if (d == 32) TTC_FWD(32, 32, float);
-    TTC_FWD(64, 64, float);
-  } else {
-    if (d == 16) TTC_FWD(16, 16, __nv_bfloat16);
-    if (d == 32) TTC_FWD(32, 32, __nv_bfloat16);
-    TTC_FWD(64, 64, __nv_bfloat16);
-  }
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_FWD, float);
+  TTC_FOR_DIMS(TTC_FWD, __nv_bfloat16);
 #undef TTC_FWD
 }
 
@@ -102,15 +110,8 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
 #define TTC_BWD(DD, DDU, TT)                                                                  \
   return ttc::launch_bwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,         \
                                  log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, ttc::QMix{}, flags, st)
-  if (dtype == TTC_DTYPE_F32) {
-    if (d == 16) TTC_BWD(16, 16, float);
-    if (d == 32) TTC_BWD(32, 32, float);
-    TTC_BWD(64, 64, float);
-  } else {
-    if (d == 16) TTC_BWD(16, 16, __nv_bfloat16);
-    if (d == 32) TTC_BWD(32, 32, __nv_bfloat16);
-    TTC_BWD(64, 64, __nv_bfloat16);
-  }
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_BWD, float);
+  TTC_FOR_DIMS(TTC_BWD, __nv_bfloat16);
 #undef TTC_BWD
 }
 
@@ -133,31 +134,17 @@ int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void
 #define TTC_FWD(DD, DDU, TT)                                                                 \
   return ttc::launch_fwd<DD, DDU, TT>(A_diag, B, Q, R_inv, coeff_Qf, log_gamma_A, log_gamma_B,   \
                                  log_gamma_Q, h0, N, nh, T, u, lam0, M, status, mix, flags, st)
-  if (dtype == TTC_DTYPE_F32) {
-    if (d == 16) TTC_FWD(16, 16, float);
-    if (d == 32) TTC_FWD(32, 32, float);
-    TTC_FWD(64, 64, float);
-  } else {
-    if (d == 16) TTC_FWD(16, 16, __nv_bfloat16);
-    if (d == 32) TTC_FWD(32, 32, __nv_bfloat16);
-    TTC_FWD(64, 64, __nv_bfloat16);
-  }
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_FWD, float);
+  TTC_FOR_DIMS(TTC_FWD, __nv_bfloat16);
 #undef TTC_FWD
 }
 
 int64_t ttc_lqr_bwd_mix_slices(int64_t N, int nh, int d, int du, int rQ, int dtype) {
   if (int rc = check_common(N, nh, d, du, 1, dtype)) return -rc;
   if (N == 0 || rQ < 1) return 0;
-#define TTC_SL(DD, TT) return ttc::bwd_mix_slices<DD, DD, TT>(N, nh, rQ)
-  if (dtype == TTC_DTYPE_F32) {
-    if (d == 16) TTC_SL(16, float);
-    if (d == 32) TTC_SL(32, float);
-    TTC_SL(64, float);
-  } else {
-    if (d == 16) TTC_SL(16, __nv_bfloat16);
-    if (d == 32) TTC_SL(32, __nv_bfloat16);
-    TTC_SL(64, __nv_bfloat16);
-  }
+#define TTC_SL(DD, DDU, TT) return ttc::bwd_mix_slices<DD, DDU, TT>(N, nh, rQ)
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_SL, float);
+  TTC_FOR_DIMS(TTC_SL, __nv_bfloat16);
 #undef TTC_SL
 }
 
@@ -196,15 +183,8 @@ int ttc_lqr_bwd_mix(const void* A_diag, const void* B, const void* Q, const void
 #define TTC_BWD(DD, DDU, TT)                                                                  \
   return ttc::launch_bwd<DD, DDU, TT>(A_diag, B, Q, R_inv, coeff_Qf, log_gamma_A, log_gamma_B,    \
                                  log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, mix, 0, st)
-  if (dtype == TTC_DTYPE_F32) {
-    if (d == 16) TTC_BWD(16, 16, float);
-    if (d == 32) TTC_BWD(32, 32, float);
-    TTC_BWD(64, 64, float);
-  } else {
-    if (d == 16) TTC_BWD(16, 16, __nv_bfloat16);
-    if (d == 32) TTC_BWD(32, 32, __nv_bfloat16);
-    TTC_BWD(64, 64, __nv_bfloat16);
-  }
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_BWD, float);
+  TTC_FOR_DIMS(TTC_BWD, __nv_bfloat16);
 #undef TTC_BWD
 }
 
