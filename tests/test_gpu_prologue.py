@@ -8,8 +8,8 @@ from prologue_ref import prologue_torch
 pytestmark = pytest.mark.gpu
 
 
-SHAPES = [(512, 16, 16, 16, 16, 16), (300, 5, 32, 32, 32, 32), (64, 3, 64, 64, 64, 64),
-          (100, 2, 16, 32, 8, 24)]
+SHAPES = [(512, 16, 16, 16, 16, 16), (77, 3, 16, 16, 16, 16), (300, 5, 32, 32, 32, 32),
+          (64, 3, 64, 64, 64, 64), (100, 2, 16, 32, 8, 24), (40, 3, 32, 16, 64, 32)]
 
 
 def _z(N, nh, d, du, rB, rQ, dtype, seed):

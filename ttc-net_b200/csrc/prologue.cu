@@ -10,8 +10,12 @@
 // softplus(x) = x > 20 ? x : log1p(exp(x)) (torch's default threshold).  Results are rounded
 // to the activation dtype where the reference's PyTorch ops round them (after each op), and
 // the backward applies the chain rule of the same ops with the same roundings of the
-// intermediate gradients.  One warp per (row, head) slice plus one warp per row for the
-// coefficients; every sum is a fixed shuffle tree, so results are run-to-run identical.
+// intermediate gradients.
+//
+// Work split: a head slice belongs to a segment of SEG lanes of a warp (SEG = 16 for vectors
+// of at most 16, so two heads share a warp; else 32), each lane holding PER elements of every
+// vector; a row's mixture coefficients (up to 64 long) take a whole warp.  Every sum is a
+// fixed xor-shuffle tree inside the segment, so results are run-to-run identical.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -32,7 +36,7 @@ using ttc::stf;
 
 constexpr float kEps = 1e-6f;
 constexpr float kRinvMin = 1e-6f;
-constexpr int kPer = 2;  // elements per lane: vectors up to 64 long
+constexpr int kMaxLen = 64;  // longest vector: h_dim, u_dim and the ranks
 
 template <typename T>
 __device__ __forceinline__ float round_t(float x) {
@@ -51,51 +55,64 @@ __device__ __forceinline__ float softplus_grad(float x, float g) {
   return g * z / (z + 1.0f);
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
+// Sum over the SEG lanes of this thread's segment (all 32 lanes execute it).
+template <int SEG>
+__device__ __forceinline__ float seg_sum(float v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int o = SEG / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 
-// A vector of n <= 64 values spread over the warp: lane l holds elements l and l + 32.
+// A vector of n <= SEG * PER values over a segment: lane l of the segment holds elements
+// l, l + SEG, ...
+template <int PER>
 struct Vec {
-  float v[kPer];
-  bool on[kPer];
+  float v[PER];
+  bool on[PER];
 };
 
-template <typename T>
-__device__ __forceinline__ Vec load_vec(const T* p, int n, int lane) {
-  Vec x;
+template <int SEG, int PER, typename T>
+__device__ __forceinline__ Vec<PER> load_vec(const T* p, int n, int ls) {
+  Vec<PER> x;
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int e = lane + 32 * k;
+  for (int k = 0; k < PER; ++k) {
+    const int e = ls + SEG * k;
     x.on[k] = e < n;
     x.v[k] = x.on[k] ? ldf(p + e) : 0.f;
   }
   return x;
 }
 
-template <typename T>
-__device__ __forceinline__ void store_vec(T* p, const Vec& x) {
-  const int lane = threadIdx.x & 31;
+template <int SEG, int PER, typename T>
+__device__ __forceinline__ void store_vec(T* p, const Vec<PER>& x, int ls) {
 #pragma unroll
-  for (int k = 0; k < kPer; ++k)
-    if (x.on[k]) stf(p + lane + 32 * k, x.v[k]);
+  for (int k = 0; k < PER; ++k)
+    if (x.on[k]) stf(p + ls + SEG * k, x.v[k]);
 }
 
-__device__ __forceinline__ float sum_sq(const Vec& x) {
-  float s = 0.f;
+template <int SEG, int PER, typename T>
+__device__ __forceinline__ Vec<PER> grad_or_zero(const T* p, int n, int ls) {
+  if (p == nullptr) {
+    Vec<PER> z;
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) s = fmaf(x.v[k], x.v[k], s);
-  return warp_sum(s);
+    for (int k = 0; k < PER; ++k) {
+      z.v[k] = 0.f;
+      z.on[k] = ls + SEG * k < n;
+    }
+    return z;
+  }
+  return load_vec<SEG, PER>(p, n, ls);
 }
 
 // y = round_T(x rsqrt(sum x^2 + eps)); returns rs.
-template <typename T>
-__device__ __forceinline__ float l2norm_fwd(const Vec& x, Vec& y) {
-  const float rs = rsqrtf(sum_sq(x) + kEps);
+template <int SEG, int PER, typename T>
+__device__ __forceinline__ float l2norm_fwd(const Vec<PER>& x, Vec<PER>& y) {
+  float s = 0.f;
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) {
+  for (int k = 0; k < PER; ++k) s = fmaf(x.v[k], x.v[k], s);
+  const float rs = rsqrtf(seg_sum<SEG>(s) + kEps);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
     y.on[k] = x.on[k];
     y.v[k] = round_t<T>(x.v[k] * rs);
   }
@@ -103,43 +120,68 @@ __device__ __forceinline__ float l2norm_fwd(const Vec& x, Vec& y) {
 }
 
 // dx = round_T(rs g - x rs^3 sum(g x)) for y = x rs(x) (autograd of the fp32 formula).
-template <typename T>
-__device__ __forceinline__ void l2norm_bwd(const Vec& x, float rs, const Vec& g, Vec& dx) {
+template <int SEG, int PER, typename T>
+__device__ __forceinline__ void l2norm_bwd(const Vec<PER>& x, float rs, const Vec<PER>& g, Vec<PER>& dx) {
   float dot = 0.f;
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) dot = fmaf(g.v[k], x.v[k], dot);
-  dot = warp_sum(dot);
-  const float c = dot * rs * rs * rs;
+  for (int k = 0; k < PER; ++k) dot = fmaf(g.v[k], x.v[k], dot);
+  const float c = seg_sum<SEG>(dot) * rs * rs * rs;
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) {
+  for (int k = 0; k < PER; ++k) {
     dx.on[k] = x.on[k];
     dx.v[k] = round_t<T>(fmaf(rs, g.v[k], -c * x.v[k]));
   }
 }
 
-template <typename T>
-__device__ __forceinline__ Vec softplus_vec(const Vec& x) {
-  Vec y;
+template <int PER, typename T>
+__device__ __forceinline__ Vec<PER> softplus_vec(const Vec<PER>& x) {
+  Vec<PER> y;
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) {
+  for (int k = 0; k < PER; ++k) {
     y.on[k] = x.on[k];
     y.v[k] = x.on[k] ? round_t<T>(softplus(x.v[k])) : 0.f;
   }
   return y;
 }
 
-template <typename T>
-__device__ __forceinline__ Vec grad_or_zero(const T* p, int n, int lane) {
-  if (p == nullptr) {
-    Vec z;
+template <int PER>
+__device__ __forceinline__ Vec<PER> negated(Vec<PER> x) {
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      z.v[k] = 0.f;
-      z.on[k] = lane + 32 * k < n;
-    }
-    return z;
+  for (int k = 0; k < PER; ++k) x.v[k] = -x.v[k];
+  return x;
+}
+
+// d/dz of l2norm(softplus(z)) (optionally clamped from below after the l2norm) for the
+// incoming gradient g of the result.
+template <int SEG, int PER, typename T, bool CLAMP>
+__device__ __forceinline__ Vec<PER> softplus_l2norm_bwd(const Vec<PER>& z, const Vec<PER>& g) {
+  const Vec<PER> sp = softplus_vec<PER, T>(z);
+  Vec<PER> y, gy = g, dsp, dz;
+  const float rs = l2norm_fwd<SEG, PER, T>(sp, y);
+  if constexpr (CLAMP) {
+    const float lo = round_t<T>(kRinvMin);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) gy.v[k] = y.v[k] >= lo ? g.v[k] : 0.f;
   }
-  return load_vec(p, n, lane);
+  l2norm_bwd<SEG, PER, T>(sp, rs, gy, dsp);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    dz.on[k] = z.on[k];
+    dz.v[k] = z.on[k] ? round_t<T>(softplus_grad(z.v[k], dsp.v[k])) : 0.f;
+  }
+  return dz;
+}
+
+// d/dz of -softplus(z): the negated gradient through softplus.
+template <int PER, typename T>
+__device__ __forceinline__ Vec<PER> neg_softplus_bwd(const Vec<PER>& z, const Vec<PER>& g) {
+  Vec<PER> dz;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    dz.on[k] = z.on[k];
+    dz.v[k] = z.on[k] ? round_t<T>(softplus_grad(z.v[k], -g.v[k])) : 0.f;
+  }
+  return dz;
 }
 
 struct Dims {
@@ -158,148 +200,131 @@ struct Dims {
   }
 };
 
-template <typename T>
+// Task w of a row: head groups of 32 / SEG heads (one per segment), then the row's
+// coefficients.  tasks_per_row = ceil(nh / (32 / SEG)) + 1.
+template <int SEG>
+__device__ __forceinline__ int tasks_per_row(int nh) {
+  constexpr int HPW = 32 / SEG;
+  return (nh + HPW - 1) / HPW + 1;
+}
+
+template <int SEG, int PER, typename T>
 __global__ void __launch_bounds__(256) prologue_fwd_kernel(
     const T* __restrict__ Z, int64_t N, Dims D, T* __restrict__ A_out, T* __restrict__ R_out,
     T* __restrict__ cQf_out, T* __restrict__ lgA_out, T* __restrict__ lgB_out,
     T* __restrict__ lgQ_out, T* __restrict__ h0_out, T* __restrict__ cB_out,
     T* __restrict__ cQ_out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t slots = N * (D.nh + 1);
+  constexpr int HPW = 32 / SEG;
+  const int lane = threadIdx.x & 31, seg = lane / SEG, ls = lane % SEG;
+  const int tpr = tasks_per_row<SEG>(D.nh);
+  const int64_t tasks = N * tpr;
   const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < slots; w += stride) {
-    const int64_t n = w / (D.nh + 1);
-    const int h = static_cast<int>(w % (D.nh + 1));
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < tasks; w += stride) {
+    const int64_t n = w / tpr;
+    const int task = static_cast<int>(w % tpr);
     const T* zr = Z + n * D.W;
-    if (h == D.nh) {  // per-row mixture coefficients
-      Vec cb = load_vec(zr + D.nh * D.Hs, D.rB, lane), y;
-      l2norm_fwd<T>(cb, y);
-      store_vec(cB_out + n * D.rB, y);
-      Vec cq = softplus_vec<T>(load_vec(zr + D.nh * D.Hs + D.rB, D.rQ, lane));
-      l2norm_fwd<T>(cq, y);
-      store_vec(cQ_out + n * D.rQ, y);
+    if (task == tpr - 1) {  // per-row mixture coefficients: the whole warp
+      Vec<2> y;
+      l2norm_fwd<32, 2, T>(load_vec<32, 2>(zr + D.nh * D.Hs, D.rB, lane), y);
+      store_vec<32, 2>(cB_out + n * D.rB, y, lane);
+      l2norm_fwd<32, 2, T>(softplus_vec<2, T>(load_vec<32, 2>(zr + D.nh * D.Hs + D.rB, D.rQ, lane)), y);
+      store_vec<32, 2>(cQ_out + n * D.rQ, y, lane);
       continue;
     }
-    const T* z = zr + (int64_t)h * D.Hs;
-    const int64_t p = n * D.nh + h;
-    Vec y;
-    store_vec(h0_out + p * D.d, load_vec(z, D.d, lane));
-    l2norm_fwd<T>(load_vec(z + D.oA, D.d, lane), y);
-    store_vec(A_out + p * D.d, y);
-    l2norm_fwd<T>(softplus_vec<T>(load_vec(z + D.oR, D.du, lane)), y);
+    const int h = task * HPW + seg;
+    const bool valid = h < D.nh;
+    // A segment without a head runs the same shuffles on empty vectors and stores nothing.
+    const int nd = valid ? D.d : 0, ndu = valid ? D.du : 0;
+    const T* z = zr + (int64_t)(valid ? h : 0) * D.Hs;
+    const int64_t p = valid ? n * D.nh + h : 0;
+    Vec<PER> y;
+    store_vec<SEG, PER>(h0_out + p * D.d, load_vec<SEG, PER>(z, nd, ls), ls);
+    l2norm_fwd<SEG, PER, T>(load_vec<SEG, PER>(z + D.oA, nd, ls), y);
+    store_vec<SEG, PER>(A_out + p * D.d, y, ls);
+    l2norm_fwd<SEG, PER, T>(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oR, ndu, ls)), y);
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) y.v[k] = round_t<T>(fmaxf(y.v[k], kRinvMin));
-    store_vec(R_out + p * D.du, y);
-    l2norm_fwd<T>(softplus_vec<T>(load_vec(z + D.oQf, D.d, lane)), y);
-    store_vec(cQf_out + p * D.d, y);
-    if (lane == 0) stf(lgA_out + p, -round_t<T>(softplus(ldf(z + D.oGA))));
-    Vec g = softplus_vec<T>(load_vec(z + D.oGB, D.du, lane));
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) g.v[k] = -g.v[k];
-    store_vec(lgB_out + p * D.du, g);
-    g = softplus_vec<T>(load_vec(z + D.oGQ, D.d, lane));
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) g.v[k] = -g.v[k];
-    store_vec(lgQ_out + p * D.d, g);
+    for (int k = 0; k < PER; ++k) y.v[k] = round_t<T>(fmaxf(y.v[k], kRinvMin));
+    store_vec<SEG, PER>(R_out + p * D.du, y, ls);
+    l2norm_fwd<SEG, PER, T>(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oQf, nd, ls)), y);
+    store_vec<SEG, PER>(cQf_out + p * D.d, y, ls);
+    if (valid && ls == 0) stf(lgA_out + p, -round_t<T>(softplus(ldf(z + D.oGA))));
+    store_vec<SEG, PER>(lgB_out + p * D.du, negated(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oGB, ndu, ls))), ls);
+    store_vec<SEG, PER>(lgQ_out + p * D.d, negated(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oGQ, nd, ls))), ls);
   }
 }
 
-// d/dz of l2norm(softplus(z)) (optionally clamped from below after the l2norm) for the
-// incoming gradient g of the result.
-template <typename T, bool CLAMP>
-__device__ __forceinline__ Vec softplus_l2norm_bwd(const Vec& z, const Vec& g) {
-  const Vec sp = softplus_vec<T>(z);
-  Vec y, gy = g, dsp, dz;
-  const float rs = l2norm_fwd<T>(sp, y);
-  if constexpr (CLAMP) {
-    const float lo = round_t<T>(kRinvMin);
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) gy.v[k] = y.v[k] >= lo ? g.v[k] : 0.f;
-  }
-  l2norm_bwd<T>(sp, rs, gy, dsp);
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    dz.on[k] = z.on[k];
-    dz.v[k] = z.on[k] ? round_t<T>(softplus_grad(z.v[k], dsp.v[k])) : 0.f;
-  }
-  return dz;
-}
-
-// d/dz of -softplus(z): the negated gradient through softplus.
-template <typename T>
-__device__ __forceinline__ Vec neg_softplus_bwd(const Vec& z, const Vec& g) {
-  Vec dz;
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    dz.on[k] = z.on[k];
-    dz.v[k] = z.on[k] ? round_t<T>(softplus_grad(z.v[k], -g.v[k])) : 0.f;
-  }
-  return dz;
-}
-
-template <typename T>
+template <int SEG, int PER, typename T>
 __global__ void __launch_bounds__(256) prologue_bwd_kernel(
     const T* __restrict__ Z, int64_t N, Dims D, const T* __restrict__ gA, const T* __restrict__ gR,
     const T* __restrict__ gcQf, const T* __restrict__ glgA, const T* __restrict__ glgB,
     const T* __restrict__ glgQ, const T* __restrict__ gh0, const T* __restrict__ gcB,
     const T* __restrict__ gcQ, T* __restrict__ dZ) {
-  const int lane = threadIdx.x & 31;
-  const int64_t slots = N * (D.nh + 1);
+  constexpr int HPW = 32 / SEG;
+  const int lane = threadIdx.x & 31, seg = lane / SEG, ls = lane % SEG;
+  const int tpr = tasks_per_row<SEG>(D.nh);
+  const int64_t tasks = N * tpr;
   const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < slots; w += stride) {
-    const int64_t n = w / (D.nh + 1);
-    const int h = static_cast<int>(w % (D.nh + 1));
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < tasks; w += stride) {
+    const int64_t n = w / tpr;
+    const int task = static_cast<int>(w % tpr);
     const T* zr = Z + n * D.W;
     T* dr = dZ + n * D.W;
-    if (h == D.nh) {
+    if (task == tpr - 1) {
       const T* zb = zr + D.nh * D.Hs;
-      Vec cb = load_vec(zb, D.rB, lane), y, dcb;
-      const float rs = l2norm_fwd<T>(cb, y);
-      l2norm_bwd<T>(cb, rs, grad_or_zero(gcB ? gcB + n * D.rB : nullptr, D.rB, lane), dcb);
-      store_vec(dr + D.nh * D.Hs, dcb);
-      const Vec cq = load_vec(zb + D.rB, D.rQ, lane);
-      store_vec(dr + D.nh * D.Hs + D.rB,
-                softplus_l2norm_bwd<T, false>(cq, grad_or_zero(gcQ ? gcQ + n * D.rQ : nullptr, D.rQ, lane)));
+      Vec<2> cb = load_vec<32, 2>(zb, D.rB, lane), y, dcb;
+      const float rs = l2norm_fwd<32, 2, T>(cb, y);
+      l2norm_bwd<32, 2, T>(cb, rs, grad_or_zero<32, 2>(gcB ? gcB + n * D.rB : nullptr, D.rB, lane), dcb);
+      store_vec<32, 2>(dr + D.nh * D.Hs, dcb, lane);
+      const Vec<2> cq = load_vec<32, 2>(zb + D.rB, D.rQ, lane);
+      store_vec<32, 2>(dr + D.nh * D.Hs + D.rB,
+                       softplus_l2norm_bwd<32, 2, T, false>(
+                           cq, grad_or_zero<32, 2>(gcQ ? gcQ + n * D.rQ : nullptr, D.rQ, lane)),
+                       lane);
       continue;
     }
-    const T* z = zr + (int64_t)h * D.Hs;
-    T* dz = dr + (int64_t)h * D.Hs;
-    const int64_t p = n * D.nh + h;
-    store_vec(dz, grad_or_zero(gh0 ? gh0 + p * D.d : nullptr, D.d, lane));
+    const int h = task * HPW + seg;
+    const bool valid = h < D.nh;
+    const int nd = valid ? D.d : 0, ndu = valid ? D.du : 0;
+    const T* z = zr + (int64_t)(valid ? h : 0) * D.Hs;
+    T* dz = dr + (int64_t)(valid ? h : 0) * D.Hs;
+    const int64_t p = valid ? n * D.nh + h : 0;
+    auto grad = [&](const T* g, int64_t off, int len) {
+      return grad_or_zero<SEG, PER>(g ? g + off : nullptr, len, ls);
+    };
+    store_vec<SEG, PER>(dz, grad(gh0, p * D.d, nd), ls);
     {
-      Vec a = load_vec(z + D.oA, D.d, lane), y, da;
-      const float rs = l2norm_fwd<T>(a, y);
-      l2norm_bwd<T>(a, rs, grad_or_zero(gA ? gA + p * D.d : nullptr, D.d, lane), da);
-      store_vec(dz + D.oA, da);
+      Vec<PER> a = load_vec<SEG, PER>(z + D.oA, nd, ls), y, da;
+      const float rs = l2norm_fwd<SEG, PER, T>(a, y);
+      l2norm_bwd<SEG, PER, T>(a, rs, grad(gA, p * D.d, nd), da);
+      store_vec<SEG, PER>(dz + D.oA, da, ls);
     }
-    store_vec(dz + D.oR, softplus_l2norm_bwd<T, true>(load_vec(z + D.oR, D.du, lane),
-                                                        grad_or_zero(gR ? gR + p * D.du : nullptr, D.du, lane)));
-    store_vec(dz + D.oQf, softplus_l2norm_bwd<T, false>(load_vec(z + D.oQf, D.d, lane),
-                                                          grad_or_zero(gcQf ? gcQf + p * D.d : nullptr, D.d, lane)));
-    if (lane == 0) {
+    store_vec<SEG, PER>(dz + D.oR, softplus_l2norm_bwd<SEG, PER, T, true>(
+                                       load_vec<SEG, PER>(z + D.oR, ndu, ls), grad(gR, p * D.du, ndu)), ls);
+    store_vec<SEG, PER>(dz + D.oQf, softplus_l2norm_bwd<SEG, PER, T, false>(
+                                        load_vec<SEG, PER>(z + D.oQf, nd, ls), grad(gcQf, p * D.d, nd)), ls);
+    if (valid && ls == 0) {
       const float g = glgA ? ldf(glgA + p) : 0.f;
       stf(dz + D.oGA, round_t<T>(softplus_grad(ldf(z + D.oGA), -g)));
     }
-    store_vec(dz + D.oGB, neg_softplus_bwd<T>(load_vec(z + D.oGB, D.du, lane),
-                                               grad_or_zero(glgB ? glgB + p * D.du : nullptr, D.du, lane)));
-    store_vec(dz + D.oGQ, neg_softplus_bwd<T>(load_vec(z + D.oGQ, D.d, lane),
-                                               grad_or_zero(glgQ ? glgQ + p * D.d : nullptr, D.d, lane)));
+    store_vec<SEG, PER>(dz + D.oGB, neg_softplus_bwd<PER, T>(load_vec<SEG, PER>(z + D.oGB, ndu, ls),
+                                                             grad(glgB, p * D.du, ndu)), ls);
+    store_vec<SEG, PER>(dz + D.oGQ, neg_softplus_bwd<PER, T>(load_vec<SEG, PER>(z + D.oGQ, nd, ls),
+                                                             grad(glgQ, p * D.d, nd)), ls);
   }
 }
 
 int check_dims(int64_t N, int nh, int d, int du, int rB, int rQ, int dtype) {
   if (N < 0 || nh < 1 || d < 1 || du < 1 || rB < 1 || rQ < 1)
     return ttc::set_error(TTC_ERR_INVALID, "prologue: sizes must be positive");
-  if (d > 32 * kPer || du > 32 * kPer || rB > 32 * kPer || rQ > 32 * kPer)
+  if (d > kMaxLen || du > kMaxLen || rB > kMaxLen || rQ > kMaxLen)
     return ttc::set_error(TTC_ERR_UNSUPPORTED, "prologue: h_dim, u_dim and ranks must be <= 64");
   if (dtype != TTC_DTYPE_F32 && dtype != TTC_DTYPE_BF16)
     return ttc::set_error(TTC_ERR_INVALID, "prologue: dtype must be TTC_DTYPE_F32 or TTC_DTYPE_BF16");
   return TTC_OK;
 }
 
-unsigned grid_for(int64_t N, int nh) {
-  const int64_t warps = N * (nh + 1);
-  int64_t blocks = (warps + 7) / 8;
+unsigned grid_for(int64_t tasks) {
+  const int64_t blocks = (tasks + 7) / 8;
   const int64_t cap = 148 * 32;  // grid-stride beyond 32 CTAs per SM
   return static_cast<unsigned>(blocks < cap ? blocks : cap);
 }
@@ -312,6 +337,49 @@ int launched(const char* what) {
   return ttc::set_error(TTC_ERR_CUDA, buf);
 }
 
+template <int SEG, int PER, typename T>
+int fwd_launch(const void* Z, int64_t N, const Dims& D, void* const* o, cudaStream_t st) {
+  const unsigned grid = grid_for(N * (int64_t)((D.nh + 32 / SEG - 1) / (32 / SEG) + 1));
+  prologue_fwd_kernel<SEG, PER, T><<<grid, 256, 0, st>>>((const T*)Z, N, D, (T*)o[0], (T*)o[1], (T*)o[2],
+                                                         (T*)o[3], (T*)o[4], (T*)o[5], (T*)o[6], (T*)o[7],
+                                                         (T*)o[8]);
+  return launched("prologue_fwd_kernel launch");
+}
+
+template <int SEG, int PER, typename T>
+int bwd_launch(const void* Z, int64_t N, const Dims& D, const void* const* g, void* dZ, cudaStream_t st) {
+  const unsigned grid = grid_for(N * (int64_t)((D.nh + 32 / SEG - 1) / (32 / SEG) + 1));
+  prologue_bwd_kernel<SEG, PER, T><<<grid, 256, 0, st>>>(
+      (const T*)Z, N, D, (const T*)g[0], (const T*)g[1], (const T*)g[2], (const T*)g[3], (const T*)g[4],
+      (const T*)g[5], (const T*)g[6], (const T*)g[7], (const T*)g[8], (T*)dZ);
+  return launched("prologue_bwd_kernel launch");
+}
+
+// Segment shape for the head-vector length max(d, du): two heads per warp up to 16, one up
+// to 32, two elements per lane up to 64.
+int shape_of(const Dims& D) {
+  const int len = D.d > D.du ? D.d : D.du;
+  return len <= 16 ? 0 : (len <= 32 ? 1 : 2);
+}
+
+template <typename T>
+int fwd_typed(const void* Z, int64_t N, const Dims& D, void* const* o, cudaStream_t st) {
+  switch (shape_of(D)) {
+    case 0: return fwd_launch<16, 1, T>(Z, N, D, o, st);
+    case 1: return fwd_launch<32, 1, T>(Z, N, D, o, st);
+    default: return fwd_launch<32, 2, T>(Z, N, D, o, st);
+  }
+}
+
+template <typename T>
+int bwd_typed(const void* Z, int64_t N, const Dims& D, const void* const* g, void* dZ, cudaStream_t st) {
+  switch (shape_of(D)) {
+    case 0: return bwd_launch<16, 1, T>(Z, N, D, g, dZ, st);
+    case 1: return bwd_launch<32, 1, T>(Z, N, D, g, dZ, st);
+    default: return bwd_launch<32, 2, T>(Z, N, D, g, dZ, st);
+  }
+}
+
 }  // namespace
 
 extern "C" int ttc_prologue_fwd(const void* Z, int64_t N, int nh, int d, int du, int rB, int rQ, int dtype,
@@ -322,18 +390,9 @@ extern "C" int ttc_prologue_fwd(const void* Z, int64_t N, int nh, int d, int du,
   if (!Z || !A_diag || !R_inv || !coeff_Qf || !lgA || !lgB || !lgQ || !h0 || !coeff_B || !coeff_Q)
     return ttc::set_error(TTC_ERR_INVALID, "prologue_fwd: null pointer");
   const Dims D(nh, d, du, rB, rQ);
+  void* const o[9] = {A_diag, R_inv, coeff_Qf, lgA, lgB, lgQ, h0, coeff_B, coeff_Q};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned grid = grid_for(N, nh);
-  if (dtype == TTC_DTYPE_F32) {
-    using T = float;
-    prologue_fwd_kernel<T><<<grid, 256, 0, st>>>((const T*)Z, N, D, (T*)A_diag, (T*)R_inv, (T*)coeff_Qf,
-                                                 (T*)lgA, (T*)lgB, (T*)lgQ, (T*)h0, (T*)coeff_B, (T*)coeff_Q);
-  } else {
-    using T = __nv_bfloat16;
-    prologue_fwd_kernel<T><<<grid, 256, 0, st>>>((const T*)Z, N, D, (T*)A_diag, (T*)R_inv, (T*)coeff_Qf,
-                                                 (T*)lgA, (T*)lgB, (T*)lgQ, (T*)h0, (T*)coeff_B, (T*)coeff_Q);
-  }
-  return launched("prologue_fwd_kernel launch");
+  return dtype == TTC_DTYPE_F32 ? fwd_typed<float>(Z, N, D, o, st) : fwd_typed<__nv_bfloat16>(Z, N, D, o, st);
 }
 
 extern "C" int ttc_prologue_bwd(const void* Z, int64_t N, int nh, int d, int du, int rB, int rQ, int dtype,
@@ -344,18 +403,8 @@ extern "C" int ttc_prologue_bwd(const void* Z, int64_t N, int nh, int d, int du,
   if (N == 0) return TTC_OK;
   if (!Z || !dZ) return ttc::set_error(TTC_ERR_INVALID, "prologue_bwd: null pointer");
   const Dims D(nh, d, du, rB, rQ);
+  const void* const g[9] = {g_A_diag, g_R_inv, g_coeff_Qf, g_lgA, g_lgB, g_lgQ, g_h0, g_coeff_B, g_coeff_Q};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned grid = grid_for(N, nh);
-  if (dtype == TTC_DTYPE_F32) {
-    using T = float;
-    prologue_bwd_kernel<T><<<grid, 256, 0, st>>>(
-        (const T*)Z, N, D, (const T*)g_A_diag, (const T*)g_R_inv, (const T*)g_coeff_Qf, (const T*)g_lgA,
-        (const T*)g_lgB, (const T*)g_lgQ, (const T*)g_h0, (const T*)g_coeff_B, (const T*)g_coeff_Q, (T*)dZ);
-  } else {
-    using T = __nv_bfloat16;
-    prologue_bwd_kernel<T><<<grid, 256, 0, st>>>(
-        (const T*)Z, N, D, (const T*)g_A_diag, (const T*)g_R_inv, (const T*)g_coeff_Qf, (const T*)g_lgA,
-        (const T*)g_lgB, (const T*)g_lgQ, (const T*)g_h0, (const T*)g_coeff_B, (const T*)g_coeff_Q, (T*)dZ);
-  }
-  return launched("prologue_bwd_kernel launch");
+  return dtype == TTC_DTYPE_F32 ? bwd_typed<float>(Z, N, D, g, dZ, st)
+                                : bwd_typed<__nv_bfloat16>(Z, N, D, g, dZ, st);
 }
