@@ -118,3 +118,34 @@ def test_four_dim_input_convention(cpu_prologue):
     y3 = layer(x.reshape(2, 6, 8), T=4).reshape(2, 2, 3, 6)
     assert y4.shape == (2, 2, 3, 6)
     assert torch.equal(y4, y3)
+
+
+@pytest.mark.parametrize("K", [4096, 300])
+def test_chunked_weight_gradients_match_torch(K):
+    """ttc_b200.reductions: linear / lowrank_mix give F.linear / einsum values and gradients
+    (K-chunked batched weight-gradient GEMM when K splits, a plain GEMM otherwise)."""
+    import torch.nn.functional as F
+    from ttc_b200.reductions import _chunks, linear, lowrank_mix
+    assert (_chunks(K) > 1) == (K == 4096)
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(K, 12, dtype=torch.float64, generator=g)
+    w = torch.randn(7, 12, dtype=torch.float64, generator=g)
+    b = torch.randn(7, dtype=torch.float64, generator=g)
+    gy = torch.randn(K, 7, dtype=torch.float64, generator=g)
+    ins = [t.clone().requires_grad_(True) for t in (x, w, b)]
+    ref = [t.clone().requires_grad_(True) for t in (x, w, b)]
+    linear(*ins).backward(gy)
+    F.linear(*ref).backward(gy)
+    for a, r in zip(ins, ref):
+        assert torch.allclose(a.grad, r.grad, rtol=1e-12, atol=1e-10)
+    c = torch.randn(K // 4, 4, 5, dtype=torch.float64, generator=g)
+    basis = torch.randn(5, 3, 6, dtype=torch.float64, generator=g)
+    go = torch.randn(K // 4, 4, 3, 6, dtype=torch.float64, generator=g)
+    a1, a2 = c.clone().requires_grad_(True), basis.clone().requires_grad_(True)
+    r1, r2 = c.clone().requires_grad_(True), basis.clone().requires_grad_(True)
+    out = lowrank_mix(a1, a2)
+    assert torch.allclose(out, torch.einsum("...r,rmn->...mn", c, basis), rtol=1e-12)
+    out.backward(go)
+    torch.einsum("...r,rmn->...mn", r1, r2).backward(go)
+    assert torch.allclose(a1.grad, r1.grad, rtol=1e-12, atol=1e-10)
+    assert torch.allclose(a2.grad, r2.grad, rtol=1e-12, atol=1e-10)

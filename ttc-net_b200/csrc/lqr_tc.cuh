@@ -81,14 +81,15 @@ __device__ __forceinline__ bool slot_sync_or(int id, int count, bool pred) {
 // further K step of 8 is 2*N*16 bytes further on: a constant added to the descriptor's
 // start-address field.  Called by one elected lane of a warp-uniform branch, so the
 // descriptors stay in uniform registers.
-template <int N, int K>
+// ACC_IN: the accumulator already holds a value to add to (the first MMA accumulates).
+template <int N, int K, bool ACC_IN = false>
 __device__ __forceinline__ void issue_3xtf32(uint32_t acc, uint32_t a_hi, uint32_t a_lo,
                                              uint64_t dh, uint64_t dl) {
   constexpr uint32_t idesc = tc::idesc_tf32(N);
   constexpr uint64_t step = (2 * N * 16) >> 4;
 #pragma unroll
   for (int kk = 0; kk < K / 8; ++kk) {
-    tc::mma_tf32_ts(acc, a_lo + kk * 8, dh + kk * step, idesc, kk > 0);
+    tc::mma_tf32_ts(acc, a_lo + kk * 8, dh + kk * step, idesc, (kk > 0 || ACC_IN) ? 1 : 0);
     tc::mma_tf32_ts(acc, a_hi + kk * 8, dl + kk * step, idesc, 1);
   }
 #pragma unroll
@@ -114,11 +115,15 @@ struct NoOverlap {
   __device__ __forceinline__ void operator()() const {}
 };
 
+// With `acc_init` (this thread's row, N columns) the accumulator starts from it, so `out`
+// returns acc_init + A * Op^T: the tensor core does the addition.
 template <int C, int N, int K, typename Overlap = NoOverlap>
 __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], float (&out)[N],
-                                             uint64_t dh, uint64_t dl, Overlap&& overlap = Overlap()) {
+                                             uint64_t dh, uint64_t dl, Overlap&& overlap = Overlap(),
+                                             const float (*acc_init)[N] = nullptr) {
   static_assert(C == K && C % 8 == 0, "A width must equal K (a multiple of 8)");
   tc::tmem_st<C>(X.my_hi, a);
+  if (acc_init != nullptr) tc::tmem_st<N>(X.my_acc, *acc_init);
 #pragma unroll
   for (int k = 0; k < C; k += 8) {
     tc::tmem_st8(X.my_lo + k, tc::tf32_residual(a[k]), tc::tf32_residual(a[k + 1]),
@@ -135,7 +140,11 @@ __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], fl
   tc::fence_after_sync();
   if (X.mma_warp) {
     if (tc::elect_one()) {
-      issue_3xtf32<N, K>(X.t_acc, X.t_hi, X.t_lo, dh, dl);
+      if (acc_init != nullptr) {
+        issue_3xtf32<N, K, true>(X.t_acc, X.t_hi, X.t_lo, dh, dl);
+      } else {
+        issue_3xtf32<N, K>(X.t_acc, X.t_hi, X.t_lo, dh, dl);
+      }
       tc::mma_commit(X.mbar);
     }
     __syncwarp();
@@ -258,16 +267,20 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
       t[4 * j4 + 2] *= e.z;
       t[4 * j4 + 3] *= e.w;
     }
-    // Y1 = (Y1 + c B^T) / A
+    // Y1 = (Y1 + c B^T) / A.  At d = 16 the sum is formed in the accumulator, started from
+    // Y1 (one TMEM store instead of d adds: 1 % faster); at d >= 32 the wider store costs more
+    // than it saves.
     float u[D];
-    if (!tile_product<DU, D, DU>(X, t, u, o2h, o2l)) return false;
+    constexpr bool kAccY1 = D <= 16;
+    if (!tile_product<DU, D, DU>(X, t, u, o2h, o2l, NoOverlap(), kAccY1 ? &y1 : nullptr)) return false;
 #pragma unroll
     for (int k4 = 0; k4 < D / 4; ++k4) {
       const float4 ia = v4[V::kIA / 4 + k4];
-      y1[4 * k4 + 0] = (y1[4 * k4 + 0] + u[4 * k4 + 0]) * ia.x;
-      y1[4 * k4 + 1] = (y1[4 * k4 + 1] + u[4 * k4 + 1]) * ia.y;
-      y1[4 * k4 + 2] = (y1[4 * k4 + 2] + u[4 * k4 + 2]) * ia.z;
-      y1[4 * k4 + 3] = (y1[4 * k4 + 3] + u[4 * k4 + 3]) * ia.w;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float s = kAccY1 ? u[4 * k4 + c] : y1[4 * k4 + c] + u[4 * k4 + c];
+        y1[4 * k4 + c] = s * (c == 0 ? ia.x : c == 1 ? ia.y : c == 2 ? ia.z : ia.w);
+      }
     }
     if (!last) {
       // Y2 = Y2 A + ((Y1 Dq) Q) Dq

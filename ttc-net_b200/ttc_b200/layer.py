@@ -18,6 +18,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .prologue import prologue
+from .reductions import linear, lowrank_mix
 from .solver import (LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_mix_with_status,
                      lqr_solve_with_status, mix_available)
 from . import _lib
@@ -82,14 +83,15 @@ class TTCLayer(nn.Module):
         """Prologue (ttc_layer.py:104-135) up to, not including, the Q_f mixture: rows
         [N, in_dim] -> (A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0) with
         Q_f = sum_r coeff_Qf[..., r] Q_basis[r].  The elementwise part (split, l2norm,
-        softplus, clamp, negation) is one CUDA kernel each way (``prologue``); the low-rank
-        B / Q mixtures are cuBLAS einsums."""
+        softplus, clamp, negation) is one CUDA kernel each way (``prologue``); in_proj and
+        the low-rank B / Q mixtures are cuBLAS GEMMs with K-chunked weight gradients
+        (``reductions``)."""
         nh, d, du = self.num_heads, self.h_dim, self.u_dim
         A_diag, R_inv_diag, coeff_Qf, log_gamma_A, log_gamma_B, log_gamma_Q, h0, coeff_B, coeff_Q = \
-            prologue(self.in_proj(x2d), nh, d, du, self.b_rank, self.q_rank)
-        B = torch.einsum("...r,rmn->...mn", coeff_B, self.Bs)
+            prologue(linear(x2d, self.in_proj.weight, self.in_proj.bias), nh, d, du, self.b_rank, self.q_rank)
+        B = lowrank_mix(coeff_B, self.Bs)
         if self.q_reparam == "plain":
-            Q = torch.einsum("...r,rmn->...mn", coeff_Q, self.Qs)
+            Q = lowrank_mix(coeff_Q, self.Qs)
             Q_basis = self.Qs
         else:
             Q = torch.einsum("...r,rmn,rkn->...mk", coeff_Q, self.Qs, self.Qs) / math.sqrt(d)
@@ -105,7 +107,7 @@ class TTCLayer(nn.Module):
     @staticmethod
     def _materialise(parts):
         A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0 = parts
-        Q_f = torch.einsum("...r,rmn->...mn", coeff_Qf, Q_basis)
+        Q_f = lowrank_mix(coeff_Qf, Q_basis)
         return (A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0)
 
     def solver_inputs(self, x2d: torch.Tensor):
@@ -144,4 +146,5 @@ class TTCLayer(nn.Module):
             h0_norm = torch.linalg.norm(x0, dim=-1, ord=2).detach()
             u_norm = torch.linalg.norm(u, dim=-1, ord=2).detach()
             u = u / u_norm[..., None] * h0_norm[..., None]
-        return self.out_proj(u.reshape(bs, seq_len, -1))
+        y = linear(u.reshape(bs * seq_len, -1), self.out_proj.weight, self.out_proj.bias)
+        return y.view(bs, seq_len, -1)
