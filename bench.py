@@ -56,6 +56,11 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--workload", default="layer", choices=["layer", "traj"],
+                    help="layer: the headline TTCLayer step; traj: closed-loop trajectories "
+                         "(lqr_trajectory) of the config's solver inputs, one GPU")
+    ap.add_argument("--traj-rows", type=int, default=0,
+                    help="rows of the trajectory workload (0: the config's per-GPU batch)")
     return ap.parse_args(argv)
 
 
@@ -281,6 +286,10 @@ def main(argv=None):
     if args.batch:
         import dataclasses
         cfg = dataclasses.replace(cfg, B=args.batch)
+    if args.workload == "traj":
+        if args.warmup < 3:
+            raise SystemExit("--warmup must be >= 3")
+        return traj_bench(args, cfg)
     if args.impl == "reference":
         return reference_arm(args, cfg)
     if args.warmup < 3:
@@ -449,6 +458,121 @@ def main(argv=None):
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------------- trajectories
+def traj_model(cfg, es):
+    """Algorithmic FLOPs and HBM bytes per problem of the rollout kernel (all outputs and the
+    affine step-0 term requested)."""
+    d = du = cfg.h_dim
+    T, nh = cfg.T, cfg.H
+    flops = T * 2 * (d * d + 2 * d * du) - 2 * d * d + 2 * d * du + T * 4 * du + 2 * d * d
+    out_b = T * du * es + 2 * T * d * 4 + d * 4 + 4
+    in_b = (4 * d + 3 * du + 1) * es + d * 4 + d * du * 4 + d * d * es + (d * du + d * d) * es / nh
+    return flops, out_b + in_b
+
+
+def traj_bench(args, cfg):
+    """Closed-loop trajectories of every LQR problem of the config's per-GPU batch: one step =
+    lqr_trajectory (ttc_lqr_fwd + ttc_lqr_rollout) with actions, states, costates, lambda0, cost
+    and an affine step-0 cost, on solver inputs made by the layer's prologue."""
+    if args.gpus != 1 or int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("--workload traj runs on one GPU")
+    from ttc_b200 import lqr_trajectory
+    from ttc_b200.solver import KernelTimer, set_kernel_timer
+    dtype = torch.bfloat16 if cfg.dtype == "bfloat16" else torch.float32
+    es = 2 if dtype == torch.bfloat16 else 4
+    flops, nbytes = traj_model(cfg, es)
+    rows = args.traj_rows or cfg.rows
+    while rows > cfg.H and rows * cfg.H * nbytes > (48 << 30):
+        rows //= 2
+    problems = rows * cfg.H
+    if args.impl == "reference":
+        from oracle import ttc_oracle as O
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        layer = O.TTCLayerOracle(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank)
+        layer.load_state_dict({k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()})
+        sample = min(rows, 256)
+        x = torch.from_numpy(layer_input(cfg, sample, seed=3)[0])
+        with torch.no_grad():
+            ins = layer.solver_inputs(x)
+        r0 = torch.randn(ins[0].shape[0], cfg.H, cfg.h_dim)
+        vals = []
+        for k in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            O.riccati_trajectory(*ins, cfg.T, r_traj=torch.nn.functional.pad(
+                r0[:, :, None], (0, 0, 0, cfg.T - 1)))
+            if k >= args.warmup:
+                vals.append(ins[0].shape[0] * cfg.H / (time.perf_counter() - t0))
+        v = statistics.median(vals)
+        print(json.dumps({
+            "impl": "reference", "metric": "LQR trajectories/s", "value": v, "unit": "trajectories/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "dtype": "f32", "config": {"workload": f"{cfg.name} trajectories, sample of {ins[0].shape[0]} rows"},
+            "cpu_baseline": {"value": v, "unit": "trajectories/s", "cores": threads, "kind": "port",
+                             "sample": f"{ins[0].shape[0] * cfg.H} problems per step: oracle riccati "
+                                       "trajectory + states/costates/cost"}}), flush=True)
+        return
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    layer = make_layer(cfg, device, dtype)
+    x = torch.from_numpy(layer_input(cfg, rows, seed=3)[0]).to(device, dtype)
+    with torch.no_grad():
+        ins = layer.solver_inputs(x)
+    r0 = torch.randn(rows, cfg.H, cfg.h_dim, device=device).to(dtype)
+    want = dict(return_states=True, return_costates=True, return_lambda0=True, return_cost=True)
+    for _ in range(args.warmup):
+        out = lqr_trajectory(*ins, cfg.T, r0=r0, **want)
+        del out
+    torch.cuda.synchronize()
+    timer = KernelTimer()
+    with ClockSampler(gpu_selector(0)) as clocks:
+        torch.cuda.synchronize()
+        set_kernel_timer(timer)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            out = lqr_trajectory(*ins, cfg.T, r0=r0, **want)
+            del out
+        end.record()
+        torch.cuda.synchronize()
+        set_kernel_timer(None)
+    ms = start.elapsed_time(end)
+    kern = timer.durations_ms()
+    roll_ms = statistics.mean(kern["ttc_lqr_rollout"])
+    fwd_ms = statistics.mean(kern["ttc_lqr_fwd"])
+    peaks = {}
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    clock_summary = clocks.summary()
+    sm_max = clock_summary.get("sm_max_mhz") or 1965.0
+    fp32_peak = SM_COUNT_B200 * FP32_LANES_PER_SM * 2 * sm_max * 1e6 / 1e12
+    gbs = nbytes * problems / (roll_ms / 1e3) / 1e9
+    tfl = flops * problems / (roll_ms / 1e3) / 1e12
+    print(json.dumps({
+        "metric": "LQR trajectories/s", "value": problems * args.steps / (ms / 1e3),
+        "unit": "trajectories/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32" if dtype == torch.float32 else "bf16 inputs, f32 state",
+        "data": "synthetic (layer prologue of seeded N(0,1) x; r0 ~ N(0,1))",
+        "config": {"workload": f"{cfg.name} trajectories: {rows} rows x {cfg.H} heads, d=du={cfg.h_dim}, "
+                               f"T={cfg.T}, actions + states + costates + lambda0 + cost, affine r0",
+                   "problems": problems, "l2": "outputs of one step far larger than L2"},
+        "roofline": {"kernel": "ttc_lqr_rollout", "bound": "hbm", "achieved": gbs, "peak": hbm,
+                     "unit": "GB/s", "frac": gbs / hbm, "bytes_per_problem": nbytes,
+                     "launch_ms": roll_ms, "fp32_tflops": tfl, "frac_fp32_peak": tfl / fp32_peak,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+        "kernels": {"ttc_lqr_fwd": {"launches": len(kern["ttc_lqr_fwd"]), "mean_ms": fwd_ms},
+                    "ttc_lqr_rollout": {"launches": len(kern["ttc_lqr_rollout"]), "mean_ms": roll_ms}},
+        "clocks": clock_summary,
+        "gpu_launches": sum(len(v) for v in kern.values()),
+    }), flush=True)
 
 
 def load_traffic(workload):

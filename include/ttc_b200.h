@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define TTC_ABI_VERSION 4
+#define TTC_ABI_VERSION 5
 
 #define TTC_DTYPE_F32 0
 #define TTC_DTYPE_BF16 1
@@ -47,6 +47,7 @@ extern "C" {
 #define TTC_STATUS_BWD_UNSTABLE 4 /* any of the nine gradients    (ttc/solvers/fused_lqr.py:243-246) */
 #define TTC_STATUS_U_NAN 8        /* NaN in u                     (ttc/layers/ttc_layer.py:139-140)  */
 #define TTC_STATUS_MMA_TIMEOUT 16 /* a tensor-core MMA did not complete within the kernel's poll limit */
+#define TTC_STATUS_TRAJ_NONFINITE 32 /* NaN or Inf in a trajectory written by ttc_lqr_rollout */
 
 /* Option bits (`flags` argument). */
 #define TTC_FLAG_INV_GUARD 1 /* Y1 + 1e-6 I after the sweep, before the solve: the reference's
@@ -108,6 +109,32 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
                 void* grad_A, void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_Q_f,
                 void* grad_lgA, void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status,
                 void* stream);
+
+/*
+ * Closed-loop trajectory of a solved problem, with an optional affine action cost on step 0.
+ * Replaces solve_traj_actions(..., r_traj, return_traj=True) and solve_traj_states
+ * (ttc/solvers/lin_solver_lqr.py:13-110,113-212) for r_traj zero after step 0 -- the form
+ * the reference's kkt backward solves (ttc/solvers/torch_lqr.py:41-47) and the affine term
+ * of its symplectic sweep (IS_AFFINE, y3 = Y3 r; ttc/solvers/symplectic_iter.py:211-238,
+ * 336-345) -- integrated forward in time as the primal half of its adjoint
+ * (symplectic_iter.py:766-845).
+ *
+ * Inputs: the forward's nine inputs (activation dtype; Q_f is read only for the cost and
+ *   may be NULL without it), the forward's lam0 and M (float32), and r0 [N,nh,du]
+ *   (activation dtype; NULL = no affine term, M may then be NULL).
+ *   lambda0 = lam0 + M r0; u_0 gets the extra -R_inv r0.
+ * Outputs: u_traj [N,nh,T,du] (activation dtype; u_t, t = 0..T-1); float32, each may be
+ *   NULL: h_traj [N,nh,T,d] (h_{t+1}), lam_traj [N,nh,T,d] (lambda_{t+1}, the costates of
+ *   solve_traj_states), lam0_out [N,nh,d] (lambda0), cost [N,nh] (the total cost
+ *   sum_t 0.5 h_{t+1}^T Q_t h_{t+1} + 0.5 u_t^T R_t u_t + r_t^T u_t, Q_{T-1} = Q_f).
+ * status: TTC_STATUS_TRAJ_NONFINITE if any value written is NaN or Inf.
+ */
+int ttc_lqr_rollout(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                    const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
+                    const void* log_gamma_Q, const void* h0, const float* lam0, const float* M,
+                    const void* r0, int64_t N, int nh, int d, int du, int T, int dtype,
+                    void* u_traj, float* h_traj, float* lam_traj, float* lam0_out, float* cost,
+                    int* status, void* stream);
 
 /* ttc_lqr_fwd with Q_f given as the layer's rank-rQ mixture (ttc_layer.py:119-123,
  * Q_f[n,h] = sum_r coeff_Qf[n,h,r] Q_basis[r]) instead of the [N,nh,d,d] tensor:

@@ -181,6 +181,16 @@ def traj_states(u_traj, A_t, B_t, Q_t, h0):
     return states, costates, lam0
 
 
+def traj_cost(u_traj, states, Q_t, R_t, r_traj=None):
+    """Total cost of a trajectory (lin_solver_lqr.py:55-68):
+    sum_t 0.5 h_{t+1}^T Q_t h_{t+1} + 0.5 u_t^T diag(R_t) u_t + r_t^T u_t.  Returns [M]."""
+    qh = (Q_t @ states[..., None])[..., 0]
+    c = 0.5 * (states * qh).sum(-1) + 0.5 * (u_traj * R_t * u_traj).sum(-1)
+    if r_traj is not None:
+        c = c + (r_traj * u_traj).sum(-1)
+    return c.sum(-1)
+
+
 def _flat(A_t, B_t, Q_t, R_t):
     N, nh, T, d = A_t.shape
     du = B_t.shape[-1]
@@ -400,6 +410,73 @@ def fused_solve(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q,
 
 
 SOLVERS = {"riccati": riccati_solve, "kkt": kkt_solve, "fused": fused_solve}
+
+
+# ---------------------------------------------------------------------------
+# Trajectories (solve_traj_actions(return_traj=True) + solve_traj_states)
+# ---------------------------------------------------------------------------
+def riccati_trajectory(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
+                       r_traj=None, solve_dtype=torch.float32):
+    """Closed-loop trajectory by the backward Riccati sweep and its rollout
+    (lin_solver_lqr.py:113-212 with return_traj=True), then states, costates, lambda0 and
+    total cost (solve_traj_states, lin_solver_lqr.py:13-110), on the time-varying system of
+    torch_lqr.py:65-91.  r_traj [N,nh,T,du] or None.
+    Returns (u_traj [N,nh,T,du], states [N,nh,T,d], costates [N,nh,T,d], lambda0 [N,nh,d],
+    cost [N,nh])."""
+    N, nh, d = A_diag.shape
+    du = B.shape[-1]
+    A_t, B_t, Q_t, R_t = _flat(*time_varying_system(
+        A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, T))
+    r = None if r_traj is None else r_traj.reshape(-1, T, du)
+    u = riccati_actions(A_t, B_t, Q_t, R_t, h0.reshape(-1, d), r_traj=r, return_traj=True,
+                        solve_dtype=solve_dtype)
+    hs, lam, lam0 = traj_states(u, A_t, B_t, Q_t, h0.reshape(-1, d))
+    cost = traj_cost(u, hs, Q_t, R_t, r)
+    return (u.reshape(N, nh, T, du), hs.reshape(N, nh, T, d), lam.reshape(N, nh, T, d),
+            lam0.reshape(N, nh, d), cost.reshape(N, nh))
+
+
+def fused_trajectory(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
+                     r0=None, inv_guard: bool = False):
+    """The trajectory as the CUDA path computes it: the symplectic forward (fused_forward)
+    gives lambda0 = P h0 and M = Y1^-1 Y3; an affine action cost r0 [N,nh,du] on step 0 adds
+    M r0 to lambda0 (Y1^-1 y3 with the y3 = Y3 r of the reference's IS_AFFINE sweep,
+    symplectic_iter.py:211-238) and -R_inv r0 to u_0.  State and costate are then integrated
+    forward in time as in the primal half of the reference's adjoint
+    (symplectic_iter.py:766-845; the same recursion as fused_backward):
+        k > 0: lam -= Q_k h;  lam /= A_{k+1};  u_k = -R_inv B_{k+1}^T lam;  h = A_{k+1} h + B_{k+1} u_k
+    Returns (u_traj, states, costates, lambda0, cost) as riccati_trajectory."""
+    N, nh, d = A_diag.shape
+    du = B.shape[-1]
+    _, lam, Y1, _, Y3, _ = fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,
+                                         log_gamma_Q, h0, T, inv_guard=inv_guard)
+    if r0 is not None:
+        lam = lam + torch.linalg.solve(Y1, Y3 @ r0[..., None])[..., 0]
+    lam0 = lam
+    h = h0
+    Bh, Qh = B[:, None], Q[:, None]
+    us, hs, ls = [], [], []
+    cost = torch.zeros(N, nh, dtype=A_diag.dtype)
+    for k in range(T):
+        if k > 0:
+            e = torch.exp(log_gamma_Q * float(k))
+            qh = (e[..., :, None] * Qh * e[..., None, :] @ h[..., None])[..., 0]
+            lam = lam - qh
+            cost = cost + 0.5 * (h * qh).sum(-1)
+        At = 1.0 + A_diag * torch.exp(log_gamma_A * float(k + 1))[..., None]
+        lam = lam / At
+        Bt = Bh * torch.exp(log_gamma_B * float(k + 1))[:, :, None, :]
+        u = -R_inv * (Bt.transpose(-1, -2) @ lam[..., None])[..., 0]
+        if k == 0 and r0 is not None:
+            u = u - R_inv * r0
+            cost = cost + (r0 * u).sum(-1)
+        cost = cost + 0.5 * (u * u / R_inv).sum(-1)
+        h = h * At + (Bt @ u[..., None])[..., 0]
+        us.append(u)
+        hs.append(h)
+        ls.append(lam)
+    cost = cost + 0.5 * (h * (Q_f @ h[..., None])[..., 0]).sum(-1)
+    return torch.stack(us, 2), torch.stack(hs, 2), torch.stack(ls, 2), lam0, cost
 
 
 # ---------------------------------------------------------------------------

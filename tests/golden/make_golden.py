@@ -11,7 +11,8 @@ fla's Triton ``l2norm`` wrapper does not run on CPU tensors, so
 (x / sqrt(sum x^2 + 1e-6), fp32 compute, cast back -- fla/modules/l2norm.py:42).
 The Triton ``fused`` solver needs CUDA and is not run here.
 
-Usage:  python tests/golden/make_golden.py
+Usage:  python tests/golden/make_golden.py          (all fixtures)
+        python tests/golden/make_golden.py traj     (trajectory fixtures only)
 """
 from __future__ import annotations
 
@@ -30,7 +31,8 @@ REF = os.environ.get("TTC_REFERENCE_ROOT", "/root/reference")
 sys.path.insert(0, REF)
 os.environ.setdefault("TRITON_NO_AUTOTUNE", "1")
 import ttc.layers.ttc_layer as ref_layer_mod  # noqa: E402
-from ttc.solvers.torch_lqr import direct_lqr_solve, kkt_lqr_solve  # noqa: E402
+from ttc.solvers.lin_solver_lqr import solve_traj_actions, solve_traj_states  # noqa: E402
+from ttc.solvers.torch_lqr import _generate_parameters, direct_lqr_solve, kkt_lqr_solve  # noqa: E402
 
 
 def _l2norm_cpu(x, eps=1e-6):
@@ -121,6 +123,56 @@ def layer_case(name, cfg, rows, dtype=torch.float32, solver="kkt", backward=True
     print(f"{name}: {time.time() - t0:.1f}s", flush=True)
 
 
+def traj_case(name, args, T, seed_r):
+    """Closed-loop trajectories from the reference's lin_solver_lqr on the time-varying
+    system of torch_lqr._generate_parameters: without an affine term, with an affine action
+    cost r0 on step 0 only (the kkt backward's form), and with an affine cost on every step."""
+    t0 = time.time()
+    args = [torch.as_tensor(a).to(torch.float32) for a in args]
+    out = {n: _np(a) for n, a in zip(SOLVER_ARG_NAMES, args)}
+    out["T"] = np.array(T)
+    N, nh, d = args[0].shape
+    du = args[1].shape[-1]
+    A_t, B_t, Q_t, R_t = _generate_parameters(*args[:8], T)
+    A_t, B_t = A_t.reshape(-1, T, d), B_t.reshape(-1, T, d, du)
+    Q_t, R_t = Q_t.reshape(-1, T, d, d), R_t.reshape(-1, T, du)
+    h0 = args[8].reshape(-1, d)
+    rng = np.random.default_rng(seed_r)
+    r0 = torch.from_numpy(rng.standard_normal((N, nh, du))).float()
+    r_full = torch.from_numpy(rng.standard_normal((N, nh, T, du))).float()
+    r_step0 = torch.zeros(N * nh, T, du)
+    r_step0[:, 0] = r0.reshape(-1, du)
+    out["r0"] = _np(r0)
+    out["r_full"] = _np(r_full)
+    with torch.no_grad():
+        for tag, r in (("", None), ("_r0", r_step0), ("_rfull", r_full.reshape(-1, T, du))):
+            u = solve_traj_actions(A_t, B_t, Q_t, R_t, h0, r_traj=r, return_traj=True)
+            cost, hs, lam, lam0 = solve_traj_states(u, A_t, B_t, Q_t, R_t, h0, r_traj=r,
+                                                    return_states=True, return_costates=True,
+                                                    return_lambda0=True)
+            out["u_traj" + tag] = _np(u.reshape(N, nh, T, du))
+            out["states" + tag] = _np(hs.reshape(N, nh, T, d))
+            out["costates" + tag] = _np(lam.reshape(N, nh, T, d))
+            out["lambda0" + tag] = _np(lam0.reshape(N, nh, d))
+            out["cost" + tag] = _np(cost.reshape(N, nh))
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+    print(f"{name}: {time.time() - t0:.1f}s", flush=True)
+
+
+def traj_cases():
+    """Trajectory fixtures (solve_traj_actions(return_traj=True) + solve_traj_states)."""
+    from ttc.solvers.bench_lqr_solvers import generate_inputs
+    torch.manual_seed(0)
+    A, B, Q, R, Qf, lgA, lgB, lgQ, h0 = generate_inputs(2, 3, 16, torch.device("cpu"),
+                                                        torch.float32, 64, False)
+    Q = (Q + Q.transpose(-1, -2)) / 2
+    Qf = (Qf + Qf.transpose(-1, -2)) / 2
+    traj_case("traj_bench_d16", [A, B, Q, R, Qf, lgA, lgB, lgQ, h0], 64, seed_r=40)
+    traj_case("traj_prologue_cfg2", capture_prologue(CONFIGS[2], 2, heads=4), 64, seed_r=41)
+    traj_case("traj_synth_d32_du16", solver_inputs_synthetic(2, 2, 32, 16, seed=6), 32, seed_r=42)
+    traj_case("traj_T1", solver_inputs_synthetic(2, 2, 16, 16, seed=7), 1, seed_r=43)
+
+
 def main():
     torch.set_num_threads(os.cpu_count() or 1)
     # 1. The reference's own correctness-check case (bench_lqr_solvers.py:173-207):
@@ -167,4 +219,9 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["traj"]:
+        torch.set_num_threads(os.cpu_count() or 1)
+        traj_cases()
+    else:
+        main()
+        traj_cases()

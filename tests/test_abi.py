@@ -26,8 +26,8 @@ def declared_functions():
 
 def test_header_declares_expected_entry_points():
     names = declared_functions()
-    for n in ("ttc_lqr_fwd", "ttc_lqr_bwd", "ttc_prologue_fwd", "ttc_prologue_bwd", "ttc_abi_version",
-              "ttc_supported", "ttc_last_error"):
+    for n in ("ttc_lqr_fwd", "ttc_lqr_bwd", "ttc_lqr_rollout", "ttc_prologue_fwd", "ttc_prologue_bwd",
+              "ttc_abi_version", "ttc_supported", "ttc_last_error"):
         assert n in names
 
 
@@ -113,3 +113,23 @@ def test_prologue_rejects_bad_arguments_without_gpu(lib):
     assert bwd(dZ=None) == _lib.ERR_INVALID
     assert bwd(rQ=100) == _lib.ERR_UNSUPPORTED
     assert bwd(N=0) == _lib.OK
+
+
+def test_rollout_rejects_bad_arguments_without_gpu(lib):
+    from ttc_b200 import _lib
+    P = 16  # never dereferenced: rejected before any launch
+
+    def roll(Qf=P, lam0=P, M=P, r0=None, u=P, cost=None, N=1, nh=1, d=16, du=16, T=4, dtype=0):
+        return lib.ttc_lqr_rollout(P, P, P, P, Qf, P, P, P, P, lam0, M, r0, N, nh, d, du, T, dtype,
+                                   u, None, None, None, cost, P, None)
+
+    assert roll(N=-1) == _lib.ERR_INVALID
+    assert roll(T=0) == _lib.ERR_INVALID
+    assert roll(d=16, du=32) == _lib.ERR_UNSUPPORTED
+    assert roll(lam0=None) == _lib.ERR_INVALID
+    assert roll(u=None) == _lib.ERR_INVALID
+    assert roll(r0=P, M=None) == _lib.ERR_INVALID          # affine term needs M
+    assert b"r0" in lib.ttc_last_error()
+    assert roll(cost=P, Qf=None) == _lib.ERR_INVALID       # cost needs Q_f
+    assert roll(N=1 << 20, nh=64, T=64) == _lib.ERR_INVALID  # N * nh * T >= 2^31
+    assert roll(N=0) == _lib.OK

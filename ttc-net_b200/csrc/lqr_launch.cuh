@@ -7,6 +7,7 @@
 #include <cstdio>
 
 #include "lqr_adjoint_mma.cuh"
+#include "lqr_rollout.cuh"
 #include "lqr_tc.cuh"
 
 namespace ttc {
@@ -57,6 +58,14 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
 // a CUDA error.
 template <int D, int DU, typename TIn>
 int64_t bwd_mix_slices(int64_t N, int nh, int rQ);
+
+// Closed-loop trajectory from the forward's lambda0 (and M r0 for an affine step-0 cost).
+template <int D, int DU, typename TIn>
+int launch_rollout(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+                   const void* lA, const void* lB, const void* lQ, const void* h0,
+                   const float* lam0, const float* M, const void* r0, int64_t N, int nh, int T,
+                   void* u, float* hs, float* lams, float* lam0_out, float* cost, int* status,
+                   cudaStream_t st);
 
 #ifdef TTC_DEFINE_LAUNCHERS
 constexpr size_t kMaxSmem = 227 * 1024;
@@ -239,6 +248,26 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
   return cuda_check(cudaGetLastError(), "lqr_bwd_tc_kernel launch");
 }
 
+template <int D, int DU, typename TIn>
+int launch_rollout(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+                   const void* lA, const void* lB, const void* lQ, const void* h0,
+                   const float* lam0, const float* M, const void* r0, int64_t N, int nh, int T,
+                   void* u, float* hs, float* lams, float* lam0_out, float* cost, int* status,
+                   cudaStream_t st) {
+  constexpr int H = rollout_heads<D>();
+  // Groups per CTA: enough to cover the row's heads H at a time, at most kRollThreads / D.
+  int G = (nh + H - 1) / H;
+  if (G > kRollThreads / D) G = kRollThreads / D;
+  auto k = ttc::lqr_rollout_kernel<D, DU, TIn, H>;
+  const size_t smem = RolloutLayout<D, DU, H>::bytes(G);
+  if (int rc = set_smem(k, smem)) return rc;
+  k<<<dim3((unsigned)N), dim3(G * D), smem, st>>>(
+      (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)lA, (const TIn*)lB,
+      (const TIn*)lQ, (const TIn*)h0, (const TIn*)Qf, lam0, M, (const TIn*)r0, nh, T, (TIn*)u,
+      hs, lams, lam0_out, cost, status);
+  return cuda_check(cudaGetLastError(), "lqr_rollout_kernel launch");
+}
+
 #endif  // TTC_DEFINE_LAUNCHERS
 
 }  // namespace ttc
@@ -253,4 +282,10 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
                                            const void*, const float*, const float*,            \
                                            const void*, int64_t, int, int, void* const*, int*, \
                                            const ttc::QMix&, int, cudaStream_t);               \
-  template int64_t ttc::bwd_mix_slices<D, DU, TIn>(int64_t, int, int);
+  template int64_t ttc::bwd_mix_slices<D, DU, TIn>(int64_t, int, int);                      \
+  template int ttc::launch_rollout<D, DU, TIn>(const void*, const void*, const void*,         \
+                                               const void*, const void*, const void*,         \
+                                               const void*, const void*, const void*,         \
+                                               const float*, const float*, const void*,       \
+                                               int64_t, int, int, void*, float*, float*,      \
+                                               float*, float*, int*, cudaStream_t);

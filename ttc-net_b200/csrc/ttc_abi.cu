@@ -115,6 +115,33 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
 #undef TTC_BWD
 }
 
+int ttc_lqr_rollout(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                    const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
+                    const void* log_gamma_Q, const void* h0, const float* lam0, const float* M,
+                    const void* r0, int64_t N, int nh, int d, int du, int T, int dtype,
+                    void* u_traj, float* h_traj, float* lam_traj, float* lam0_out, float* cost,
+                    int* status, void* stream) {
+  if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (N == 0) return TTC_OK;
+  if (!A_diag || !B || !Q || !R_inv || !log_gamma_A || !log_gamma_B || !log_gamma_Q || !h0 ||
+      !lam0 || !u_traj || !status)
+    return fail(TTC_ERR_INVALID, "null pointer argument");
+  if (r0 != nullptr && M == nullptr)
+    return fail(TTC_ERR_INVALID, "an affine term r0 needs the forward's M");
+  if (cost != nullptr && Q_f == nullptr)
+    return fail(TTC_ERR_INVALID, "the total cost needs Q_f");
+  if (N * nh * (int64_t)T > 0x7fffffffLL)
+    return fail(TTC_ERR_INVALID, "N * num_heads * T must be below 2^31");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define TTC_ROLL(DD, DDU, TT)                                                                 \
+  return ttc::launch_rollout<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,     \
+                                     log_gamma_Q, h0, lam0, M, r0, N, nh, T, u_traj, h_traj,      \
+                                     lam_traj, lam0_out, cost, status, st)
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_ROLL, float);
+  TTC_FOR_DIMS(TTC_ROLL, __nv_bfloat16);
+#undef TTC_ROLL
+}
+
 int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                     const void* coeff_Qf, const void* Q_basis, int rQ, const void* log_gamma_A,
                     const void* log_gamma_B, const void* log_gamma_Q, const void* h0, int64_t N, int nh,

@@ -10,7 +10,7 @@ import os
 import threading
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libttc_b200.so")
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -24,6 +24,8 @@ STATUS_FWD_UNSTABLE = 1
 STATUS_LU_UNSTABLE = 2
 STATUS_BWD_UNSTABLE = 4
 STATUS_U_NAN = 8
+STATUS_MMA_TIMEOUT = 16
+STATUS_TRAJ_NONFINITE = 32
 
 FLAG_INV_GUARD = 1
 
@@ -38,6 +40,7 @@ SIGNATURES = {
     "ttc_last_error": (ctypes.c_char_p, []),
     "ttc_lqr_fwd": (_I, [_P] * 9 + [_I64, _I, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
     "ttc_lqr_bwd": (_I, [_P] * 9 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I, _I] + [_P] * 9 + [_P, _P]),
+    "ttc_lqr_rollout": (_I, [_P] * 9 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I] + [_P] + [_FP] * 4 + [_P, _P]),
     "ttc_lqr_fwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_I64, _I, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
     "ttc_lqr_bwd_mix_slices": (_I64, [_I64, _I, _I, _I, _I, _I]),
     "ttc_lqr_bwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I]

@@ -22,6 +22,8 @@ FWD_UNSTABLE_MSG = "Numerical instability detected during fused LQR forward recu
 LU_UNSTABLE_MSG = "Numerical instability detected during fused LQR LU solve."
 BWD_UNSTABLE_MSG = "Numerical instability detected during fused LQR backward pass."
 U_NAN_MSG = "NaN detected in TTC layer solver output."
+MMA_TIMEOUT_MSG = ("ttc_b200: a tensor-core MMA did not complete within the kernel's poll limit "
+                   "(the launch's results are not valid)")
 
 # The backward needs d_p = Y1^-1 (Y3 du).  The forward keeps M = Y1^-1 Y3
 # ([N,nh,d,du] fp32) when it fits this budget, else the backward recomputes the sweep.
@@ -91,6 +93,24 @@ def _check_shapes(A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T):
     return bs, nh, d, du
 
 
+def check_fwd_status(st: int) -> None:
+    """Raise the reference's forward RuntimeError for the TTC_STATUS_* bits of a forward."""
+    if st & _lib.STATUS_MMA_TIMEOUT:
+        raise RuntimeError(MMA_TIMEOUT_MSG)
+    if st & _lib.STATUS_FWD_UNSTABLE:
+        raise RuntimeError(FWD_UNSTABLE_MSG)
+    if st & _lib.STATUS_LU_UNSTABLE:
+        raise RuntimeError(LU_UNSTABLE_MSG)
+
+
+def check_bwd_status(st: int) -> None:
+    """Raise for the TTC_STATUS_* bits of a backward."""
+    if st & _lib.STATUS_MMA_TIMEOUT:
+        raise RuntimeError(MMA_TIMEOUT_MSG)
+    if st & _lib.STATUS_BWD_UNSTABLE:
+        raise RuntimeError(BWD_UNSTABLE_MSG)
+
+
 def _prepare(tensors, dtype):
     out = []
     for t in tensors:
@@ -125,10 +145,7 @@ class LQRSolveFunction(torch.autograd.Function):
             _launch("ttc_lqr_fwd", dev, lib.ttc_lqr_fwd, *[_ptr(a) for a in args], N, nh, d, du,
                     T, _DTYPES[dtype], flags, _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
         st = int(status.item())
-        if st & _lib.STATUS_FWD_UNSTABLE:
-            raise RuntimeError(FWD_UNSTABLE_MSG)
-        if st & _lib.STATUS_LU_UNSTABLE:
-            raise RuntimeError(LU_UNSTABLE_MSG)
+        check_fwd_status(st)
         A_c, B_c, Q_c, R_c, Qf_c, lA_c, lB_c, lQ_c, h0_c = args
         ctx.save_for_backward(A_c, B_c, Q_c, R_c, None if keep_m else Qf_c, lA_c, lB_c, lQ_c,
                               h0_c, lam0 if keep_m else None, M)
@@ -157,8 +174,7 @@ class LQRSolveFunction(torch.autograd.Function):
                     *[_ptr(t) for t in (A, B, Q, R, Qf, lA, lB, lQ, h0)], _ptr(lam0), _ptr(M),
                     _ptr(d_u), N, nh, d, du, T, _DTYPES[dtype], ctx.flags, *[_ptr(g) for g in grads],
                     _ptr(status))
-        if int(status.item()) & _lib.STATUS_BWD_UNSTABLE:
-            raise RuntimeError(BWD_UNSTABLE_MSG)
+        check_bwd_status(int(status.item()))
         grads = [g.to(dt) for g, dt in zip(grads, ctx.in_dtypes)]
         return (*grads, None, None, None)
 
@@ -203,10 +219,7 @@ class LQRSolveMixFunction(torch.autograd.Function):
                     _ptr(cQf_c), _ptr(Qb_c), rQ, _ptr(lA_c), _ptr(lB_c), _ptr(lQ_c), _ptr(h0_c), N, nh, d,
                     du, T, _DTYPES[dtype], 0, _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
         st = int(status.item())
-        if st & _lib.STATUS_FWD_UNSTABLE:
-            raise RuntimeError(FWD_UNSTABLE_MSG)
-        if st & _lib.STATUS_LU_UNSTABLE:
-            raise RuntimeError(LU_UNSTABLE_MSG)
+        check_fwd_status(st)
         ctx.save_for_backward(*args, lam0, M)
         ctx.dims = (N, nh, d, du, rQ, T)
         ctx.dtype = dtype
@@ -238,8 +251,7 @@ class LQRSolveMixFunction(torch.autograd.Function):
                     *[_ptr(t) for t in (lA, lB, lQ, h0)], _ptr(lam0), _ptr(M), _ptr(d_u), N, nh, d, du,
                     T, _DTYPES[dtype], _ptr(gA), _ptr(gB), _ptr(gQ), _ptr(gR), _ptr(gcQf), _ptr(partial),
                     slices, _ptr(glA), _ptr(glB), _ptr(glQ), _ptr(gh0), _ptr(status))
-        if int(status.item()) & _lib.STATUS_BWD_UNSTABLE:
-            raise RuntimeError(BWD_UNSTABLE_MSG)
+        check_bwd_status(int(status.item()))
         S = partial.sum(0)
         gQb = 0.5 * (S + S.transpose(-1, -2))
         grads = [gA, gB, gQ, gR, gcQf, gQb, glA, glB, glQ, gh0]
