@@ -208,9 +208,9 @@ def run_step(layer, x, dy, T, chunk, world):
 
 
 # ------------------------------------------------------------------------- CPU legs
-def cpu_sample(cfg, target_s, threads):
+def cpu_sample(cfg, target_s, threads, rows=None):
     """Reference algorithm on the host: oracle riccati layer fwd + autograd bwd on a row
-    sample sized to ~target_s seconds.  Returns (tokens/s, rows, seconds)."""
+    sample sized to ~target_s seconds (or of `rows` rows).  Returns (tokens/s, rows, seconds)."""
     from oracle import ttc_oracle as O
     torch.set_num_threads(threads)
     layer = O.TTCLayerOracle(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
@@ -226,10 +226,18 @@ def cpu_sample(cfg, target_s, threads):
             y.backward(torch.from_numpy(dy_np)[None])
         return time.perf_counter() - t0
 
+    if rows is not None:
+        dt = once(rows)
+        return (rows / cfg.H) / dt, rows, dt
+    # A tiny probe is dominated by per-step Python overhead and overestimates the cost of a
+    # row; one more rescale from the first real sample brings the sample to ~target_s.
     probe = max(1, cfg.H // 8)
     t = once(probe)
     rows = int(max(probe, min(cfg.rows, probe * target_s / max(t, 1e-6))))
     dt = once(rows)
+    if dt < 0.5 * target_s and rows < cfg.rows:
+        rows = int(min(cfg.rows, rows * target_s / max(dt, 1e-6)))
+        dt = once(rows)
     return (rows / cfg.H) / dt, rows, dt
 
 
@@ -241,10 +249,9 @@ def reference_arm(args, cfg):
     threads = os.cpu_count() or 1
     budget = 150.0 / max(1, args.steps + args.warmup)
     vals = []
-    rows_used = 0
+    rows_used = None
     for k in range(args.warmup + args.steps):
-        v, rows, _ = cpu_sample(cfg, budget, threads)
-        rows_used = rows
+        v, rows_used, _ = cpu_sample(cfg, budget, threads, rows_used)
         if k >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
@@ -375,11 +382,26 @@ def main(argv=None):
               for s in range(2)]
     dy_host = [torch.from_numpy(layer_input(cfg, cfg.rows, seed=500 + s)[1]).to(dtype).pin_memory()
                for s in range(2)]
-    dx_host = torch.empty(cfg.rows, cfg.in_dim, dtype=dtype).pin_memory()
+    dx_host = [torch.empty(cfg.rows, cfg.in_dim, dtype=dtype).pin_memory() for _ in range(2)]
+    # A data-loader pattern: step k+1's inputs are copied in on a side stream while step k
+    # computes, and step k's dx is copied out on it while step k+1 computes.  Every step's
+    # copies are inside the timed region (the region ends after the last copy out).
+    copy_stream = torch.cuda.Stream(device)
+    compute = torch.cuda.current_stream(device)
 
-    def e2e_step(k):
-        x = x_host[k % 2].to(device, non_blocking=True).view(cfg.B, rows, cfg.in_dim)
-        dy = dy_host[k % 2].to(device, non_blocking=True).view(cfg.B, rows, cfg.out_dim)
+    def fetch(k):
+        with torch.cuda.stream(copy_stream):
+            x = x_host[k % 2].to(device, non_blocking=True).view(cfg.B, rows, cfg.in_dim)
+            dy = dy_host[k % 2].to(device, non_blocking=True).view(cfg.B, rows, cfg.out_dim)
+            ready = torch.cuda.Event()
+            ready.record(copy_stream)
+        return x, dy, ready
+
+    def e2e_step(k, inputs):
+        x, dy, ready = inputs
+        compute.wait_event(ready)
+        x.record_stream(compute)
+        dy.record_stream(compute)
         x.requires_grad_(True)
         layer.zero_grad(set_to_none=True)
         for s in range(0, rows, chunk):
@@ -388,17 +410,29 @@ def main(argv=None):
         if world > 1:
             from ttc_b200.parallel import allreduce_grads
             allreduce_grads(layer)
-        dx_host.copy_(x.grad.view(cfg.rows, cfg.in_dim), non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(compute)
+        gx = x.grad.view(cfg.rows, cfg.in_dim)
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(done)
+            gx.record_stream(copy_stream)
+            dx_host[k % 2].copy_(gx, non_blocking=True)
 
-    e2e_step(0)
+    e2e_step(0, fetch(0))
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
+    copy_stream.wait_event(t0)
+    nxt = fetch(0)
     for k in range(args.steps):
-        e2e_step(k)
+        cur = nxt
+        if k + 1 < args.steps:
+            nxt = fetch(k + 1)
+        e2e_step(k, cur)
+    compute.wait_stream(copy_stream)
     t1.record()
     torch.cuda.synchronize()
     barrier()

@@ -18,6 +18,11 @@
 namespace ttc {
 
 constexpr uint32_t kMaxPolls = 1u << 24;  // bounded mbarrier polls before TTC_STATUS_MMA_TIMEOUT
+// At d = 16 (six tiles per SM) sleeping in try_wait instead of polling frees issue slots for
+// the other tiles' CUDA-core work (2.4 % on config 2); at d = 32 and 64 (fewer tiles per SM)
+// the wake-up costs more than it saves.
+template <int D>
+constexpr uint32_t kWaitHintNs = D <= 16 ? 1000u : 0u;
 
 template <int D, int DU>
 struct TcCfg {
@@ -102,6 +107,7 @@ struct TileCtx {
   uint32_t t_hi, t_lo, t_acc;        // lane 0 of the tile (MMA operands)
   uint64_t* mbar;
   uint32_t parity;
+  uint32_t wait_hint_ns;             // mbar_wait's suspend hint (0: plain polls)
   int bar_id;
   bool mma_warp;                     // warp 0 of the tile: one elected lane issues the MMAs
   bool timed_out;
@@ -150,7 +156,7 @@ __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], fl
     __syncwarp();
   }
   overlap();  // independent work while the tensor core runs
-  const bool ok = tc::mbar_wait(X.mbar, X.parity, kMaxPolls);
+  const bool ok = tc::mbar_wait(X.mbar, X.parity, kMaxPolls, X.wait_hint_ns);
   X.parity ^= 1u;
   if (!ok) {
     X.timed_out = true;
@@ -447,6 +453,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     X.my_acc = X.t_acc + lane_off;
     X.mbar = &mbars[slot];
     X.parity = 0;
+    X.wait_hint_ns = kWaitHintNs<D>;
     X.bar_id = 1 + slot;
     X.mma_warp = (lane < 32);
     X.timed_out = false;
@@ -655,6 +662,7 @@ lqr_bwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     X.my_acc = X.t_acc + lane_off;
     X.mbar = &mbars[slot];
     X.parity = 0;
+    X.wait_hint_ns = kWaitHintNs<D>;
     X.bar_id = 1 + slot;
     X.mma_warp = (lane < 32);
     X.timed_out = false;

@@ -77,8 +77,33 @@ __device__ __forceinline__ void mbar_init_fence() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 // Polls phase `parity` of `mbar` at most `max_polls` times; false if it never completed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t max_polls) {
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for phase `parity` of the mbarrier; false if it did not complete in time.
+// hint_ns == 0: at most max_polls polls of try_wait.  hint_ns > 0: try_wait with that
+// suspend-time hint, so the thread sleeps until the phase completes (or the hint elapses)
+// instead of re-issuing polls that take issue slots from the other warps on the SM; bounded
+// by one second of %globaltimer.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t max_polls,
+                                          uint32_t hint_ns = 0) {
   uint32_t done = 0;
+  if (hint_ns > 0) {
+    const uint64_t t0 = global_ns();
+    while (true) {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(done)
+          : "r"(smem_u32(mbar)), "r"(parity), "r"(hint_ns)
+          : "memory");
+      if (done) return true;
+      if (global_ns() - t0 > 1000000000ull) return false;
+    }
+  }
   for (uint32_t it = 0; it < max_polls; ++it) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
