@@ -19,10 +19,20 @@ namespace ttc {
 
 constexpr uint32_t kMaxPolls = 1u << 24;  // bounded mbarrier polls before TTC_STATUS_MMA_TIMEOUT
 // At d = 16 (six tiles per SM) sleeping in try_wait instead of polling frees issue slots for
-// the other tiles' CUDA-core work (2.4 % on config 2); at d = 32 and 64 (fewer tiles per SM)
-// the wake-up costs more than it saves.
+// the other tiles' CUDA-core work (2.4 % on config 2; the hint's value, 50 ns to 5 us, does
+// not matter), and 1.5 % at d = 64; at d = 32 (four tiles per SM, the whole TMEM) the
+// wake-up costs 1.2 % more than it saves.
+#ifndef TTC_WAIT_HINT16
+#define TTC_WAIT_HINT16 1000u
+#endif
+#ifndef TTC_WAIT_HINT32
+#define TTC_WAIT_HINT32 0u
+#endif
+#ifndef TTC_WAIT_HINT64
+#define TTC_WAIT_HINT64 1000u
+#endif
 template <int D>
-constexpr uint32_t kWaitHintNs = D <= 16 ? 1000u : 0u;
+constexpr uint32_t kWaitHintNs = D <= 16 ? TTC_WAIT_HINT16 : (D <= 32 ? TTC_WAIT_HINT32 : TTC_WAIT_HINT64);
 
 template <int D, int DU>
 struct TcCfg {
