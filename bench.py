@@ -56,6 +56,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--solver", default="cuda", choices=["cuda", "kkt"],
+                    help="the layer's solver_impl (kkt: the reference's two-problem backward on the GPU)")
     ap.add_argument("--workload", default="layer", choices=["layer", "traj"],
                     help="layer: the headline TTCLayer step; traj: closed-loop trajectories "
                          "(lqr_trajectory) of the config's solver inputs, one GPU")
@@ -177,10 +179,10 @@ def dist_setup(ngpus):
     return world, rank, local
 
 
-def make_layer(cfg, device, dtype):
+def make_layer(cfg, device, dtype, solver="cuda"):
     from ttc_b200 import TTCLayer
     layer = TTCLayer(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
-                     solver_impl="cuda")
+                     solver_impl=solver)
     layer.load_state_dict({k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()})
     return layer.to(device=device, dtype=dtype)
 
@@ -262,7 +264,8 @@ def reference_arm(args, cfg):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * (rows_used / cfg.H) / value, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(cfg, world, args, chunk=None),
+        "config": {**workload_config(cfg, world, args, chunk=None),
+                   "solver_impl": "riccati (oracle port, CPU)"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -283,6 +286,7 @@ def workload_config(cfg, world, args, chunk):
         "global_batch": cfg.B * world, "activations": cfg.dtype, "solver_state": "f32",
         "parallelism": f"dp{world}" if world > 1 else "single",
         "chunk_rows": chunk, "l2": "rotating input sets larger than L2 (no flush)",
+        "solver_impl": args.solver,
     }
 
 
@@ -316,7 +320,7 @@ def main(argv=None):
     dtype = torch.bfloat16 if cfg.dtype == "bfloat16" else torch.float32
 
     from ttc_b200.solver import KernelTimer, set_kernel_timer
-    layer = make_layer(cfg, device, dtype)
+    layer = make_layer(cfg, device, dtype, args.solver)
     chunk = args.chunk_rows or auto_chunk(cfg, dtype)
     rows = cfg.L * cfg.H
 
@@ -444,6 +448,10 @@ def main(argv=None):
     if rank == 0:
         fwd_f, bwd_f = solver_flops(cfg)
         fwd_ms = kern.get("ttc_lqr_fwd", [float("nan")])
+        # kkt: the backward is one more forward and two rollouts, so the forward launches
+        # alternate between the layer's forward and the backward's
+        if args.solver == "kkt":
+            fwd_ms = fwd_ms[0::2]
         bwd_ms = kern.get("ttc_lqr_bwd", [float("nan")])
         calls_per_step = math.ceil(rows / chunk)
         probs_per_launch = cfg.problems / calls_per_step
@@ -471,9 +479,12 @@ def main(argv=None):
             "kernels": {
                 "ttc_lqr_fwd": {"launches": len(fwd_ms), "mean_ms": statistics.mean(fwd_ms),
                                 "tflops": fwd_tflops},
-                "ttc_lqr_bwd": {"launches": len(bwd_ms), "mean_ms": statistics.mean(bwd_ms),
-                                "tflops": bwd_tflops,
-                                "frac_fp32_peak": bwd_tflops / fp32_peak},
+                **({"ttc_lqr_bwd": {"launches": len(bwd_ms), "mean_ms": statistics.mean(bwd_ms),
+                                    "tflops": bwd_tflops,
+                                    "frac_fp32_peak": bwd_tflops / fp32_peak}}
+                   if "ttc_lqr_bwd" in kern else {}),
+                **{k: {"launches": len(v), "mean_ms": statistics.mean(v)} for k, v in kern.items()
+                   if k not in ("ttc_lqr_fwd", "ttc_lqr_bwd")},
             },
             "clocks": clock_summary,
             "e2e": {"value": tokens_per_step * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",

@@ -8,8 +8,8 @@ The solver is libttc_b200.so (include/ttc_b200.h), bound with ctypes.
 """
 from .layer import TTCLayer, l2norm
 from .solver import (LQR_SOLVER_IMPL_MAP, LQRSolveFunction, cuda_lqr_solve, fused_lqr_solve,
-                     lqr_solve_with_status)
+                     kkt_lqr_solve, lqr_solve_with_status)
 from .trajectory import lqr_trajectory
 
 __all__ = ["TTCLayer", "LQR_SOLVER_IMPL_MAP", "LQRSolveFunction", "cuda_lqr_solve",
-           "fused_lqr_solve", "lqr_solve_with_status", "lqr_trajectory", "l2norm"]
+           "fused_lqr_solve", "kkt_lqr_solve", "lqr_solve_with_status", "lqr_trajectory", "l2norm"]

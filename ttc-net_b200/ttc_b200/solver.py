@@ -301,9 +301,20 @@ def fused_lqr_solve(A_diag, B, Q, R_inv_diag, Q_f, gamma_A, gamma_B, gamma_Q, h0
                           inv_guard=inv_guard)
 
 
+def kkt_lqr_solve(A_diag, B, Q, R_inv_diag, Q_f, gamma_A, gamma_B, gamma_Q, h0, T,
+                  save_budget: int | None = None):
+    """The reference's ``kkt`` solver on the GPU (see ttc_b200.kkt)."""
+    from .kkt import kkt_lqr_solve as impl
+    return impl(A_diag, B, Q, R_inv_diag, Q_f, gamma_A, gamma_B, gamma_Q, h0, T, save_budget)
+
+
 # The plug-in map of ttc_layer.py:18-22.  "fused" (the reference's default name) maps to
-# the CUDA solver so TTCLayer(..., solver_impl="fused") keeps working after the switch.
+# the CUDA solver so TTCLayer(..., solver_impl="fused") keeps working after the switch;
+# "kkt" is the reference's kkt solver (Riccati forward, two-problem backward) on the GPU.
+# The reference's "riccati" (autograd through the Riccati recursion, whose Q gradient is not
+# symmetrised) is the CPU oracle and has no GPU entry.
 LQR_SOLVER_IMPL_MAP = {
     "cuda": cuda_lqr_solve,
     "fused": cuda_lqr_solve,
+    "kkt": kkt_lqr_solve,
 }
