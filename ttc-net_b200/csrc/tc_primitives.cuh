@@ -23,6 +23,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ float tf32_residual(float x) {
   return x - __uint_as_float(__float_as_uint(x) & 0xffffe000u);
 }
+// Two residuals with one paired subtraction: (x, y) - ((x, y) & mask).
+__device__ __forceinline__ void tf32_residual2(float x, float y, float& rx, float& ry) {
+  asm("{\n\t.reg .b64 p, m;\n\tmov.b64 p, {%2, %3};\n\t"
+      "and.b64 m, p, 0xffffe000ffffe000;\n\tsub.rn.f32x2 p, p, m;\n\t"
+      "mov.b64 {%0, %1}, p;\n\t}"
+      : "=f"(rx), "=f"(ry)
+      : "f"(x), "f"(y));
+}
 __device__ __forceinline__ float tf32_trunc(float x) {
   return __uint_as_float(__float_as_uint(x) & 0xffffe000u);
 }
