@@ -139,13 +139,15 @@ __device__ __forceinline__ void stage_rows(float* S, const float (&v)[D / 8][4],
 }
 
 // acc[n-tile][.] += sum_r SX[r][16 mi + m] * SY[(r + 8) % 16][n]  over the 16 staged rows
-// (K) for one m-tile of the output, 3xTF32.
-template <int D>
+// (K) for one m-tile of the output, 3xTF32.  KK = 1 takes the first 8 rows only (the primal
+// rows against the tangent rows): for a symmetric pair X = Y = [v; dv] that is
+// S = sum v dv^T, whose S + S^T is the full sum at half the MMAs.
+template <int D, int KK = 2>
 __device__ __forceinline__ void accumulate_unit(float (&acc)[D / 8][4], const float* SX, const float* SY,
                                                 int mi, int g, int t) {
   constexpr int SS = AdjMma<D>::SS, NT = D / 8;
 #pragma unroll
-  for (int kk = 0; kk < 2; ++kk) {
+  for (int kk = 0; kk < KK; ++kk) {
     const float* x0 = SX + (8 * kk + t) * SS + 16 * mi;
     const float* x1 = SX + (8 * kk + t + 4) * SS + 16 * mi;
     uint32_t ah[4], al[4];
@@ -519,7 +521,8 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         __syncwarp();
       }
       // grad_B += lambda (du e^lgB)^T + dlambda (u e^lgB)^T ;
-      // grad_Q += (h Dq)(dh Dq)^T + (dh Dq)(h Dq)^T  (the 1/2 is applied at the end)
+      // grad_Q += (h Dq)(dh Dq)^T + (dh Dq)(h Dq)^T  (the 1/2 is applied at the end; at
+      // d = 16 only the first term is accumulated and the transpose added at the end)
 #pragma unroll
       for (int q = 0; q < UPW; ++q) {
         const int unit = C::kOwn ? q : hb + q * wpr;
@@ -530,7 +533,12 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
             const int off = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : 0);
             const int offy = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : C::kStage);
             if constexpr (C::kOwn) {
-              accumulate_unit<D>(acc[q], stg + off, stg + offy, mi, g, t);
+              // grad_Q as S = sum (h Dq)(dh Dq)^T, symmetrised at the end
+              if (isq) {
+                accumulate_unit<D, 1>(acc[q], stg + off, stg + offy, mi, g, t);
+              } else {
+                accumulate_unit<D>(acc[q], stg + off, stg + offy, mi, g, t);
+              }
             } else {
               for (int w = 0; w < wpr; ++w) {
                 const float* base = row_stage + (size_t)w * C::kWarp;
@@ -620,8 +628,17 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         if (nr >= N) break;
         for (int e = tid; e < 2 * D * D; e += nthreads) {
           float v = 0.f;
-          for (int w = 0; w < wpr; ++w) v += warp_s[(size_t)(r * wpr + w) * C::kWarp + e];
-          if (e >= D * D) v *= 0.5f;
+          if (e < D * D) {
+            for (int w = 0; w < wpr; ++w) v += warp_s[(size_t)(r * wpr + w) * C::kWarp + e];
+          } else {
+            // grad_Q = (S + S^T) / 2 over the warps' partial S
+            const int ij = e - D * D, ji = D * D + (ij % D) * D + ij / D;
+            for (int w = 0; w < wpr; ++w) {
+              const float* ws = warp_s + (size_t)(r * wpr + w) * C::kWarp;
+              v += ws[e] + ws[ji];
+            }
+            v *= 0.5f;
+          }
           bad |= unstable(v);
           stf((e < D * D ? gB_out : gQ_out) + nr * (D * D) + (e % (D * D)), v);
         }
