@@ -198,8 +198,10 @@ def auto_chunk(cfg, dtype):
 
 
 def run_step(layer, x, dy, T, chunk, world):
-    """One fwd+bwd over the batch (row chunks when the batch does not fit one call)."""
+    """One fwd+bwd over the batch (row chunks when the batch does not fit one call): the
+    parameter gradients and dx, as the end-to-end step and the CPU baseline compute them."""
     layer.zero_grad(set_to_none=True)
+    x.grad = None
     rows = x.shape[1]
     for s in range(0, rows, chunk):
         y = layer(x[:, s:s + chunk], T)
@@ -331,7 +333,7 @@ def main(argv=None):
     sets = []
     for s in range(nsets):
         x_np, dy_np = layer_input(cfg, cfg.rows, seed=1000 * rank + s)
-        sets.append((torch.from_numpy(x_np).to(device, dtype).view(cfg.B, rows, cfg.in_dim),
+        sets.append((torch.from_numpy(x_np).to(device, dtype).view(cfg.B, rows, cfg.in_dim).requires_grad_(True),
                      torch.from_numpy(dy_np).to(device, dtype).view(cfg.B, rows, cfg.out_dim)))
 
     def barrier():
