@@ -254,6 +254,27 @@ int launch_rollout(const void* A, const void* B, const void* Q, const void* R, c
                    const float* lam0, const float* M, const void* r0, int64_t N, int nh, int T,
                    void* u, float* hs, float* lams, float* lam0_out, float* cost, int* status,
                    cudaStream_t st) {
+#ifndef TTC_ROLL_MMA
+#define TTC_ROLL_MMA 1
+#endif
+  if constexpr (TTC_ROLL_MMA && D == DU && D <= 32) {
+    // 16 heads per warp on warp-level tensor-core MMAs: 1.25x (d = 16, 16 heads) and 1.9x
+    // (d = 32, 32 heads) the CUDA-core rollout; with fewer than 16 heads at d = 16 half of
+    // each warp's MMA rows would idle and the CUDA-core kernel is faster.
+    using C = RollMma<D>;
+    if (C::fits(nh) && (D > 16 || nh >= 16)) {
+      const int rpc = C::rows_per_cta(nh);
+      const size_t smem = C::bytes(nh);
+      auto k = ttc::lqr_rollout_mma_kernel<D, TIn>;
+      if (int rc = set_smem(k, smem)) return rc;
+      const int64_t grid = (N + rpc - 1) / rpc;
+      k<<<dim3((unsigned)grid), dim3(32 * C::warps(nh)), smem, st>>>(
+          (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)lA, (const TIn*)lB,
+          (const TIn*)lQ, (const TIn*)h0, (const TIn*)Qf, lam0, M, (const TIn*)r0, N, nh, T, rpc,
+          (TIn*)u, hs, lams, lam0_out, cost, status);
+      return cuda_check(cudaGetLastError(), "lqr_rollout_mma_kernel launch");
+    }
+  }
   constexpr int H = rollout_heads<D>();
   // Groups per CTA: enough to cover the row's heads H at a time, at most kRollThreads / D.
   int G = (nh + H - 1) / H;

@@ -22,6 +22,7 @@
 // (and of u for i < du).  Fixed summation order: results are reproducible run to run.
 #pragma once
 
+#include "lqr_adjoint_mma.cuh"
 #include "lqr_kernels.cuh"
 
 namespace ttc {
@@ -262,6 +263,239 @@ lqr_rollout_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         if (i == 0 && valid[m]) cost_out[p[m]] = total;
       }
       G.sync();
+    }
+  }
+  if (bad) atomicOr(status, TTC_STATUS_TRAJ_NONFINITE);
+}
+
+// --------------------------------------------------------------------------------------
+// The same rollout on warp-level tensor-core MMAs, for d = du in {16, 32}.  All heads of a
+// batch row share B and Q, so a step of 16 heads is three small matrix products
+// [h Dq] Q^T, [lambda] B and [u e^lgB] B^T: one warp carries 16 heads of a row as the 16
+// rows of mma.sync.m16n8k8 (3xTF32, the operand layout and K permutation of the warp-MMA
+// adjoint: thread (g, t) = (lane / 4, lane % 4) holds entries {8j + 2t, 8j + 2t + 1} of heads
+// g and g + 8), and every elementwise update is thread-local.  Grid: ceil(N / R) CTAs of R
+// rows x ceil(nh / 16) warps; the rows' operands are built once per CTA in shared memory.
+// --------------------------------------------------------------------------------------
+template <int D>
+struct RollMma {
+  static constexpr int NT = D / 8;
+  static constexpr int kFrag = AdjMma<D>::kFrag;
+  static constexpr int SS = AdjMma<D>::SS;
+  static constexpr int kRow = 3 * kFrag;        // Q^T, B, B^T
+  static constexpr int kWarp = 16 * SS;         // final-state staging for the terminal cost
+  static constexpr int kMaxWarps = 8;
+  __host__ __device__ static int warps_per_row(int nh) { return (nh + 15) / 16; }
+  static int rows_per_cta(int nh) {
+    const int wpr = warps_per_row(nh);
+    return wpr >= kMaxWarps ? 1 : kMaxWarps / wpr;
+  }
+  static int warps(int nh) { return warps_per_row(nh) * rows_per_cta(nh); }
+  static size_t bytes(int nh) {
+    return sizeof(float) * ((size_t)rows_per_cta(nh) * kRow + (size_t)warps(nh) * kWarp);
+  }
+  static bool fits(int nh) { return warps_per_row(nh) <= kMaxWarps && bytes(nh) <= 227 * 1024; }
+};
+
+__device__ __forceinline__ void st_pair(float* p, float a, float b) {
+  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+__device__ __forceinline__ void st_pair(__nv_bfloat16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+
+template <int D, typename TIn>
+__global__ void __launch_bounds__(256, D <= 16 ? 2 : 1)
+lqr_rollout_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
+                       const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
+                       const TIn* __restrict__ lgA, const TIn* __restrict__ lgB,
+                       const TIn* __restrict__ lgQ, const TIn* __restrict__ H0,
+                       const TIn* __restrict__ Qf, const float* __restrict__ lam0_in,
+                       const float* __restrict__ M_in, const TIn* __restrict__ R0, int64_t N,
+                       int nh, int T, int rows_per_cta, TIn* __restrict__ u_out,
+                       float* __restrict__ h_out, float* __restrict__ lam_out,
+                       float* __restrict__ lam0_out, float* __restrict__ cost_out,
+                       int* __restrict__ status) {
+  using C = RollMma<D>;
+  constexpr int NT = C::NT, SS = C::SS;
+  extern __shared__ __align__(128) float smem[];
+  const int tid = threadIdx.x, nthreads = blockDim.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int wpr = C::warps_per_row(nh);
+  const int rloc = warp / wpr, hb = warp % wpr;
+  float* rows_s = smem;
+  float* stg = smem + (size_t)rows_per_cta * C::kRow + (size_t)warp * C::kWarp;
+  const int64_t n0 = (int64_t)blockIdx.x * rows_per_cta;
+  for (int r = 0; r < rows_per_cta; ++r) {
+    const int64_t nr = n0 + r;
+    if (nr >= N) break;
+    float* base = rows_s + r * C::kRow;
+    const TIn* Bn = Bm + nr * (D * D);
+    const TIn* Qn = Qm + nr * (D * D);
+    build_operand<D>(base, [&](int k, int c) { return ldf(Qn + c * D + k); }, tid, nthreads);
+    build_operand<D>(base + C::kFrag, [&](int k, int c) { return ldf(Bn + k * D + c); }, tid, nthreads);
+    build_operand<D>(base + 2 * C::kFrag, [&](int k, int c) { return ldf(Bn + c * D + k); }, tid, nthreads);
+  }
+  __syncthreads();
+  const int64_t n = n0 + rloc;
+  // Past the last row there is nothing to write and that row's operands were not built: the
+  // warp stops here (no CTA-wide barrier follows).
+  if (n >= N) return;
+  const float* rbase = rows_s + rloc * C::kRow;
+  const float4* Wqt = reinterpret_cast<const float4*>(rbase);
+  const float4* Wb = reinterpret_cast<const float4*>(rbase + C::kFrag);
+  const float4* Wbt = reinterpret_cast<const float4*>(rbase + 2 * C::kFrag);
+
+  // rows q = 0, 1 of this thread: heads g and g + 8 of the warp's 16
+  bool valid[2];
+  int64_t p[2];
+  float lgA2[2], cost[2] = {0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int h = hb * 16 + g + 8 * q;
+    valid[q] = h < nh;
+    p[q] = valid[q] ? n * nh + h : 0;
+    lgA2[q] = valid[q] ? ldf(lgA + p[q]) * kLog2e : 0.f;
+  }
+  // fragment index [j][2q + s] <-> head row q, entry 8j + 2t + s; a head past nh runs on
+  // zeros (finite with the row's operands) and writes nothing
+  float a[NT][4], lgQ2[NT][4], lgB2[NT][4], rinv[NT][4], dqp[NT][4], H[NT][4], L[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const int r = 2 * q + s, e = 8 * j + 2 * t + s;
+        const bool v = valid[q];
+        const int64_t pe = p[q] * D + e;
+        a[j][r] = v ? ldf(A_diag + pe) : 0.f;
+        lgQ2[j][r] = v ? ldf(lgQ + pe) * kLog2e : 0.f;
+        lgB2[j][r] = v ? ldf(lgB + pe) * kLog2e : 0.f;
+        rinv[j][r] = v ? ldf(Rinv + pe) : 1.f;
+        H[j][r] = v ? ldf(H0 + pe) : 0.f;
+        float lam = v ? lam0_in[pe] : 0.f;
+        if (v && R0 != nullptr) {
+          // lambda0 += M r0: the affine offset Y1^-1 (Y3 r0)
+          const float* mrow = M_in + pe * D;
+          const TIn* r0 = R0 + p[q] * D;
+          for (int c = 0; c < D; ++c) lam = fmaf(mrow[c], ldf(r0 + c), lam);
+        }
+        L[j][r] = lam;
+        dqp[j][r] = 1.0f;
+      }
+  if (lam0_out != nullptr) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+        if (valid[q]) st_pair(lam0_out + p[q] * D + 8 * j + 2 * t, L[j][2 * q], L[j][2 * q + 1]);
+  }
+  bool bad = false;
+  for (int k = 0; k < T; ++k) {
+    const float ke = static_cast<float>(k + 1);
+    if (k > 0) {
+      // lambda -= Dq Q Dq h
+      float HD[NT][4], QH[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r];
+      frag_product<D>(HD, QH, Wqt, lane);
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float qh = dqp[j][r] * QH[j][r];  // (Q_{k-1} h_k)_e
+          L[j][r] -= qh;
+          cost[r >> 1] = fmaf(0.5f * H[j][r], qh, cost[r >> 1]);
+        }
+    }
+    float At[NT][4];
+    {
+      const float eA[2] = {exp_scaled(lgA2[0], ke), exp_scaled(lgA2[1], ke)};
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          At[j][r] = fmaf(a[j][r], eA[r >> 1], 1.0f);
+          L[j][r] *= recip(At[j][r]);
+        }
+    }
+    // u = -R_inv e^lgB (B^T lambda); step 0: - R_inv r0
+    float UE[NT][4];
+    {
+      float BL[NT][4];
+      frag_product<D>(L, BL, Wb, lane);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        float u[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float eB = exp_scaled(lgB2[j][r], ke);
+          u[r] = -(BL[j][r] * eB) * rinv[j][r];
+          if (k == 0 && R0 != nullptr && valid[r >> 1]) {
+            const float r0 = ldf(R0 + p[r >> 1] * D + 8 * j + 2 * t + (r & 1));
+            u[r] = fmaf(r0, -rinv[j][r], u[r]);
+            cost[r >> 1] = fmaf(r0, u[r], cost[r >> 1]);
+          }
+          cost[r >> 1] = fmaf(0.5f * u[r], u[r] * recip(rinv[j][r]), cost[r >> 1]);
+          bad |= nonfinite(u[r]);
+          UE[j][r] = u[r] * eB;
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+          if (valid[q]) st_pair(u_out + (p[q] * T + k) * D + 8 * j + 2 * t, u[2 * q], u[2 * q + 1]);
+      }
+    }
+    // h = A h + B (e^lgB u)
+    {
+      float BU[NT][4];
+      frag_product<D>(UE, BU, Wbt, lane);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          H[j][r] = fmaf(H[j][r], At[j][r], BU[j][r]);
+          bad |= nonfinite(H[j][r] + L[j][r]);
+          dqp[j][r] = exp_scaled(lgQ2[j][r], ke);
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          if (!valid[q]) continue;
+          const int64_t o = (p[q] * T + k) * D + 8 * j + 2 * t;
+          if (h_out != nullptr) st_pair(h_out + o, H[j][2 * q], H[j][2 * q + 1]);
+          if (lam_out != nullptr) st_pair(lam_out + o, L[j][2 * q], L[j][2 * q + 1]);
+        }
+      }
+    }
+  }
+  if (cost_out != nullptr) {
+    // terminal 0.5 h_T^T Q_f h_T: the final states through the warp's staging rows
+    stage_rows<D>(stg, H, g, t);
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const float* hrow = stg + (g + 8 * q) * SS;
+      if (valid[q]) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            const int e = 8 * j + 2 * t + s;
+            const TIn* qf = Qf + (p[q] * D + e) * D;
+            float acc = 0.f;
+#pragma unroll 4
+            for (int c = 0; c < D; ++c) acc = fmaf(ldf(qf + c), hrow[c], acc);
+            cost[q] = fmaf(0.5f * hrow[e], acc, cost[q]);
+          }
+      }
+      float c = cost[q];
+      c += __shfl_xor_sync(0xffffffffu, c, 1);
+      c += __shfl_xor_sync(0xffffffffu, c, 2);
+      bad |= nonfinite(c);
+      if (valid[q] && t == 0) cost_out[p[q]] = c;
     }
   }
   if (bad) atomicOr(status, TTC_STATUS_TRAJ_NONFINITE);
