@@ -167,6 +167,31 @@ int ttc_lqr_bwd_mix(const void* A_diag, const void* B, const void* Q, const void
                     float* grad_basis_partial, int64_t slices, void* grad_lgA, void* grad_lgB,
                     void* grad_lgQ, void* grad_h0, int* status, void* stream);
 
+/*
+ * ttc_lqr_bwd_mix without device allocations.  No counterpart in the reference: this entry
+ * point exists for callers that cannot allocate device memory -- a host runtime that owns all
+ * device memory through its own pool and forbids plug-ins from calling cudaMalloc, or a
+ * latency-bound loop where a cudaMalloc / cudaFree (which may synchronise the device) is not
+ * acceptable.  Instead of the caller's grad_basis_partial buffer it uses a fixed scratch array
+ * inside the library (16 MiB of device memory per GPU, held from library load until process
+ * exit) and runs at most as many CTAs as there are [rQ, d, d] fp32 slices in it (a rank-rQ
+ * slice larger than the array is rejected with TTC_ERR_INVALID).  It writes the finished basis
+ * gradient grad_basis [rQ, d, d] (fp32) = (S + S^T) / 2, S the sum of the slices; all other
+ * arguments and outputs as ttc_lqr_bwd_mix (d = du in {16, 32}).  Allocates nothing and calls
+ * no allocating library routine.  The array is shared by all calls and keeps the last call's
+ * contents (each call zeroes the slices it uses); calls that overlap on the GPU race on it and
+ * must be serialised.  The first call on a device looks up the array's device address; make
+ * it before any stream capture.
+ */
+int ttc_lqr_bwd_mix_noalloc(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                            const void* coeff_Qf, const void* Q_basis, int rQ,
+                            const void* log_gamma_A, const void* log_gamma_B, const void* log_gamma_Q,
+                            const void* h0, const float* lam0, const float* M, const void* d_u,
+                            int64_t N, int nh, int d, int du, int T, int dtype, void* grad_A,
+                            void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_coeff_Qf,
+                            float* grad_basis, void* grad_lgA, void* grad_lgB, void* grad_lgQ,
+                            void* grad_h0, int* status, void* stream);
+
 /* Elementwise layer prologue (replaces the PyTorch ops of ttc/layers/ttc_layer.py:106-133
  * between in_proj and the low-rank einsums; the einsums stay with the caller).
  * Z [N, W] row-major in the activation dtype, W = nh*(4d + 2du + 1) + rB + rQ: per row nh

@@ -45,6 +45,8 @@ SIGNATURES = {
     "ttc_lqr_bwd_mix_slices": (_I64, [_I64, _I, _I, _I, _I, _I]),
     "ttc_lqr_bwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I]
                         + [_P] * 5 + [_FP, _I64] + [_P] * 4 + [_P, _P]),
+    "ttc_lqr_bwd_mix_noalloc": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I]
+                                + [_P] * 5 + [_FP] + [_P] * 4 + [_P, _P]),
     "ttc_prologue_fwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P]),
     "ttc_prologue_bwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P, _P]),
 }
