@@ -358,6 +358,14 @@ lqr_rollout_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ B
     p[q] = valid[q] ? n * nh + h : 0;
     lgA2[q] = valid[q] ? ldf(lgA + p[q]) * kLog2e : 0.f;
   }
+  // r0 of the warp's 16 heads into its staging rows (coalesced; read back per entry)
+  if (R0 != nullptr) {
+    for (int e = lane; e < 16 * D; e += 32) {
+      const int hr = e / D, h = hb * 16 + hr;
+      stg[hr * SS + e % D] = h < nh ? ldf(R0 + (n * nh + h) * D + e % D) : 0.f;
+    }
+    __syncwarp();
+  }
   // fragment index [j][2q + s] <-> head row q, entry 8j + 2t + s; a head past nh runs on
   // zeros (finite with the row's operands) and writes nothing
   float a[NT][4], lgQ2[NT][4], lgB2[NT][4], rinv[NT][4], dqp[NT][4], H[NT][4], L[NT][4];
@@ -378,9 +386,16 @@ lqr_rollout_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ B
         float lam = v ? lam0_in[pe] : 0.f;
         if (v && R0 != nullptr) {
           // lambda0 += M r0: the affine offset Y1^-1 (Y3 r0)
-          const float* mrow = M_in + pe * D;
-          const TIn* r0 = R0 + p[q] * D;
-          for (int c = 0; c < D; ++c) lam = fmaf(mrow[c], ldf(r0 + c), lam);
+          const float4* mrow = reinterpret_cast<const float4*>(M_in + pe * D);
+          const float* r0 = stg + (g + 8 * q) * SS;
+#pragma unroll 4
+          for (int c4 = 0; c4 < D / 4; ++c4) {
+            const float4 m = mrow[c4];
+            lam = fmaf(m.x, r0[4 * c4], lam);
+            lam = fmaf(m.y, r0[4 * c4 + 1], lam);
+            lam = fmaf(m.z, r0[4 * c4 + 2], lam);
+            lam = fmaf(m.w, r0[4 * c4 + 3], lam);
+          }
         }
         L[j][r] = lam;
         dqp[j][r] = 1.0f;
@@ -436,7 +451,7 @@ lqr_rollout_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ B
           const float eB = exp_scaled(lgB2[j][r], ke);
           u[r] = -(BL[j][r] * eB) * rinv[j][r];
           if (k == 0 && R0 != nullptr && valid[r >> 1]) {
-            const float r0 = ldf(R0 + p[r >> 1] * D + 8 * j + 2 * t + (r & 1));
+            const float r0 = stg[(g + 8 * (r >> 1)) * SS + 8 * j + 2 * t + (r & 1)];
             u[r] = fmaf(r0, -rinv[j][r], u[r]);
             cost[r >> 1] = fmaf(r0, u[r], cost[r >> 1]);
           }
@@ -472,7 +487,9 @@ lqr_rollout_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ B
     }
   }
   if (cost_out != nullptr) {
-    // terminal 0.5 h_T^T Q_f h_T: the final states through the warp's staging rows
+    // terminal 0.5 h_T^T Q_f h_T: the final states through the warp's staging rows (which
+    // held r0 until step 0)
+    __syncwarp();
     stage_rows<D>(stg, H, g, t);
     __syncwarp();
 #pragma unroll
