@@ -3,7 +3,7 @@
 Runs the reference package (VITA-Group/TTC-Net ``ttc/``) on the CPU -- its
 ``riccati`` and ``kkt`` solvers and its ``TTCLayer`` -- and stores inputs and
 outputs as compressed .npz fixtures beside this script.  The reference must be
-importable (set TTC_REFERENCE_ROOT, default /root/reference); it is NOT needed
+importable (set TTC_REFERENCE_ROOT to its checkout); it is NOT needed
 to run the tests, which only read the fixtures.
 
 fla's Triton ``l2norm`` wrapper does not run on CPU tensors, so
@@ -11,8 +11,8 @@ fla's Triton ``l2norm`` wrapper does not run on CPU tensors, so
 (x / sqrt(sum x^2 + 1e-6), fp32 compute, cast back -- fla/modules/l2norm.py:42).
 The Triton ``fused`` solver needs CUDA and is not run here.
 
-Usage:  python tests/golden/make_golden.py          (all fixtures)
-        python tests/golden/make_golden.py traj     (trajectory fixtures only)
+Usage:  TTC_REFERENCE_ROOT=<checkout> python tests/golden/make_golden.py        (all fixtures)
+        TTC_REFERENCE_ROOT=<checkout> python tests/golden/make_golden.py traj   (trajectory fixtures only)
 """
 from __future__ import annotations
 
@@ -27,7 +27,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))          # tests/ for ttc_cases
 from ttc_cases import CONFIGS, SOLVER_ARG_NAMES, layer_input, layer_weights, solver_inputs_synthetic  # noqa: E402
 
-REF = os.environ.get("TTC_REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("TTC_REFERENCE_ROOT")
+if not REF:
+    raise SystemExit("set TTC_REFERENCE_ROOT to the reference (VITA-Group/TTC-Net) checkout")
 sys.path.insert(0, REF)
 os.environ.setdefault("TRITON_NO_AUTOTUNE", "1")
 import ttc.layers.ttc_layer as ref_layer_mod  # noqa: E402
