@@ -20,6 +20,7 @@ class PrologueFunction(torch.autograd.Function):
     """Z [N, W] -> (A_diag, R_inv, coeff_Qf, lgA, lgB, lgQ, h0, coeff_B, coeff_Q)."""
 
     @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
     def forward(ctx, Z, nh, d, du, rB, rQ):
         if Z.dtype not in _DTYPES:
             raise TypeError(f"ttc_b200 prologue: unsupported dtype {Z.dtype}")
@@ -40,6 +41,7 @@ class PrologueFunction(torch.autograd.Function):
         return outs
 
     @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
     def backward(ctx, *grads):
         (Z,) = ctx.saved_tensors
         nh, d, du, rB, rQ = ctx.dims

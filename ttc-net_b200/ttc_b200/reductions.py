@@ -33,6 +33,7 @@ def _at_b(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 
 class _Linear(torch.autograd.Function):
     @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
     def forward(ctx, x, weight, bias):
         ctx.save_for_backward(x, weight)
         ctx.has_bias = bias is not None
@@ -40,6 +41,7 @@ class _Linear(torch.autograd.Function):
         return y + bias if bias is not None else y
 
     @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
     def backward(ctx, gy):
         x, weight = ctx.saved_tensors
         gx = gy @ weight if ctx.needs_input_grad[0] else None
@@ -55,12 +57,14 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> 
 
 class _LowRankMix(torch.autograd.Function):
     @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
     def forward(ctx, coeff, basis):
         ctx.save_for_backward(coeff, basis)
         r = basis.shape[0]
         return (coeff.reshape(-1, r) @ basis.reshape(r, -1)).view(*coeff.shape[:-1], *basis.shape[1:])
 
     @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
     def backward(ctx, g):
         coeff, basis = ctx.saved_tensors
         r = basis.shape[0]

@@ -126,6 +126,7 @@ class LQRSolveFunction(torch.autograd.Function):
     tensor carrying the forward's TTC_STATUS_* bits."""
 
     @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
     def forward(ctx, A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0, T, save_budget, flags=0):
         T = int(T)
         flags = int(flags)
@@ -158,6 +159,7 @@ class LQRSolveFunction(torch.autograd.Function):
         return u, status_cpu
 
     @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
     def backward(ctx, d_u, _d_status):
         A, B, Q, R, Qf, lA, lB, lQ, h0, lam0, M = ctx.saved_tensors
         N, nh, d, du, T = ctx.dims
@@ -196,6 +198,7 @@ class LQRSolveMixFunction(torch.autograd.Function):
     saves M (callers check ``mix_available`` first)."""
 
     @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
     def forward(ctx, A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0, T):
         T = int(T)
         N, nh, d = A_diag.shape
@@ -229,6 +232,7 @@ class LQRSolveMixFunction(torch.autograd.Function):
         return u, status_cpu
 
     @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
     def backward(ctx, d_u, _d_status):
         A, B, Q, R, cQf, Qb, lA, lB, lQ, h0, lam0, M = ctx.saved_tensors
         N, nh, d, du, rQ, T = ctx.dims
