@@ -1,0 +1,97 @@
+"""Data parallelism over NCCL on real GPUs (needs >= 2 visible GPUs, skipped otherwise): two
+ranks, one GPU each, run TTCLayer with the CUDA solver on their halves of a batch and
+all-reduce the parameter gradients once; y and dx of each rank and the reduced parameter
+gradients must equal one GPU's full-batch step."""
+import datetime
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _setup_paths():
+    for p in (os.path.dirname(HERE), os.path.join(os.path.dirname(HERE), "ttc-net_b200"), HERE):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+
+
+def _layer_and_data(device):
+    from ttc_b200 import TTCLayer
+    from ttc_cases import CONFIGS, layer_input, layer_weights
+    cfg = CONFIGS[2]
+    layer = TTCLayer(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank)
+    layer.load_state_dict({k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()})
+    rows = 4 * cfg.H * 64                      # 4 sequences of 64 positions x 16 heads
+    x_np, dy_np = layer_input(cfg, rows, seed=11)
+    x = torch.from_numpy(x_np).view(4, rows // 4, cfg.in_dim)
+    dy = torch.from_numpy(dy_np).view(4, rows // 4, cfg.out_dim)
+    return layer.to(device), x.to(device), dy.to(device), cfg.T
+
+
+def _step(layer, x, dy, T):
+    x = x.clone().requires_grad_(True)
+    y = layer(x, T)
+    y.backward(dy)
+    return y.detach(), x.grad.detach()
+
+
+def _worker(rank, world, port, out_dir):
+    _setup_paths()
+    import torch.distributed as dist
+    from ttc_b200.parallel import allreduce_grads, shard_rows
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        layer, x, dy, T = _layer_and_data(torch.device("cuda", rank))
+        y, dx = _step(layer, shard_rows(x, rank, world), shard_rows(dy, rank, world), T)
+        allreduce_grads(layer)
+        torch.cuda.synchronize()
+        torch.save({"y": y.cpu(), "dx": dx.cpu(),
+                    "grads": {n: p.grad.cpu() for n, p in layer.named_parameters()}},
+                   os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_data_parallel_matches_one_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _setup_paths()
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+    from oracle import ttc_oracle as O
+    from ttc_b200.parallel import shard_rows
+    layer, x, dy, T = _layer_and_data(torch.device("cuda", 0))
+    y, dx = _step(layer, x, dy, T)
+    parts = [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) for r in range(2)]
+    for r, part in enumerate(parts):
+        # rows are independent and the solver kernels batch-invariant: y is exact; dx also
+        # passes through cuBLAS GEMMs whose kernel choice depends on the row count
+        assert torch.equal(part["y"], shard_rows(y, r, 2).cpu())
+        assert O.max_rel(part["dx"], shard_rows(dx, r, 2).cpu()) < 1e-5
+    for n, p in layer.named_parameters():
+        # the same sums grouped per rank, then added by the all-reduce
+        assert O.max_rel(parts[0]["grads"][n], p.grad.cpu()) < 1e-5, n
+        assert torch.equal(parts[0]["grads"][n], parts[1]["grads"][n]), n
