@@ -80,6 +80,29 @@ def test_cuda_solver_rejects_cpu_tensors():
         cuda_lqr_solve(*host, 4)
 
 
+def test_registry_has_gpu_kkt():
+    """The reference's "kkt" name maps to the GPU kkt solver; "riccati" stays the CPU oracle."""
+    from ttc_b200 import LQR_SOLVER_IMPL_MAP, kkt_lqr_solve
+    assert LQR_SOLVER_IMPL_MAP["kkt"] is kkt_lqr_solve
+    assert "riccati" not in LQR_SOLVER_IMPL_MAP
+
+
+def test_trajectory_host_checks():
+    """lqr_trajectory validates before any launch: an affine cost on every step is not
+    supported, a wrong r0 shape is an error, and CPU tensors have no path."""
+    from ttc_b200 import kkt_lqr_solve, lqr_trajectory
+    from ttc_cases import solver_inputs_synthetic
+    host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(2, 2, 16, 16, seed=1)]
+    with pytest.raises(NotImplementedError, match="every step"):
+        lqr_trajectory(*host, 4, r0=torch.zeros(2, 2, 4, 16))
+    with pytest.raises(AssertionError, match="r0 must be"):
+        lqr_trajectory(*host, 4, r0=torch.zeros(2, 16))
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        lqr_trajectory(*host, 4)
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        kkt_lqr_solve(*host, 4)
+
+
 def test_solver_shape_contract():
     from ttc_b200 import cuda_lqr_solve
     from ttc_cases import solver_inputs_synthetic
