@@ -89,3 +89,17 @@ def test_kkt_bf16_inputs_run_in_fp32():
     assert O.max_rel(u16.float(), u32) < 1e-2
     for name, a, b in zip(GRAD_NAMES, g16, g32):
         assert O.max_rel(a.float(), b) < 1e-2, name
+
+
+def test_kkt_backward_row_chunks(monkeypatch):
+    """A small work budget splits the backward's trajectories into row chunks: same gradients."""
+    import ttc_b200.kkt as K
+    from ttc_b200 import kkt_lqr_solve
+    host = [torch.from_numpy(a) for a in solver_inputs_synthetic(10, 4, 16, 16, seed=73)]
+    dy = torch.randn(10, 4, 16, device="cuda")
+    mk = lambda: [a.to("cuda", torch.float32).requires_grad_(True) for a in host]  # noqa: E731
+    _, whole = _run(kkt_lqr_solve, mk(), 24, dy)
+    monkeypatch.setattr(K, "KKT_WORK_BYTES", 3 * K.KKT_BYTES_PER_STEP * 4 * 24 * (2 * 16 + 4 * 16))
+    _, chunked = _run(kkt_lqr_solve, mk(), 24, dy)
+    for name, a, b in zip(GRAD_NAMES, chunked, whole):
+        assert O.max_rel(a, b) < 1e-6, name

@@ -25,6 +25,11 @@ from .solver import (SAVE_BUDGET_BYTES, _DTYPES, _check_shapes, _launch, _prepar
 from .trajectory import TRAJ_NONFINITE_MSG
 
 _F32 = _DTYPES[torch.float32]
+# Device memory the backward's trajectories and gradient temporaries may take at once, and
+# the bytes they take per row, head, step and vector entry (six fp32 trajectories plus the
+# gradient terms formed from them, about three times that).
+KKT_WORK_BYTES = 16 << 30
+KKT_BYTES_PER_STEP = 12
 
 
 def _rollouts(args, T, d_u, budget):
@@ -154,10 +159,20 @@ class KKTSolveFunction(torch.autograd.Function):
         args = ctx.saved_tensors
         T = ctx.T
         d_u = d_u.to(torch.float32).contiguous()
-        with torch.profiler.record_function("bwd:kkt rollouts"):
-            fwd, bwd, lam0_b = _rollouts(args, T, d_u, ctx.budget)
-        A, B, Q, R, _, lA, lB, lQ, h0 = args
-        grads = kkt_grads(A, B, Q, R, lA, lB, lQ, h0, T, fwd, bwd, lam0_b)
+        N, nh, d = args[0].shape
+        du = args[1].shape[-1]
+        # Rows are independent: the two problems' trajectories and the gradient terms built
+        # from them are formed in row chunks of about KKT_WORK_BYTES.
+        rows = max(1, min(N, KKT_WORK_BYTES // (KKT_BYTES_PER_STEP * nh * T * (2 * du + 4 * d))))
+        grads = [torch.empty_like(t) for t in args]
+        for a in range(0, N, rows):
+            sub = [t[a:a + rows] for t in args]
+            with torch.profiler.record_function("bwd:kkt rollouts"):
+                fwd, bwd, lam0_b = _rollouts(sub, T, d_u[a:a + rows], ctx.budget)
+            A, B, Q, R, _, lA, lB, lQ, h0 = sub
+            for out, g in zip(grads, kkt_grads(A, B, Q, R, lA, lB, lQ, h0, T, fwd, bwd, lam0_b)):
+                out[a:a + rows] = g
+            del fwd, bwd, lam0_b
         grads = [g.to(dt) for g, dt in zip(grads, ctx.in_dtypes)]
         return (*grads, None, None)
 
