@@ -173,15 +173,16 @@ int ttc_lqr_bwd_mix(const void* A_diag, const void* B, const void* Q, const void
  * device memory through its own pool and forbids plug-ins from calling cudaMalloc, or a
  * latency-bound loop where a cudaMalloc / cudaFree (which may synchronise the device) is not
  * acceptable.  Instead of the caller's grad_basis_partial buffer it uses a fixed scratch array
- * inside the library (16 MiB of device memory per GPU, held from library load until process
- * exit) and runs at most as many CTAs as there are [rQ, d, d] fp32 slices in it (a rank-rQ
+ * inside the library (16 MiB of device memory per GPU, held until process exit; under CUDA's
+ * lazy module loading, the default since CUDA 12.2, it is reserved by the first call on each
+ * device, CUDA_MODULE_LOADING=EAGER reserves it when the context is created) and runs at most as many CTAs as there are [rQ, d, d] fp32 slices in it (a rank-rQ
  * slice larger than the array is rejected with TTC_ERR_INVALID).  It writes the finished basis
  * gradient grad_basis [rQ, d, d] (fp32) = (S + S^T) / 2, S the sum of the slices; all other
  * arguments and outputs as ttc_lqr_bwd_mix (d = du in {16, 32}).  Allocates nothing and calls
  * no allocating library routine.  The array is shared by all calls and keeps the last call's
  * contents (each call zeroes the slices it uses); calls that overlap on the GPU race on it and
  * must be serialised.  The first call on a device looks up the array's device address; make
- * it before any stream capture.
+ * it before any stream capture.  N = 0 writes zeros to grad_basis (when it is not null).
  */
 int ttc_lqr_bwd_mix_noalloc(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                             const void* coeff_Qf, const void* Q_basis, int rQ,

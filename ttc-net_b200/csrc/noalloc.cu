@@ -14,7 +14,11 @@
 // zeroes its own slice before accumulating, so nothing carries over.  Calls whose kernels
 // overlap on the GPU (other streams, other host threads) race on the array: serialise them.
 // The first call on a device looks up the array's device address (cudaGetSymbolAddress), so
-// make that first call before any stream capture.
+// make that first call before any stream capture.  Under CUDA's lazy module loading (the
+// default since CUDA 12.2) that lookup is also when the driver loads this module and reserves
+// the 16 MiB on the device: a host whose pool already holds all device memory should make the
+// first call while 16 MiB are still free, or set CUDA_MODULE_LOADING=EAGER so that the array
+// is reserved when the context is created.  An empty batch (N = 0) writes a zero grad_basis.
 #define TTC_DEFINE_LAUNCHERS
 #include <cstdio>
 #include <mutex>
@@ -120,7 +124,14 @@ extern "C" int ttc_lqr_bwd_mix_noalloc(const void* A_diag, const void* B, const 
     snprintf(buf, sizeof(buf), "no mixed-Q_f backward for h_dim=%d u_dim=%d (needs h_dim = u_dim in {16, 32})", d, du);
     return ttc::set_error(TTC_ERR_UNSUPPORTED, buf);
   }
-  if (N == 0) return TTC_OK;
+  if (N == 0) {
+    // An empty batch has a zero basis gradient (the allocating path's caller sums no slices).
+    // A memset allocates nothing.
+    if (grad_basis == nullptr) return TTC_OK;
+    return ttc::cuda_check(cudaMemsetAsync(grad_basis, 0, sizeof(float) * (size_t)rQ * d * d,
+                                           static_cast<cudaStream_t>(stream)),
+                           "cudaMemsetAsync(grad_basis)");
+  }
   void* g[9] = {grad_A, grad_B, grad_Q, grad_R_inv, nullptr, grad_lgA, grad_lgB, grad_lgQ, grad_h0};
   if (!A_diag || !B || !Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A || !log_gamma_B ||
       !log_gamma_Q || !h0 || !lam0 || !M || !d_u || !grad_A || !grad_B || !grad_Q || !grad_R_inv ||

@@ -139,7 +139,11 @@ class KKTSolveFunction(torch.autograd.Function):
         dtype = Q.dtype
         if dtype not in _DTYPES:
             raise TypeError(f"ttc_b200 'kkt' solver supports float32 and bfloat16, got {dtype}")
-        args = _prepare((A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0), torch.float32)
+        inputs = (A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0)
+        # The inputs are kept in their own dtype for the backward, which converts one row chunk
+        # at a time to fp32: a bf16 layer keeps no full-size fp32 copy between the passes.
+        kept = [t.detach().contiguous() for t in inputs]
+        args = _prepare(kept, torch.float32)
         dev = Q.device
         u = torch.empty(N, nh, du, device=dev, dtype=torch.float32)
         status = torch.zeros(1, device=dev, dtype=torch.int32)
@@ -148,10 +152,10 @@ class KKTSolveFunction(torch.autograd.Function):
             _launch("ttc_lqr_fwd", dev, lib.ttc_lqr_fwd, *[_ptr(a) for a in args], N, nh, d, du, T,
                     _F32, 0, _ptr(u), None, None, _ptr(status))
         check_fwd_status(int(status.item()))
-        ctx.save_for_backward(*args)
+        del args
+        ctx.save_for_backward(*kept)
         ctx.T = T
         ctx.budget = int(save_budget)
-        ctx.in_dtypes = [t.dtype for t in (A_diag, B, Q, R_inv, Q_f, lgA, lgB, lgQ, h0)]
         return u.to(dtype)
 
     @staticmethod
@@ -162,18 +166,18 @@ class KKTSolveFunction(torch.autograd.Function):
         N, nh, d = args[0].shape
         du = args[1].shape[-1]
         # Rows are independent: the two problems' trajectories and the gradient terms built
-        # from them are formed in row chunks of about KKT_WORK_BYTES.
+        # from them are formed in row chunks of about KKT_WORK_BYTES (beyond that budget: the
+        # chunk's fp32 copies of the inputs, and the gradients in the inputs' own dtype).
         rows = max(1, min(N, KKT_WORK_BYTES // (KKT_BYTES_PER_STEP * nh * T * (2 * du + 4 * d))))
         grads = [torch.empty_like(t) for t in args]
         for a in range(0, N, rows):
-            sub = [t[a:a + rows] for t in args]
+            sub = [t[a:a + rows].float() for t in args]
             with torch.profiler.record_function("bwd:kkt rollouts"):
                 fwd, bwd, lam0_b = _rollouts(sub, T, d_u[a:a + rows], ctx.budget)
             A, B, Q, R, _, lA, lB, lQ, h0 = sub
             for out, g in zip(grads, kkt_grads(A, B, Q, R, lA, lB, lQ, h0, T, fwd, bwd, lam0_b)):
                 out[a:a + rows] = g
-            del fwd, bwd, lam0_b
-        grads = [g.to(dt) for g, dt in zip(grads, ctx.in_dtypes)]
+            del fwd, bwd, lam0_b, sub
         return (*grads, None, None)
 
 
