@@ -3,11 +3,14 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl cuda|reference]
 
-One step = TTCLayer forward + backward on one batch of the chosen config (default:
-config 2, fp32, x[4,1024,16,64], h_dim 16, T 64), rows read as [B, L*H, in_dim].  At N > 1
-(torchrun) every rank runs the same per-GPU batch on its own data and the parameter
-gradients are all-reduced (NCCL) inside the step: weak scaling -- except config 5, whose
-global batch of 64 sequences is split over the N GPUs (strong scaling, as BASELINE.json
+One step = TTCLayer forward + backward on one batch of the chosen config, rows read as
+[B, L*H, in_dim], with the parameter gradients and dx of the whole batch (gradient
+accumulation over row micro-batches where one call's activations would not fit).  Default:
+config 3 per GPU (bf16 activations, fp32 solver, x[8,4096,32,128], h_dim 32, T 128), which
+is also config 5's per-GPU shard at 8 GPUs.  At N > 1 (torchrun) every rank runs the same
+per-GPU batch on its own data and the parameter gradients are all-reduced (NCCL) inside the
+step: weak scaling, so N = 8 runs config 5's global batch of 64 sequences.  ``--config 5``
+instead splits config 5's global batch over the N GPUs (strong scaling, as BASELINE.json
 defines it).  Rank 0 prints one JSON line.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle's restatement of the
@@ -47,10 +50,10 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--chunk-rows", type=int, default=0,
-                    help="sequence rows (of L*H) per layer call inside a step (0: auto)")
+                    help="rows (of B*L*H) per layer call inside a step (0: TTCLayer.rows_per_call)")
     ap.add_argument("--batch", type=int, default=0,
                     help="sequences per GPU (0: the config's B); smaller batches for ncu captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -187,25 +190,13 @@ def make_layer(cfg, device, dtype, solver="cuda"):
     return layer.to(device=device, dtype=dtype)
 
 
-def auto_chunk(cfg, dtype):
-    """Sequence rows (dim 1 of x[B, L*H, in]) per layer call so one call's activations
-    stay near 24 GB: the whole batch for configs 1-2, row chunks for configs 3-5."""
-    es = 2 if dtype == torch.bfloat16 else 4
-    d, nh = cfg.h_dim, cfg.H
-    per_row = es * (3 * cfg.width + 4 * nh * d * d + 6 * d * d) + 4 * nh * (4 * d + d * d)
-    fit_rows = max(cfg.B, (24 << 30) // per_row)
-    return max(1, min(cfg.L * cfg.H, fit_rows // cfg.B))
-
-
 def run_step(layer, x, dy, T, chunk, world):
-    """One fwd+bwd over the batch (row chunks when the batch does not fit one call): the
-    parameter gradients and dx, as the end-to-end step and the CPU baseline compute them."""
+    """One fwd+bwd over the batch: TTCLayer.forward_backward (row micro-batches of `chunk`
+    rows, gradient accumulation), the parameter gradients and dx, as the end-to-end step and
+    the CPU baseline compute them; then the gradient all-reduce at N > 1."""
     layer.zero_grad(set_to_none=True)
     x.grad = None
-    rows = x.shape[1]
-    for s in range(0, rows, chunk):
-        y = layer(x[:, s:s + chunk], T)
-        y.backward(dy[:, s:s + chunk])
+    layer.forward_backward(x, dy, T, rows=chunk)
     if world > 1:
         from ttc_b200.parallel import allreduce_grads
         allreduce_grads(layer)
@@ -278,10 +269,20 @@ def reference_arm(args, cfg):
 STRONG_SCALING = {5}
 
 
-def workload_config(cfg, world, args, chunk):
+def workload_name(cfg, world, strong):
+    base = (f"{cfg.name}: TTCLayer fwd+bwd, x[{cfg.B},{cfg.L},{cfg.H},{cfg.in_dim}] per GPU "
+            f"as [B, L*H, in] rows, h_dim={cfg.h_dim}, rank={cfg.rank}, T={cfg.T}")
+    if cfg.name == "cfg3":
+        base += (f"; {cfg.B * world} sequences over {world} GPU(s) (config 5's geometry; at 8 GPUs "
+                 "its global batch of 64)")
+    elif strong:
+        base += f"; config 5's global batch of {cfg.B * world} split over {world} GPU(s)"
+    return base
+
+
+def workload_config(cfg, world, args, chunk, strong=False):
     return {
-        "workload": f"{cfg.name}: TTCLayer fwd+bwd, x[{cfg.B},{cfg.L},{cfg.H},{cfg.in_dim}] per GPU "
-                    f"as [B, L*H, in] rows, h_dim={cfg.h_dim}, rank={cfg.rank}, T={cfg.T}",
+        "workload": workload_name(cfg, world, strong),
         "B_per_gpu": cfg.B, "L": cfg.L, "H": cfg.H, "in_dim": cfg.in_dim, "out_dim": cfg.out_dim,
         "h_dim": cfg.h_dim, "num_heads": cfg.H, "rank": cfg.rank, "T": cfg.T,
         "rows_per_gpu": cfg.rows, "lqr_problems_per_gpu": cfg.problems,
@@ -323,8 +324,8 @@ def main(argv=None):
 
     from ttc_b200.solver import KernelTimer, set_kernel_timer
     layer = make_layer(cfg, device, dtype, args.solver)
-    chunk = args.chunk_rows or auto_chunk(cfg, dtype)
     rows = cfg.L * cfg.H
+    chunk = args.chunk_rows or layer.rows_per_call(cfg.rows, dtype, device)
 
     # Rotating (x, dy) sets on the device, together larger than L2.
     set_bytes = cfg.B * rows * (cfg.in_dim + cfg.out_dim) * (2 if dtype == torch.bfloat16 else 4)
@@ -410,9 +411,7 @@ def main(argv=None):
         dy.record_stream(compute)
         x.requires_grad_(True)
         layer.zero_grad(set_to_none=True)
-        for s in range(0, rows, chunk):
-            y = layer(x[:, s:s + chunk], cfg.T)
-            y.backward(dy[:, s:s + chunk])
+        layer.forward_backward(x, dy, cfg.T, rows=chunk)
         if world > 1:
             from ttc_b200.parallel import allreduce_grads
             allreduce_grads(layer)
@@ -424,6 +423,11 @@ def main(argv=None):
             gx.record_stream(copy_stream)
             dx_host[k % 2].copy_(gx, non_blocking=True)
 
+    # The device-resident loop above is the warm-up of this one (one more step here).  Steps
+    # of seconds (configs 3-5) time a quarter of the steps end to end, at least three, so
+    # that the whole run stays within a few minutes; the copies are then far below 1 % of a
+    # step either way.
+    e2e_steps = args.steps if ms / args.steps < 2000.0 else max(3, args.steps // 4)
     e2e_step(0, fetch(0))
     torch.cuda.synchronize()
     barrier()
@@ -433,9 +437,9 @@ def main(argv=None):
     t0.record()
     copy_stream.wait_event(t0)
     nxt = fetch(0)
-    for k in range(args.steps):
+    for k in range(e2e_steps):
         cur = nxt
-        if k + 1 < args.steps:
+        if k + 1 < e2e_steps:
             nxt = fetch(k + 1)
         e2e_step(k, cur)
     compute.wait_stream(copy_stream)
@@ -455,7 +459,7 @@ def main(argv=None):
         if args.solver == "kkt":
             fwd_ms = fwd_ms[0::2]
         bwd_ms = kern.get("ttc_lqr_bwd", [float("nan")])
-        calls_per_step = math.ceil(rows / chunk)
+        calls_per_step = math.ceil(cfg.rows / chunk)
         probs_per_launch = cfg.problems / calls_per_step
         sm_max = clock_summary.get("sm_max_mhz") or 1965.0
         fp32_peak = SM_COUNT_B200 * FP32_LANES_PER_SM * 2 * sm_max * 1e6 / 1e12
@@ -468,7 +472,7 @@ def main(argv=None):
             "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
             "dtype": "f32" if dtype == torch.float32 else "bf16 activations, f32 solver",
             "data": "synthetic (seeded N(0,1) x and dy, reference init distributions)",
-            "config": workload_config(cfg, world, args, chunk),
+            "config": workload_config(cfg, world, args, chunk, strong),
             "roofline": {
                 "kernel": "ttc_lqr_fwd (sweep + solve + first step)",
                 "bound": "fp32", "achieved": fwd_tflops, "peak": fp32_peak, "unit": "TFLOP/s",
@@ -489,8 +493,8 @@ def main(argv=None):
                    if k not in ("ttc_lqr_fwd", "ttc_lqr_bwd")},
             },
             "clocks": clock_summary,
-            "e2e": {"value": tokens_per_step * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": tokens_per_step * e2e_steps / (e2e_ms / 1000.0), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": launches * world,
             "gpu_launches_per_gpu": launches,
         }

@@ -14,6 +14,7 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU and the built CUDA library")
+    config.addinivalue_line("markers", "fullsize: a GPU test at a BASELINE config's full size (minutes)")
 
 
 @pytest.fixture(scope="session")

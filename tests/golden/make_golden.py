@@ -13,6 +13,7 @@ The Triton ``fused`` solver needs CUDA and is not run here.
 
 Usage:  TTC_REFERENCE_ROOT=<checkout> python tests/golden/make_golden.py        (all fixtures)
         TTC_REFERENCE_ROOT=<checkout> python tests/golden/make_golden.py traj   (trajectory fixtures only)
+        TTC_REFERENCE_ROOT=<checkout> python tests/golden/make_golden.py cfg5   (config-5 and bf16-gradient fixtures only)
 """
 from __future__ import annotations
 
@@ -218,12 +219,56 @@ def main():
     layer_case("layer_cfg4", CONFIGS[4], 1)
     layer_case("layer_cfg3_bf16", CONFIGS[3], 4, dtype=torch.bfloat16, solver="riccati",
                backward=False)
+    # 5. Config 5 (seed 4; config 3's geometry): fp32 y and kkt gradients, and the bf16
+    #    cases below.
+    layer_case("layer_cfg5", CONFIGS[5], 4)
+    bf16_layer_cases()
+
+
+def bf16_layer_cases():
+    """bf16-activation layers (configs 3 and 5): the recommended oracle, fp32 y and kkt
+    gradients on the bf16-rounded x, dy and weights, next to the reference's own bf16 forward
+    (riccati; the reference's kkt backward does not run in bf16: its Riccati solve mixes
+    float and bfloat16 operands, lin_solver_lqr.py:6)."""
+    for cid in (3, 5):
+        cfg = CONFIGS[cid]
+        t0 = time.time()
+        x_np, dy_np = layer_input(cfg, 4)
+        w = {k: torch.from_numpy(v).to(torch.bfloat16) for k, v in layer_weights(cfg).items()}
+        xb = torch.from_numpy(x_np).to(torch.bfloat16)
+        dyb = torch.from_numpy(dy_np).to(torch.bfloat16)
+        out = {"x": x_np, "dy": dy_np, "T": np.array(cfg.T), "rows": np.array(4), "cfg": np.array(cid)}
+        layer = RefTTCLayer(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
+                            solver_impl="kkt")
+        layer.load_state_dict({k: v.float() for k, v in w.items()})
+        x = xb.float()[None].requires_grad_(True)
+        y = layer(x, T=cfg.T)
+        (y * dyb.float()[None]).sum().backward()
+        out["y"] = _np(y[0])
+        out["g_x"] = _np(x.grad[0])
+        for pn, p in layer.named_parameters():
+            g = _np(p.grad)
+            stride = max(1, -(-g.size // MAX_FIXTURE_FLOATS))
+            out["g_" + pn] = g[::stride]
+            out["stride_" + pn] = np.array(stride)
+        ref16 = RefTTCLayer(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
+                            solver_impl="riccati")
+        ref16.load_state_dict({k: v.float() for k, v in w.items()})
+        ref16 = ref16.to(torch.bfloat16)
+        with torch.no_grad():
+            out["y_refbf16"] = _np(ref16(xb[None], T=cfg.T)[0])
+        np.savez_compressed(os.path.join(HERE, f"layer_cfg{cid}_bf16grad.npz"), **out)
+        print(f"layer_cfg{cid}_bf16grad: {time.time() - t0:.1f}s", flush=True)
 
 
 if __name__ == "__main__":
     if sys.argv[1:] == ["traj"]:
         torch.set_num_threads(os.cpu_count() or 1)
         traj_cases()
+    elif sys.argv[1:] == ["cfg5"]:
+        torch.set_num_threads(os.cpu_count() or 1)
+        layer_case("layer_cfg5", CONFIGS[5], 4)
+        bf16_layer_cases()
     else:
         main()
         traj_cases()

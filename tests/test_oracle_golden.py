@@ -73,7 +73,8 @@ def _oracle_layer(cfg, solver, dtype=torch.float32):
 
 
 @pytest.mark.parametrize("case,solver", [("layer_cfg1", "riccati"), ("layer_cfg2", "kkt"),
-                                         ("layer_cfg2", "fused"), ("layer_cfg3", "fused")])
+                                         ("layer_cfg2", "fused"), ("layer_cfg3", "fused"),
+                                         ("layer_cfg5", "fused")])
 def test_layer_matches_reference(case, solver):
     z = load(case)
     cfg = CONFIGS[int(z["cfg"])]
@@ -96,6 +97,28 @@ def test_layer_bf16_matches_reference():
     layer = _oracle_layer(cfg, "riccati", torch.bfloat16)
     y = layer(torch.from_numpy(z["x"]).to(torch.bfloat16)[None], T=int(z["T"]))
     assert O.max_rel(y[0].float(), torch.from_numpy(z["y"])) < 2e-2
+
+
+@pytest.mark.parametrize("cid", [3, 5])
+def test_layer_bf16_rounded_oracle_matches_reference(cid):
+    """The bf16 oracle of configs 3 and 5: the fp32 layer on bf16-rounded x, dy and weights
+    (reference kkt gradients in the fixture), and the reference's own bf16 forward within the
+    bf16 bar of it."""
+    z = load(f"layer_cfg{cid}_bf16grad")
+    cfg = CONFIGS[cid]
+    layer = O.TTCLayerOracle(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
+                             solver_impl="fused")
+    layer.load_state_dict({k: torch.from_numpy(v).to(torch.bfloat16).float()
+                           for k, v in layer_weights(cfg).items()})
+    x = torch.from_numpy(z["x"]).to(torch.bfloat16).float()[None].requires_grad_(True)
+    y = layer(x, T=int(z["T"]))
+    assert O.max_rel(y[0], torch.from_numpy(z["y"])) < 1e-4
+    assert O.max_rel(torch.from_numpy(z["y_refbf16"]), torch.from_numpy(z["y"])) < 2e-2
+    (y[0] * torch.from_numpy(z["dy"]).to(torch.bfloat16).float()).sum().backward()
+    assert O.max_rel(x.grad[0], torch.from_numpy(z["g_x"])) < 1e-3
+    for pn, p in layer.named_parameters():
+        s = int(z["stride_" + pn])
+        assert O.max_rel(p.grad[::s], torch.from_numpy(z["g_" + pn])) < 1e-3, pn
 
 
 def test_kkt_fp64_against_riccati_autograd():

@@ -16,12 +16,19 @@ import math
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+from torch.utils.checkpoint import checkpoint
 
 from .prologue import prologue
 from .reductions import linear, lowrank_mix
 from .solver import (LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_mix_with_status,
                      lqr_solve_with_status, mix_available)
 from . import _lib
+
+
+# Device memory one layer call may keep for its backward (in_proj output, prologue outputs,
+# B / Q mixtures, the solver's saved state), capped further at half the free memory when the
+# call starts.  Larger inputs run in row chunks (see TTCLayer.forward).
+CALL_BUDGET_BYTES = 24 << 30
 
 
 def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
@@ -115,17 +122,80 @@ class TTCLayer(nn.Module):
         materialised as [N, nh, d, d]."""
         return self._materialise(self.mixed_inputs(x2d))
 
+    def call_bytes_per_row(self, dtype: torch.dtype) -> int:
+        """Upper estimate of the device memory one row of a layer call keeps until its
+        backward: in_proj output, prologue outputs, B / Q mixtures, Q_f where it is
+        materialised, and the solver's saved state (lambda0 and M in fp32)."""
+        es = 2 if dtype == torch.bfloat16 else 4
+        nh, d, du = self.num_heads, self.h_dim, self.u_dim
+        width = self.in_proj.out_features
+        return es * (3 * width + 4 * nh * d * d + 3 * d * du + 3 * d * d) + 4 * nh * (4 * d + d * du)
+
+    def rows_per_call(self, N: int, dtype: torch.dtype, device: torch.device) -> int:
+        """Rows one layer call takes so that its saved state stays within CALL_BUDGET_BYTES
+        and half the device's free memory."""
+        budget = CALL_BUDGET_BYTES
+        if device.type == "cuda":
+            free, _ = torch.cuda.mem_get_info(device)
+            budget = min(budget, free // 2)
+        return max(1, min(N, budget // self.call_bytes_per_row(dtype)))
+
     def forward(self, h0: torch.Tensor, T: int) -> torch.Tensor:
         """y = layer(x, T).  x is [bs, seq, in_dim] as in the reference; a 4-D
         [B, L, H, in_dim] input is read as [B, L*H, in_dim] rows and returned as
-        [B, L, H, out_dim]."""
+        [B, L, H, out_dim].
+
+        Rows are independent.  When the whole input would keep more than
+        ``rows_per_call`` rows of backward state, the rows run in chunks of that size, each
+        under activation checkpointing: the forward keeps only the chunk's input, and the
+        backward recomputes one chunk at a time (prologue and solve) before differentiating
+        it, so memory stays bounded at any batch size (config 5, 8.4 M rows, on one GPU)."""
         if h0.dim() == 4:
             b, l, hh, _ = h0.shape
             return self.forward(h0.reshape(b, l * hh, -1), T).reshape(b, l, hh, self.out_dim)
         if T == 0:
             return torch.zeros(h0.shape[0], h0.shape[1], self.out_dim, device=h0.device, dtype=h0.dtype)
         bs, seq_len, in_dim = h0.shape
-        parts = self.mixed_inputs(h0.reshape(-1, in_dim))
+        x2d = h0.reshape(-1, in_dim)
+        N = x2d.shape[0]
+        rows = self.rows_per_call(N, x2d.dtype, x2d.device) if x2d.is_cuda else N
+        if rows >= N:
+            return self._forward_rows(x2d, T).view(bs, seq_len, -1)
+        keep = torch.is_grad_enabled() and (x2d.requires_grad or any(p.requires_grad for p in self.parameters()))
+        outs = []
+        for s in range(0, N, rows):
+            xs = x2d[s:s + rows]
+            if keep:
+                outs.append(checkpoint(self._forward_rows, xs, T, use_reentrant=False))
+            else:
+                outs.append(self._forward_rows(xs, T))
+        return torch.cat(outs).view(bs, seq_len, -1)
+
+    def forward_backward(self, x: torch.Tensor, dy: torch.Tensor, T: int, rows: int | None = None) -> torch.Tensor:
+        """Forward and backward of the layer over row micro-batches (gradient accumulation):
+        each micro-batch of ``rows`` rows (default ``rows_per_call``) runs forward and is
+        immediately differentiated with its slice of the upstream gradient ``dy``, so its
+        saved state is freed before the next one starts.  Parameter gradients accumulate into
+        ``.grad`` and, when ``x`` requires grad, into ``x.grad``, exactly as one
+        ``layer(x, T).backward(dy)`` would; returns y (detached), shaped like ``layer(x, T)``."""
+        if T == 0:  # y = 0 whatever the parameters (ttc_layer.py:101-102): no gradient
+            return torch.zeros(*x.shape[:-1], self.out_dim, device=x.device, dtype=x.dtype)
+        in_dim = x.shape[-1]
+        x2d = x.reshape(-1, in_dim)
+        dy2d = dy.reshape(-1, self.out_dim)
+        N = x2d.shape[0]
+        if rows is None:
+            rows = self.rows_per_call(N, x2d.dtype, x2d.device)
+        y = torch.empty(N, self.out_dim, device=x.device, dtype=x.dtype)
+        for s in range(0, N, rows):
+            ys = self._forward_rows(x2d[s:s + rows], T)
+            ys.backward(dy2d[s:s + rows])
+            y[s:s + rows] = ys.detach()
+        return y.view(*x.shape[:-1], self.out_dim)
+
+    def _forward_rows(self, x2d: torch.Tensor, T: int) -> torch.Tensor:
+        """The layer on rows x2d [N, in_dim] -> y [N, out_dim] (ttc_layer.py:104-153)."""
+        parts = self.mixed_inputs(x2d)
         if self.solver is cuda_lqr_solve:
             N, nh, d = parts[0].shape
             if mix_available(N, nh, d, self.u_dim, parts[5].shape[0], parts[2].dtype):
@@ -146,5 +216,4 @@ class TTCLayer(nn.Module):
             h0_norm = torch.linalg.norm(x0, dim=-1, ord=2).detach()
             u_norm = torch.linalg.norm(u, dim=-1, ord=2).detach()
             u = u / u_norm[..., None] * h0_norm[..., None]
-        y = linear(u.reshape(bs * seq_len, -1), self.out_proj.weight, self.out_proj.bias)
-        return y.view(bs, seq_len, -1)
+        return linear(u.reshape(u.shape[0], -1), self.out_proj.weight, self.out_proj.bias)
