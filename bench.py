@@ -190,16 +190,16 @@ def make_layer(cfg, device, dtype, solver="cuda"):
     return layer.to(device=device, dtype=dtype)
 
 
-def run_step(layer, x, dy, T, chunk, world):
+def run_step(layer, x, dy, T, chunk, world, reducer=None):
     """One fwd+bwd over the batch: TTCLayer.forward_backward (row micro-batches of `chunk`
     rows, gradient accumulation), the parameter gradients and dx, as the end-to-end step and
-    the CPU baseline compute them; then the gradient all-reduce at N > 1."""
+    the CPU baseline compute them.  At N > 1 `reducer` (an OverlappedGradAllReduce) all-reduces
+    each parameter gradient as soon as the last micro-batch's backward has completed it."""
     layer.zero_grad(set_to_none=True)
     x.grad = None
-    layer.forward_backward(x, dy, T, rows=chunk)
-    if world > 1:
-        from ttc_b200.parallel import allreduce_grads
-        allreduce_grads(layer)
+    layer.forward_backward(x, dy, T, rows=chunk, before_last_backward=reducer.arm if reducer else None)
+    if reducer is not None:
+        reducer.wait()
 
 
 # ------------------------------------------------------------------------- CPU legs
@@ -350,8 +350,12 @@ def main(argv=None):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    reducer = None
+    if world > 1:
+        from ttc_b200.parallel import OverlappedGradAllReduce
+        reducer = OverlappedGradAllReduce(layer)
     for k in range(args.warmup):
-        run_step(layer, *sets[k % nsets], cfg.T, chunk, world)
+        run_step(layer, *sets[k % nsets], cfg.T, chunk, world, reducer)
     torch.cuda.synchronize()
 
     # ---- device-resident timed region
@@ -365,7 +369,7 @@ def main(argv=None):
         end = torch.cuda.Event(enable_timing=True)
         start.record()
         for k in range(args.steps):
-            run_step(layer, *sets[k % nsets], cfg.T, chunk, world)
+            run_step(layer, *sets[k % nsets], cfg.T, chunk, world, reducer)
         end.record()
         torch.cuda.synchronize()
         set_kernel_timer(None)
@@ -411,10 +415,10 @@ def main(argv=None):
         dy.record_stream(compute)
         x.requires_grad_(True)
         layer.zero_grad(set_to_none=True)
-        layer.forward_backward(x, dy, cfg.T, rows=chunk)
-        if world > 1:
-            from ttc_b200.parallel import allreduce_grads
-            allreduce_grads(layer)
+        layer.forward_backward(x, dy, cfg.T, rows=chunk,
+                               before_last_backward=reducer.arm if reducer else None)
+        if reducer is not None:
+            reducer.wait()
         done = torch.cuda.Event()
         done.record(compute)
         gx = x.grad.view(cfg.rows, cfg.in_dim)

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define TTC_ABI_VERSION 5
+#define TTC_ABI_VERSION 6
 
 #define TTC_DTYPE_F32 0
 #define TTC_DTYPE_BF16 1
@@ -192,6 +192,48 @@ int ttc_lqr_bwd_mix_noalloc(const void* A_diag, const void* B, const void* Q, co
                             void* grad_B, void* grad_Q, void* grad_R_inv, void* grad_coeff_Qf,
                             float* grad_basis, void* grad_lgA, void* grad_lgB, void* grad_lgQ,
                             void* grad_h0, int* status, void* stream);
+
+/*
+ * The layer's whole low-rank solve: ttc_lqr_fwd_mix with B and Q given as the layer's
+ * low-rank mixtures too (ttc/layers/ttc_layer.py:115-123, the einsums of coeff_B with Bs and of
+ * coeff_Q with Qs), so that no [N,d,du] B or [N,d,d] Q tensor exists either:
+ *   B[n] = sum_r coeff_B[n,r] B_basis[r],  Q[n] = sum_r coeff_Q[n,r] Q_basis[r],
+ * coeff_B [N,rB], B_basis [rB,d,du], coeff_Q [N,rQ] in the activation dtype; Q_basis [rQ,d,d]
+ * is the basis of the Q_f mixture as well (the layer's Qs, or Qs Qs^T / sqrt(d) for its
+ * cholesky reparametrisation).  Each sum runs in fp32 in rank order and is rounded to the
+ * activation dtype, as the einsum it replaces.  Everything else as ttc_lqr_fwd_mix.
+ */
+int ttc_lqr_fwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_basis, int rB,
+                        const void* coeff_Q, const void* R_inv, const void* coeff_Qf, const void* Q_basis,
+                        int rQ, const void* log_gamma_A, const void* log_gamma_B, const void* log_gamma_Q,
+                        const void* h0, int64_t N, int nh, int d, int du, int T, int dtype, int flags,
+                        void* u, float* lam0, float* M, int* status, void* stream);
+
+/*
+ * Backward of ttc_lqr_fwd_lowrank (saved lam0 and M required; d = du in {16, 32}).  In place of
+ * grad_B, grad_Q and grad_Q_f it writes, in the activation dtype, grad_coeff_B [N,rB] =
+ * <grad_B[n], B_basis[r]>, grad_coeff_Q [N,rQ] = <grad_Q[n], Q_basis[r]> and grad_coeff_Qf
+ * [N,nh,rQ] (as ttc_lqr_bwd_mix), and per-CTA fp32 partial sums of the basis gradients:
+ * grad_B_basis_partial [slices,rB,d,du] (the B-basis gradient is their sum) and
+ * grad_basis_partial [slices,rQ,d,d] (the Q-basis gradient is (S + S^T) / 2 with S their sum:
+ * the Q_f terms of ttc_lqr_bwd_mix plus sum_n coeff_Q[n,r] grad_Q[n]).  slices from
+ * ttc_lqr_bwd_mix_slices; every slice is written.  Other outputs as ttc_lqr_bwd.
+ */
+int ttc_lqr_bwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_basis, int rB,
+                        const void* coeff_Q, const void* R_inv, const void* coeff_Qf, const void* Q_basis,
+                        int rQ, const void* log_gamma_A, const void* log_gamma_B, const void* log_gamma_Q,
+                        const void* h0, const float* lam0, const float* M, const void* d_u, int64_t N,
+                        int nh, int d, int du, int T, int dtype, void* grad_A, void* grad_coeff_B,
+                        float* grad_B_basis_partial, void* grad_coeff_Q, void* grad_R_inv,
+                        void* grad_coeff_Qf, float* grad_basis_partial, int64_t slices, void* grad_lgA,
+                        void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status, void* stream);
+
+/* Layer epilogue (replaces the fla l2norm of u, ttc/layers/ttc_layer.py:142-143): for each
+ * of `rows` rows of n <= 64 values (activation dtype, contiguous),
+ *   y = x rsqrt(sum x^2 + 1e-6)   (fp32, rounded to the activation dtype; fla/modules/l2norm.py:42)
+ * and its backward  dx = rs g - x rs^3 sum(g x)  with rs = rsqrt(sum x^2 + 1e-6) recomputed from x. */
+int ttc_rownorm_fwd(const void* x, int64_t rows, int n, int dtype, void* y, void* stream);
+int ttc_rownorm_bwd(const void* x, const void* g, int64_t rows, int n, int dtype, void* dx, void* stream);
 
 /* Elementwise layer prologue (replaces the PyTorch ops of ttc/layers/ttc_layer.py:106-133
  * between in_proj and the low-rank einsums; the einsums stay with the caller).

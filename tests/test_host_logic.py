@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from oracle import ttc_oracle as O
-from prologue_ref import prologue_torch
+from prologue_ref import _l2norm, prologue_torch
 from ttc_cases import CONFIGS, layer_weights
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -20,9 +20,10 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 @pytest.fixture
 def cpu_prologue(monkeypatch):
-    """Swap the layer's CUDA prologue for the PyTorch one (test-only)."""
+    """Swap the layer's CUDA prologue and epilogue for PyTorch ones (test-only)."""
     import ttc_b200.layer as L
     monkeypatch.setattr(L, "prologue", prologue_torch)
+    monkeypatch.setattr(L, "rownorm", _l2norm)
 
 
 def test_product_layer_has_no_cpu_path():

@@ -20,8 +20,9 @@ def _free_port():
 
 def _use_cpu_prologue(setattr_fn=setattr):
     import ttc_b200.layer as L
-    from prologue_ref import prologue_torch
+    from prologue_ref import _l2norm, prologue_torch
     setattr_fn(L, "prologue", prologue_torch)  # CPU stand-in for the CUDA prologue
+    setattr_fn(L, "rownorm", _l2norm)          # and for the CUDA epilogue
 
 
 def _layer():
@@ -39,7 +40,7 @@ def _data():
         torch.randn(4, 6, 6, generator=g, dtype=torch.float64)
 
 
-def _worker(rank, world, port, out_dir, fail_rank):
+def _worker(rank, world, port, out_dir, fail_rank, overlapped=False):
     for p in (os.path.dirname(HERE), os.path.join(os.path.dirname(HERE), "ttc-net_b200"), HERE):
         sys.path.insert(0, p)
     import datetime
@@ -53,6 +54,17 @@ def _worker(rank, world, port, out_dir, fail_rank):
     layer = _layer()
     x, dy = _data()
     xs, dys = shard_rows(x, rank, world), shard_rows(dy, rank, world)
+    if overlapped:
+        # micro-batches of 5 rows, each gradient all-reduced as soon as the last one has
+        # completed it (the bench's N > 1 step)
+        from ttc_b200.parallel import OverlappedGradAllReduce
+        red = OverlappedGradAllReduce(layer)
+        layer.forward_backward(xs, dys, 5, rows=5, before_last_backward=red.arm)
+        red.wait()
+        torch.save({n: p.grad for n, p in layer.named_parameters()},
+                   os.path.join(out_dir, f"grads{rank}.pt"))
+        dist.destroy_process_group()
+        return
     y = layer(xs, T=5)
     y.backward(dys)
     if rank == fail_rank:
@@ -63,10 +75,10 @@ def _worker(rank, world, port, out_dir, fail_rank):
     dist.destroy_process_group()
 
 
-def _run(world, tmp_path, fail_rank=-1):
+def _run(world, tmp_path, fail_rank=-1, overlapped=False):
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path), fail_rank))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path), fail_rank, overlapped))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -82,6 +94,21 @@ def _run(world, tmp_path, fail_rank=-1):
 def test_sharded_gradients_equal_full_batch(tmp_path, monkeypatch):
     _use_cpu_prologue(monkeypatch.setattr)
     codes = _run(2, tmp_path)
+    assert codes == [0, 0]
+    layer = _layer()
+    x, dy = _data()
+    layer(x, T=5).backward(dy)
+    for r in range(2):
+        g = torch.load(os.path.join(tmp_path, f"grads{r}.pt"))
+        for n, p in layer.named_parameters():
+            assert torch.allclose(g[n], p.grad, rtol=1e-10, atol=1e-12), n
+
+
+def test_overlapped_allreduce_of_micro_batches_equals_full_batch(tmp_path, monkeypatch):
+    """forward_backward over micro-batches with each parameter's all-reduce started from its
+    post-accumulate hook gives every rank the full-batch gradients."""
+    _use_cpu_prologue(monkeypatch.setattr)
+    codes = _run(2, tmp_path, overlapped=True)
     assert codes == [0, 0]
     layer = _layer()
     x, dy = _data()

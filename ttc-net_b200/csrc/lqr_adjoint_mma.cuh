@@ -316,7 +316,7 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                    TIn* __restrict__ glgB_out, TIn* __restrict__ glgQ_out, TIn* __restrict__ gh0_out,
                    const TIn* __restrict__ Qbasis, int rQ, const TIn* __restrict__ cQf,
                    TIn* __restrict__ gcQf_out, float* __restrict__ gQb_partial,
-                   int* __restrict__ status) {
+                   int* __restrict__ status, LowRank<TIn> lr) {
   using C = AdjMma<D>;
   constexpr int NT = C::NT, MT = C::MT;
   extern __shared__ __align__(128) float smem[];
@@ -336,6 +336,14 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     slice = gQb_partial + (int64_t)blockIdx.x * rQ * D * D;
     for (int e = tid; e < rQ * D * D; e += nthreads) slice[e] = 0.f;
   }
+  // Low-rank B / Q (which needs the mixed Q_f above): the CTA's partial of the B-basis
+  // gradient, and each row's B and Q formed from its coefficients.
+  const bool lowrank = lr.cB != nullptr && Qbasis != nullptr;
+  float* bslice = nullptr;
+  if (lowrank) {
+    bslice = lr.gBb + (int64_t)blockIdx.x * lr.rB * D * D;
+    for (int e = tid; e < lr.rB * D * D; e += nthreads) bslice[e] = 0.f;
+  }
   bool bad = false;
   const int64_t ngroups = (N + rows_per_cta - 1) / rows_per_cta;
   for (int64_t grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
@@ -350,6 +358,27 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       const int64_t nr = n0 + r;
       if (nr >= N) break;
       float* base = rows_s + r * C::kRow;
+      if (lowrank) {
+        // B and Q of the row, mixed into the (still unused) staging area first
+        float* tB = warp_s;
+        float* tQ = warp_s + D * D;
+        const TIn* cBn = lr.cB + nr * lr.rB;
+        const TIn* cQn = lr.cQ + nr * rQ;
+        for (int e = tid; e < D * D; e += nthreads) {
+          tB[e] = mix_elem<TIn>(cBn, lr.Bb, lr.rB, D * D, e);
+          tQ[e] = mix_elem<TIn>(cQn, Qbasis, rQ, D * D, e);
+        }
+        __syncthreads();
+        build_operand<D>(base, [&](int k, int c) { return tQ[c * D + k]; }, tid, nthreads);
+        build_operand<D>(base + C::kFrag, [&](int k, int c) { return tB[k * D + c]; }, tid, nthreads);
+        build_operand<D>(base + 2 * C::kFrag, [&](int k, int c) { return tB[c * D + k]; }, tid, nthreads);
+        build_operand<D>(base + 3 * C::kFrag, [&](int k, int c) { return tQ[k * D + c]; }, tid, nthreads);
+        bool asym = false;
+        for (int e = tid; e < D * D; e += nthreads) asym |= tQ[e] != tQ[(e % D) * D + e / D];
+        if (asym) reinterpret_cast<int*>(base + 4 * C::kFrag)[0] = 0;
+        __syncthreads();
+        continue;
+      }
       const TIn* Bn = Bm + nr * (D * D);
       const TIn* Qn = Qm + nr * (D * D);
       build_operand<D>(base, [&](int k, int c) { return ldf(Qn + c * D + k); }, tid, nthreads);
@@ -640,7 +669,11 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
             v *= 0.5f;
           }
           bad |= unstable(v);
-          stf((e < D * D ? gB_out : gQ_out) + nr * (D * D) + (e % (D * D)), v);
+          if (lowrank) {
+            rows_s[r * C::kRow + e] = v;  // the row's [grad_B | grad_Q] for the contractions
+          } else {
+            stf((e < D * D ? gB_out : gQ_out) + nr * (D * D) + (e % (D * D)), v);
+          }
         }
       }
     } else if (row_ok) {
@@ -653,15 +686,59 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
           const int mi = isq ? unit - MT : unit;
           const float sc = isq ? 0.5f : 1.0f;
           TIn* out = (isq ? gQ_out : gB_out) + n * (D * D);
+          // low-rank: into the row's [grad_B | grad_Q] buffer (the operands are no longer read:
+          // every warp passed the barrier before the Q_f contractions)
+          float* buf = rows_s + rloc * C::kRow + (isq ? D * D : 0);
 #pragma unroll
           for (int nj = 0; nj < NT; ++nj) {
             const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
             const float v[4] = {sc * acc[q][nj][0], sc * acc[q][nj][1], sc * acc[q][nj][2], sc * acc[q][nj][3]};
             bad |= unstable(v[0]) | unstable(v[1]) | unstable(v[2]) | unstable(v[3]);
-            stf(out + r0 * D + c0, v[0]);
-            stf(out + r0 * D + c0 + 1, v[1]);
-            stf(out + (r0 + 8) * D + c0, v[2]);
-            stf(out + (r0 + 8) * D + c0 + 1, v[3]);
+            if (lowrank) {
+              buf[r0 * D + c0] = v[0];
+              buf[r0 * D + c0 + 1] = v[1];
+              buf[(r0 + 8) * D + c0] = v[2];
+              buf[(r0 + 8) * D + c0 + 1] = v[3];
+            } else {
+              stf(out + r0 * D + c0, v[0]);
+              stf(out + r0 * D + c0 + 1, v[1]);
+              stf(out + (r0 + 8) * D + c0, v[2]);
+              stf(out + (r0 + 8) * D + c0 + 1, v[3]);
+            }
+          }
+        }
+      }
+    }
+    if (lowrank) {
+      // grad_coeff_B / grad_coeff_Q of the group's rows and their terms of the basis
+      // gradients.  Each basis index is handled by one warp (a CTA barrier separates this
+      // from the Q_f contractions, which update the same Q slices), rows in order:
+      // deterministic.
+      __syncthreads();
+      const int nw = nthreads >> 5;
+      for (int r = 0; r < rows_per_cta; ++r) {
+        const int64_t nr = n0 + r;
+        if (nr >= N) break;
+        const float* gBr = rows_s + r * C::kRow;
+        const float* gQr = gBr + D * D;
+        for (int k = warp; k < lr.rB + rQ; k += nw) {
+          const bool isb = k < lr.rB;
+          const int rr = isb ? k : k - lr.rB;
+          const float* gr = isb ? gBr : gQr;
+          const TIn* bas = (isb ? lr.Bb : Qbasis) + (int64_t)rr * D * D;
+          float* sl = (isb ? bslice : slice) + (int64_t)rr * D * D;
+          const float c = ldf((isb ? lr.cB + nr * lr.rB : lr.cQ + nr * rQ) + rr);
+          float dot = 0.f;
+          for (int e = lane; e < D * D; e += 32) {
+            const float gv = gr[e];
+            dot = fmaf(gv, ldf(bas + e), dot);
+            sl[e] = fmaf(c, gv, sl[e]);
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+          if (lane == 0) {
+            bad |= unstable(dot);
+            stf((isb ? lr.gcB + nr * lr.rB : lr.gcQ + nr * rQ) + rr, dot);
           }
         }
       }

@@ -19,6 +19,45 @@ __device__ __forceinline__ float ldf(const __nv_bfloat16* p) { return __bfloat16
 __device__ __forceinline__ void stf(float* p, float v) { *p = v; }
 __device__ __forceinline__ void stf(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
 
+// Rounds to the activation dtype (identity for float).
+template <typename T>
+__device__ __forceinline__ float round_to(float x) {
+  if constexpr (sizeof(T) == 2) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  } else {
+    return x;
+  }
+}
+
+// The layer's low-rank parametrisation of B and Q (ttc_layer.py:115-123): per batch row n
+// B[n] = sum_r coeff_B[n][r] B_basis[r] and Q[n] = sum_r coeff_Q[n][r] Q_basis[r], formed
+// by the solver kernels instead of being read as [N, d, du] / [N, d, d] tensors.  Q_basis is
+// the basis of the Q_f mixture too.  Backward outputs: grad_coeff_B [N, rB] and
+// grad_coeff_Q [N, rQ] = <grad_B[n], B_basis[r]>, <grad_Q[n], Q_basis[r]>, and per-CTA
+// partial sums of sum_n coeff[n][r] grad[n] (the basis gradients; Q's go into the Q_f
+// mixture's partial slices).  cB == nullptr: B and Q are read as tensors.
+template <typename TIn>
+struct LowRank {
+  const TIn* cB = nullptr;
+  const TIn* Bb = nullptr;
+  int rB = 0;
+  const TIn* cQ = nullptr;
+  TIn* gcB = nullptr;
+  TIn* gcQ = nullptr;
+  float* gBb = nullptr;  // [gridDim.x][rB][d][du]
+};
+
+// Element e of the mixture sum_r c[r] basis[r][e] (each basis matrix `len` elements),
+// summed in rank order in fp32 and rounded to the activation dtype like the einsum it
+// replaces.
+template <typename TIn>
+__device__ __forceinline__ float mix_elem(const TIn* __restrict__ c, const TIn* __restrict__ basis, int rank,
+                                          int len, int e) {
+  float s = 0.f;
+  for (int r = 0; r < rank; ++r) s = fmaf(ldf(c + r), ldf(basis + (int64_t)r * len + e), s);
+  return round_to<TIn>(s);
+}
+
 // True for NaN, +-Inf and |v| >= 1e6: the reference's isnan | isinf | abs >= 1e6.
 __device__ __forceinline__ bool unstable(float v) { return !(fabsf(v) < kUnstable); }
 

@@ -39,6 +39,31 @@ struct QMix {
   int rank = 0;
   void* grad_coeff = nullptr;
   float* grad_basis_partial = nullptr;
+  // B and Q given as the layer's low-rank mixtures as well (needs the Q_f mixture): the B and
+  // Q arguments are then unused.  B = sum_r coeff_B[n][r] B_basis[r] (B_basis [rB, d, du]),
+  // Q = sum_r coeff_Q[n][r] basis[r]; the backward writes grad_coeff_B [N, rB],
+  // grad_coeff_Q [N, rQ], adds the Q-basis terms to grad_basis_partial and writes the
+  // B-basis terms to grad_B_basis_partial (slices x [rB, d, du] fp32), in place of grad_B
+  // and grad_Q.
+  const void* coeff_B = nullptr;
+  const void* B_basis = nullptr;
+  int rB = 0;
+  const void* coeff_Q = nullptr;
+  void* grad_coeff_B = nullptr;
+  void* grad_coeff_Q = nullptr;
+  float* grad_B_basis_partial = nullptr;
+  template <typename TIn>
+  LowRank<TIn> lowrank() const {
+    LowRank<TIn> lr;
+    lr.cB = static_cast<const TIn*>(coeff_B);
+    lr.Bb = static_cast<const TIn*>(B_basis);
+    lr.rB = rB;
+    lr.cQ = static_cast<const TIn*>(coeff_Q);
+    lr.gcB = static_cast<TIn*>(grad_coeff_B);
+    lr.gcQ = static_cast<TIn*>(grad_coeff_Q);
+    lr.gBb = grad_B_basis_partial;
+    return lr;
+  }
 };
 
 template <int D, int DU, typename TIn>
@@ -120,7 +145,7 @@ int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, co
   k<<<dim3((unsigned)N), dim3(slots * 128), smem, st>>>(
       (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf,
       (const TIn*)mix.basis, mix.rank, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0,
-      nh, T, opts, cols, (TIn*)u, lam0, M, status);
+      nh, T, opts, cols, (TIn*)u, lam0, M, status, mix.lowrank<TIn>());
   return cuda_check(cudaGetLastError(), "lqr_fwd_tc_kernel launch");
 }
 
@@ -183,7 +208,7 @@ int launch_bwd_mma(const void* A, const void* B, const void* Q, const void* R, c
       (const TIn*)lQ, (const TIn*)h0, lam0, M_or_dp, (const TIn*)dU, N, nh, T, rpc, (TIn*)g[0],
       (TIn*)g[1], (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6], (TIn*)g[7],
       (TIn*)g[8], (const TIn*)mix.basis, mix.rank, (const TIn*)coeff_Qf, (TIn*)mix.grad_coeff,
-      mix.grad_basis_partial, status);
+      mix.grad_basis_partial, status, mix.lowrank<TIn>());
   return cuda_check(cudaGetLastError(), "lqr_bwd_mma_kernel launch");
 }
 

@@ -415,7 +415,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                   const TIn* __restrict__ lgB, const TIn* __restrict__ lgQ,
                   const TIn* __restrict__ H0, int nh, int T, int opts, uint32_t tmem_cols,
                   TIn* __restrict__ u_out, float* __restrict__ lam0_out, float* __restrict__ M_out,
-                  int* __restrict__ status) {
+                  int* __restrict__ status, LowRank<TIn> lr) {
   using CF = TcCfg<D, DU>;
   using L = TcFwdLayout<D, DU, SAVE_M>;
   using V = SweepVec<D, DU>;
@@ -433,10 +433,13 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   const Group<D> G(tid);
   const int64_t n = blockIdx.x;
 
-  // The row's operands, split into tf32 hi and residual.
+  // The row's operands, split into tf32 hi and residual.  With the layer's low-rank
+  // parametrisation B and Q are mixed here from the row's coefficients and the bases.
+  const TIn* cBn = lr.cB != nullptr ? lr.cB + n * lr.rB : nullptr;
+  const TIn* cQn = lr.cB != nullptr ? lr.cQ + n * rQ : nullptr;
   for (int e = tid; e < D * DU; e += blockDim.x) {
     const int k = e / DU, j = e % DU;
-    const float b = ldf(Bm + n * (D * DU) + e);
+    const float b = cBn != nullptr ? mix_elem<TIn>(cBn, lr.Bb, lr.rB, D * DU, e) : ldf(Bm + n * (D * DU) + e);
     const float hi = tc::tf32_trunc(b), lo = b - hi;
     ops[CF::kO1 + tc::canon(j, k, DU)] = hi;
     ops[CF::kO1 + D * DU + tc::canon(j, k, DU)] = lo;
@@ -445,7 +448,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   }
   for (int e = tid; e < D * D; e += blockDim.x) {
     const int j = e / D, k = e % D;
-    const float q = ldf(Qm + n * (D * D) + e);
+    const float q = cQn != nullptr ? mix_elem<TIn>(cQn, Qbasis, rQ, D * D, e) : ldf(Qm + n * (D * D) + e);
     const float hi = tc::tf32_trunc(q);
     ops[CF::kO3 + tc::canon(k, j, D)] = hi;
     ops[CF::kO3 + D * D + tc::canon(k, j, D)] = q - hi;

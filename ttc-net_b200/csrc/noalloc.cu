@@ -94,7 +94,7 @@ int launch_noalloc(const void* A, const void* B, const void* Q, const void* R, c
       (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)lA, (const TIn*)lB,
       (const TIn*)lQ, (const TIn*)h0, lam0, M, (const TIn*)dU, N, nh, T, C::rows_per_cta(nh),
       (TIn*)g[0], (TIn*)g[1], (TIn*)g[2], (TIn*)g[3], nullptr, (TIn*)g[5], (TIn*)g[6], (TIn*)g[7],
-      (TIn*)g[8], (const TIn*)basis, rQ, (const TIn*)cQf, (TIn*)gcQf, scratch, status);
+      (TIn*)g[8], (const TIn*)basis, rQ, (const TIn*)cQf, (TIn*)gcQf, scratch, status, ttc::LowRank<TIn>{});
   if (int rc = ttc::cuda_check(cudaGetLastError(), "lqr_bwd_mma_kernel launch")) return rc;
   const int64_t blocks = (per + 255) / 256;
   basis_reduce_kernel<<<dim3((unsigned)(blocks < 1024 ? blocks : 1024)), dim3(256), 0, st>>>(scratch, grid, rQ, D,

@@ -313,6 +313,44 @@ __global__ void __launch_bounds__(256) prologue_bwd_kernel(
   }
 }
 
+// Epilogue: l2norm over rows of n <= SEG * PER values (the layer's u, ttc_layer.py:142-143),
+// one segment of SEG lanes per row.
+template <int SEG, int PER, typename T>
+__global__ void __launch_bounds__(256) rownorm_fwd_kernel(const T* __restrict__ x, int64_t rows, int n,
+                                                          T* __restrict__ y) {
+  constexpr int RPW = 32 / SEG;
+  const int lane = threadIdx.x & 31, seg = lane / SEG, ls = lane % SEG;
+  const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5) * RPW;
+  for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW; r0 < rows;
+       r0 += stride) {
+    const int64_t r = r0 + seg;
+    const int len = r < rows ? n : 0;  // a segment past the last row runs the shuffles only
+    const int64_t off = (r < rows ? r : 0) * n;
+    Vec<PER> v;
+    l2norm_fwd<SEG, PER, T>(load_vec<SEG, PER>(x + off, len, ls), v);
+    store_vec<SEG, PER>(y + off, v, ls);
+  }
+}
+
+template <int SEG, int PER, typename T>
+__global__ void __launch_bounds__(256) rownorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ g,
+                                                          int64_t rows, int n, T* __restrict__ dx) {
+  constexpr int RPW = 32 / SEG;
+  const int lane = threadIdx.x & 31, seg = lane / SEG, ls = lane % SEG;
+  const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5) * RPW;
+  for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW; r0 < rows;
+       r0 += stride) {
+    const int64_t r = r0 + seg;
+    const int len = r < rows ? n : 0;
+    const int64_t off = (r < rows ? r : 0) * n;
+    const Vec<PER> xv = load_vec<SEG, PER>(x + off, len, ls);
+    Vec<PER> y, d;
+    const float rs = l2norm_fwd<SEG, PER, T>(xv, y);
+    l2norm_bwd<SEG, PER, T>(xv, rs, load_vec<SEG, PER>(g + off, len, ls), d);
+    store_vec<SEG, PER>(dx + off, d, ls);
+  }
+}
+
 int check_dims(int64_t N, int nh, int d, int du, int rB, int rQ, int dtype) {
   if (N < 0 || nh < 1 || d < 1 || du < 1 || rB < 1 || rQ < 1)
     return ttc::set_error(TTC_ERR_INVALID, "prologue: sizes must be positive");
@@ -336,6 +374,39 @@ int launched(const char* what) {
   snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
   return ttc::set_error(TTC_ERR_CUDA, buf);
 }
+
+template <typename T>
+int rownorm_launch(const void* x, const void* g, int64_t rows, int n, void* out, cudaStream_t st) {
+  const int seg = n <= 16 ? 16 : 32;
+  const int64_t warps = (rows + (32 / seg) - 1) / (32 / seg);
+  const unsigned grid = grid_for(warps);
+#define TTC_RN(SEG, PER)                                                                                   \
+  do {                                                                                                     \
+    if (g == nullptr)                                                                                      \
+      rownorm_fwd_kernel<SEG, PER, T><<<grid, 256, 0, st>>>((const T*)x, rows, n, (T*)out);               \
+    else                                                                                                   \
+      rownorm_bwd_kernel<SEG, PER, T><<<grid, 256, 0, st>>>((const T*)x, (const T*)g, rows, n, (T*)out);  \
+  } while (0)
+  if (n <= 16) {
+    TTC_RN(16, 1);
+  } else if (n <= 32) {
+    TTC_RN(32, 1);
+  } else {
+    TTC_RN(32, 2);
+  }
+#undef TTC_RN
+  return launched(g == nullptr ? "rownorm_fwd_kernel launch" : "rownorm_bwd_kernel launch");
+}
+
+int rownorm_checks(const void* x, int64_t rows, int n, int dtype, const void* out) {
+  if (rows < 0 || n < 1) return ttc::set_error(TTC_ERR_INVALID, "rownorm: rows must be >= 0 and n >= 1");
+  if (n > kMaxLen) return ttc::set_error(TTC_ERR_UNSUPPORTED, "rownorm: rows longer than 64 values");
+  if (dtype != TTC_DTYPE_F32 && dtype != TTC_DTYPE_BF16)
+    return ttc::set_error(TTC_ERR_INVALID, "rownorm: dtype must be TTC_DTYPE_F32 or TTC_DTYPE_BF16");
+  if (rows > 0 && (!x || !out)) return ttc::set_error(TTC_ERR_INVALID, "rownorm: null pointer");
+  return TTC_OK;
+}
+
 
 template <int SEG, int PER, typename T>
 int fwd_launch(const void* Z, int64_t N, const Dims& D, void* const* o, cudaStream_t st) {
@@ -407,4 +478,22 @@ extern "C" int ttc_prologue_bwd(const void* Z, int64_t N, int nh, int d, int du,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == TTC_DTYPE_F32 ? bwd_typed<float>(Z, N, D, g, dZ, st)
                                 : bwd_typed<__nv_bfloat16>(Z, N, D, g, dZ, st);
+}
+
+extern "C" int ttc_rownorm_fwd(const void* x, int64_t rows, int n, int dtype, void* y, void* stream) {
+  if (int rc = rownorm_checks(x, rows, n, dtype, y)) return rc;
+  if (rows == 0) return TTC_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == TTC_DTYPE_F32 ? rownorm_launch<float>(x, nullptr, rows, n, y, st)
+                                : rownorm_launch<__nv_bfloat16>(x, nullptr, rows, n, y, st);
+}
+
+extern "C" int ttc_rownorm_bwd(const void* x, const void* g, int64_t rows, int n, int dtype, void* dx,
+                               void* stream) {
+  if (int rc = rownorm_checks(x, rows, n, dtype, dx)) return rc;
+  if (rows == 0) return TTC_OK;
+  if (!g) return ttc::set_error(TTC_ERR_INVALID, "rownorm_bwd: null gradient");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == TTC_DTYPE_F32 ? rownorm_launch<float>(x, g, rows, n, dx, st)
+                                : rownorm_launch<__nv_bfloat16>(x, g, rows, n, dx, st);
 }

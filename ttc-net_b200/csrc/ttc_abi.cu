@@ -215,4 +215,81 @@ int ttc_lqr_bwd_mix(const void* A_diag, const void* B, const void* Q, const void
 #undef TTC_BWD
 }
 
+int ttc_lqr_fwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_basis, int rB,
+                        const void* coeff_Q, const void* R_inv, const void* coeff_Qf, const void* Q_basis,
+                        int rQ, const void* log_gamma_A, const void* log_gamma_B, const void* log_gamma_Q,
+                        const void* h0, int64_t N, int nh, int d, int du, int T, int dtype, int flags,
+                        void* u, float* lam0, float* M, int* status, void* stream) {
+  if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (int rc = check_flags(flags)) return rc;
+  if (rQ < 1 || rB < 1) return fail(TTC_ERR_INVALID, "ranks of the B and Q mixtures must be >= 1");
+  if (N == 0) return TTC_OK;
+  if (!A_diag || !coeff_B || !B_basis || !coeff_Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A ||
+      !log_gamma_B || !log_gamma_Q || !h0 || !u || !status)
+    return fail(TTC_ERR_INVALID, "null pointer argument");
+  ttc::QMix mix;
+  mix.basis = Q_basis;
+  mix.rank = rQ;
+  mix.coeff_B = coeff_B;
+  mix.B_basis = B_basis;
+  mix.rB = rB;
+  mix.coeff_Q = coeff_Q;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define TTC_FWD(DD, DDU, TT)                                                                   \
+  return ttc::launch_fwd<DD, DDU, TT>(A_diag, nullptr, nullptr, R_inv, coeff_Qf, log_gamma_A, log_gamma_B, \
+                                      log_gamma_Q, h0, N, nh, T, u, lam0, M, status, mix, flags, st)
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_FWD, float);
+  TTC_FOR_DIMS(TTC_FWD, __nv_bfloat16);
+#undef TTC_FWD
+}
+
+int ttc_lqr_bwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_basis, int rB,
+                        const void* coeff_Q, const void* R_inv, const void* coeff_Qf, const void* Q_basis,
+                        int rQ, const void* log_gamma_A, const void* log_gamma_B, const void* log_gamma_Q,
+                        const void* h0, const float* lam0, const float* M, const void* d_u, int64_t N,
+                        int nh, int d, int du, int T, int dtype, void* grad_A, void* grad_coeff_B,
+                        float* grad_B_basis_partial, void* grad_coeff_Q, void* grad_R_inv,
+                        void* grad_coeff_Qf, float* grad_basis_partial, int64_t slices, void* grad_lgA,
+                        void* grad_lgB, void* grad_lgQ, void* grad_h0, int* status, void* stream) {
+  if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (rQ < 1 || rB < 1) return fail(TTC_ERR_INVALID, "ranks of the B and Q mixtures must be >= 1");
+  if (N == 0) return TTC_OK;
+  if (!A_diag || !coeff_B || !B_basis || !coeff_Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A ||
+      !log_gamma_B || !log_gamma_Q || !h0 || !d_u || !status || !lam0 || !M || !grad_basis_partial ||
+      !grad_B_basis_partial)
+    return fail(TTC_ERR_INVALID, "null pointer argument (the low-rank backward needs lam0 and M)");
+  void* g[9] = {grad_A, nullptr, nullptr, grad_R_inv, nullptr, grad_lgA, grad_lgB, grad_lgQ, grad_h0};
+  for (int i = 0; i < 9; ++i)
+    if ((i == 0 || i == 3 || i > 4) && !g[i]) return fail(TTC_ERR_INVALID, "null gradient pointer");
+  if (!grad_coeff_Qf || !grad_coeff_B || !grad_coeff_Q) return fail(TTC_ERR_INVALID, "null gradient pointer");
+  const int64_t need = ttc_lqr_bwd_mix_slices(N, nh, d, du, rQ, dtype);
+  if (need < 0) return static_cast<int>(-need);
+  if (need == 0) return fail(TTC_ERR_UNSUPPORTED, "no low-rank backward for this shape");
+  if (slices != need) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "the basis partials have %lld slices, this launch needs %lld",
+             (long long)slices, (long long)need);
+    return fail(TTC_ERR_INVALID, buf);
+  }
+  ttc::QMix mix;
+  mix.basis = Q_basis;
+  mix.rank = rQ;
+  mix.grad_coeff = grad_coeff_Qf;
+  mix.grad_basis_partial = grad_basis_partial;
+  mix.coeff_B = coeff_B;
+  mix.B_basis = B_basis;
+  mix.rB = rB;
+  mix.coeff_Q = coeff_Q;
+  mix.grad_coeff_B = grad_coeff_B;
+  mix.grad_coeff_Q = grad_coeff_Q;
+  mix.grad_B_basis_partial = grad_B_basis_partial;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define TTC_BWD(DD, DDU, TT)                                                                    \
+  return ttc::launch_bwd<DD, DDU, TT>(A_diag, nullptr, nullptr, R_inv, coeff_Qf, log_gamma_A, log_gamma_B, \
+                                      log_gamma_Q, h0, lam0, M, d_u, N, nh, T, g, status, mix, 0, st)
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_BWD, float);
+  TTC_FOR_DIMS(TTC_BWD, __nv_bfloat16);
+#undef TTC_BWD
+}
+
 }  // extern "C"

@@ -10,7 +10,7 @@ import os
 import threading
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libttc_b200.so")
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -47,6 +47,13 @@ SIGNATURES = {
                         + [_P] * 5 + [_FP, _I64] + [_P] * 4 + [_P, _P]),
     "ttc_lqr_bwd_mix_noalloc": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I]
                                 + [_P] * 5 + [_FP] + [_P] * 4 + [_P, _P]),
+    "ttc_lqr_fwd_lowrank": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _P, _P, _P]
+                            + [_I64, _I, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
+    "ttc_lqr_bwd_lowrank": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _P, _P, _P, _FP, _FP, _P]
+                            + [_I64, _I, _I, _I, _I, _I] + [_P, _P, _FP, _P, _P, _P, _FP, _I64]
+                            + [_P] * 4 + [_P, _P]),
+    "ttc_rownorm_fwd": (_I, [_P, _I64, _I, _I, _P, _P]),
+    "ttc_rownorm_bwd": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
     "ttc_prologue_fwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P]),
     "ttc_prologue_bwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P, _P]),
 }

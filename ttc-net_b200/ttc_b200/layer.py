@@ -3,11 +3,12 @@
 and initialisation, so a reference ``state_dict`` loads 1:1.
 
 The prologue's elementwise part (split, l2norm / softplus / clamp, ttc_layer.py:106-133)
-runs as one CUDA kernel each way (``prologue.py``); the per-head Q_f mixture (:119-123) is
-done inside the solver kernels when the saved-state backward applies (``mix_available``),
-so no [N, nh, d, d] Q_f or grad_Q_f tensor exists; in_proj, the low-rank B / Q mixtures and
-the epilogue (l2norm, out_proj, :142-150) are PyTorch / cuBLAS ops on the GPU; the LQR solve
-runs in libttc_b200.so through ``LQR_SOLVER_IMPL_MAP``.
+runs as one CUDA kernel each way (``prologue.py``); the low-rank mixtures of B, Q and the
+per-head Q_f (:115-123) are formed inside the solver kernels when the saved-state backward
+applies (``mix_available``), so no [N, d, du] B, [N, d, d] Q or [N, nh, d, d] Q_f tensor (nor
+their gradients) exists; the epilogue's l2norm of u (:142-143) is one CUDA kernel each way
+(``epilogue.py``); in_proj and out_proj are cuBLAS GEMMs; the LQR solve runs in
+libttc_b200.so through ``LQR_SOLVER_IMPL_MAP``.
 """
 from __future__ import annotations
 
@@ -18,9 +19,10 @@ import torch.nn as nn
 import torch.nn.functional as F
 from torch.utils.checkpoint import checkpoint
 
+from .epilogue import rownorm
 from .prologue import prologue
 from .reductions import linear, lowrank_mix
-from .solver import (LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_mix_with_status,
+from .solver import (LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_lowrank_with_status,
                      lqr_solve_with_status, mix_available)
 from . import _lib
 
@@ -86,22 +88,20 @@ class TTCLayer(nn.Module):
                 else:
                     module.bias_gamma.data.fill_(0.0)
 
-    def mixed_inputs(self, x2d: torch.Tensor):
-        """Prologue (ttc_layer.py:104-135) up to, not including, the Q_f mixture: rows
-        [N, in_dim] -> (A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0) with
-        Q_f = sum_r coeff_Qf[..., r] Q_basis[r].  The elementwise part (split, l2norm,
-        softplus, clamp, negation) is one CUDA kernel each way (``prologue``); in_proj and
-        the low-rank B / Q mixtures are cuBLAS GEMMs with K-chunked weight gradients
-        (``reductions``)."""
+    def lowrank_inputs(self, x2d: torch.Tensor):
+        """Prologue (ttc_layer.py:104-135) up to, not including, the low-rank mixtures: rows
+        [N, in_dim] -> (A_diag, coeff_B, B_basis, coeff_Q, Q_basis, R_inv, coeff_Qf, lgA, lgB,
+        lgQ, h0) with B = sum_r coeff_B[..., r] B_basis[r], Q = sum_r coeff_Q[..., r]
+        Q_basis[r] and Q_f = sum_r coeff_Qf[..., r] Q_basis[r].  in_proj is a cuBLAS GEMM with
+        a K-chunked weight gradient (``reductions``); the elementwise split / l2norm / softplus
+        / clamp / negation is one CUDA kernel each way (``prologue``).  Q_basis is the layer's
+        Qs, or Qs Qs^T / sqrt(h_dim) for its cholesky reparametrisation (:121-123)."""
         nh, d, du = self.num_heads, self.h_dim, self.u_dim
         A_diag, R_inv_diag, coeff_Qf, log_gamma_A, log_gamma_B, log_gamma_Q, h0, coeff_B, coeff_Q = \
             prologue(linear(x2d, self.in_proj.weight, self.in_proj.bias), nh, d, du, self.b_rank, self.q_rank)
-        B = lowrank_mix(coeff_B, self.Bs)
         if self.q_reparam == "plain":
-            Q = lowrank_mix(coeff_Q, self.Qs)
             Q_basis = self.Qs
         else:
-            Q = torch.einsum("...r,rmn,rkn->...mk", coeff_Q, self.Qs, self.Qs) / math.sqrt(d)
             Q_basis = torch.einsum("rmn,rkn->rmk", self.Qs, self.Qs) / math.sqrt(d)
         if self.bias_gamma is not None:
             # log_gammas = -softplus(.) - relu(-bias_gamma), split as [1, du, d] (:129-133)
@@ -109,7 +109,21 @@ class TTCLayer(nn.Module):
             log_gamma_A = log_gamma_A - bg[0]
             log_gamma_B = log_gamma_B - bg[1:1 + du]
             log_gamma_Q = log_gamma_Q - bg[1 + du:]
-        return (A_diag, B, Q, R_inv_diag, coeff_Qf, Q_basis, log_gamma_A, log_gamma_B, log_gamma_Q, h0)
+        return (A_diag, coeff_B, self.Bs, coeff_Q, Q_basis, R_inv_diag, coeff_Qf, log_gamma_A, log_gamma_B,
+                log_gamma_Q, h0)
+
+    @staticmethod
+    def _mix(parts):
+        """Low-rank parts -> (A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0): B and Q
+        mixed by cuBLAS GEMMs (the einsums of ttc_layer.py:115-123)."""
+        A_diag, coeff_B, B_basis, coeff_Q, Q_basis, R_inv, coeff_Qf, lgA, lgB, lgQ, h0 = parts
+        return (A_diag, lowrank_mix(coeff_B, B_basis), lowrank_mix(coeff_Q, Q_basis), R_inv, coeff_Qf,
+                Q_basis, lgA, lgB, lgQ, h0)
+
+    def mixed_inputs(self, x2d: torch.Tensor):
+        """(A_diag, B, Q, R_inv, coeff_Qf, Q_basis, lgA, lgB, lgQ, h0): the prologue with B and Q
+        formed, Q_f still as its mixture."""
+        return self._mix(self.lowrank_inputs(x2d))
 
     @staticmethod
     def _materialise(parts):
@@ -171,13 +185,16 @@ class TTCLayer(nn.Module):
                 outs.append(self._forward_rows(xs, T))
         return torch.cat(outs).view(bs, seq_len, -1)
 
-    def forward_backward(self, x: torch.Tensor, dy: torch.Tensor, T: int, rows: int | None = None) -> torch.Tensor:
+    def forward_backward(self, x: torch.Tensor, dy: torch.Tensor, T: int, rows: int | None = None,
+                         before_last_backward=None) -> torch.Tensor:
         """Forward and backward of the layer over row micro-batches (gradient accumulation):
         each micro-batch of ``rows`` rows (default ``rows_per_call``) runs forward and is
         immediately differentiated with its slice of the upstream gradient ``dy``, so its
         saved state is freed before the next one starts.  Parameter gradients accumulate into
         ``.grad`` and, when ``x`` requires grad, into ``x.grad``, exactly as one
-        ``layer(x, T).backward(dy)`` would; returns y (detached), shaped like ``layer(x, T)``."""
+        ``layer(x, T).backward(dy)`` would; returns y (detached), shaped like ``layer(x, T)``.
+        ``before_last_backward`` (optional) is called just before the backward that completes
+        the parameter gradients (e.g. ``OverlappedGradAllReduce.arm``)."""
         if T == 0:  # y = 0 whatever the parameters (ttc_layer.py:101-102): no gradient
             return torch.zeros(*x.shape[:-1], self.out_dim, device=x.device, dtype=x.dtype)
         in_dim = x.shape[-1]
@@ -189,28 +206,31 @@ class TTCLayer(nn.Module):
         y = torch.empty(N, self.out_dim, device=x.device, dtype=x.dtype)
         for s in range(0, N, rows):
             ys = self._forward_rows(x2d[s:s + rows], T)
+            if before_last_backward is not None and s + rows >= N:
+                before_last_backward()
             ys.backward(dy2d[s:s + rows])
             y[s:s + rows] = ys.detach()
         return y.view(*x.shape[:-1], self.out_dim)
 
     def _forward_rows(self, x2d: torch.Tensor, T: int) -> torch.Tensor:
         """The layer on rows x2d [N, in_dim] -> y [N, out_dim] (ttc_layer.py:104-153)."""
-        parts = self.mixed_inputs(x2d)
+        parts = self.lowrank_inputs(x2d)
         if self.solver is cuda_lqr_solve:
             N, nh, d = parts[0].shape
-            if mix_available(N, nh, d, self.u_dim, parts[5].shape[0], parts[2].dtype):
-                # Q_f mixed inside the kernels: no [N, nh, d, d] tensor either way.
-                u, status = lqr_solve_mix_with_status(*parts, T)
+            if mix_available(N, nh, d, self.u_dim, parts[4].shape[0], parts[0].dtype):
+                # B, Q and Q_f mixed inside the kernels: no [N, d, du], [N, d, d] or
+                # [N, nh, d, d] tensor either way.
+                u, status = lqr_solve_lowrank_with_status(*parts, T)
             else:
-                u, status = lqr_solve_with_status(*self._materialise(parts), T)
+                u, status = lqr_solve_with_status(*self._materialise(self._mix(parts)), T)
             if status & _lib.STATUS_U_NAN:
                 raise RuntimeError(U_NAN_MSG)
         else:
-            u = self.solver(*self._materialise(parts), T)
+            u = self.solver(*self._materialise(self._mix(parts)), T)
             if torch.isnan(u).any():
                 raise RuntimeError(U_NAN_MSG)
         if self.rescale == "l2_norm":
-            u = l2norm(u)
+            u = rownorm(u)
         elif self.rescale == "h0_norm":
             x0 = parts[-1]
             h0_norm = torch.linalg.norm(x0, dim=-1, ord=2).detach()

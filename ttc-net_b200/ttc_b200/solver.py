@@ -271,6 +271,95 @@ def lqr_solve_mix_with_status(A_diag, B, Q, R_inv_diag, coeff_Qf, Q_basis, log_g
     return u, int(status.item())
 
 
+class LQRSolveLowRankFunction(torch.autograd.Function):
+    """The layer's whole low-rank solve (ttc_layer.py:115-137 fused): B = sum_r coeff_B[r]
+    B_basis[r], Q = sum_r coeff_Q[r] Q_basis[r] and Q_f = sum_r coeff_Qf[..., r] Q_basis[r]
+    are formed inside the kernels (ttc_lqr_fwd_lowrank / ttc_lqr_bwd_lowrank), so none of the
+    [N, d, du], [N, d, d] or [N, nh, d, d] tensors exists; the backward returns the gradients of
+    the coefficients and the bases.  Saves M when an input needs a gradient (callers check
+    ``mix_available`` first)."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
+    def forward(ctx, A_diag, coeff_B, B_basis, coeff_Q, Q_basis, R_inv, coeff_Qf, lgA, lgB, lgQ, h0, T):
+        T = int(T)
+        N, nh, d = A_diag.shape
+        rB, _, du = B_basis.shape
+        rQ = Q_basis.shape[0]
+        assert coeff_B.shape == (N, rB), f"coeff_B must be [{N},{rB}]"
+        assert coeff_Q.shape == (N, rQ), f"coeff_Q must be [{N},{rQ}]"
+        assert coeff_Qf.shape == (N, nh, rQ), f"coeff_Qf must be [{N},{nh},{rQ}]"
+        assert Q_basis.shape == (rQ, d, d), f"Q_basis must be [{rQ},{d},{d}]"
+        assert B_basis.shape == (rB, d, du), f"B_basis must be [{rB},{d},{du}]"
+        dtype = A_diag.dtype
+        if dtype not in _DTYPES:
+            raise TypeError(f"ttc_b200 'cuda' solver supports float32 and bfloat16, got {dtype}")
+        inputs = (A_diag, coeff_B, B_basis, coeff_Q, Q_basis, R_inv, coeff_Qf, lgA, lgB, lgQ, h0)
+        args = _prepare(inputs, dtype)
+        A_c, cB_c, Bb_c, cQ_c, Qb_c, R_c, cQf_c, lA_c, lB_c, lQ_c, h0_c = args
+        dev = A_diag.device
+        lib = _lib.load()
+        keep = any(ctx.needs_input_grad[:11])
+        u = torch.empty(N, nh, du, device=dev, dtype=dtype)
+        lam0 = torch.empty(N, nh, d, device=dev, dtype=torch.float32) if keep else None
+        M = torch.empty(N, nh, d, du, device=dev, dtype=torch.float32) if keep else None
+        status = torch.zeros(1, device=dev, dtype=torch.int32)
+        with torch.cuda.device(dev), torch.profiler.record_function("fwd:ttc_lqr_fwd_lowrank"):
+            _launch("ttc_lqr_fwd", dev, lib.ttc_lqr_fwd_lowrank, _ptr(A_c), _ptr(cB_c), _ptr(Bb_c), rB,
+                    _ptr(cQ_c), _ptr(R_c), _ptr(cQf_c), _ptr(Qb_c), rQ, _ptr(lA_c), _ptr(lB_c), _ptr(lQ_c),
+                    _ptr(h0_c), N, nh, d, du, T, _DTYPES[dtype], 0, _ptr(u), _ptr(lam0), _ptr(M), _ptr(status))
+        st = int(status.item())
+        check_fwd_status(st)
+        if keep:
+            ctx.save_for_backward(*args, lam0, M)
+        ctx.dims = (N, nh, d, du, rB, rQ, T)
+        ctx.dtype = dtype
+        ctx.in_dtypes = [t.dtype for t in inputs]
+        status_cpu = torch.tensor([st], dtype=torch.int32)
+        ctx.mark_non_differentiable(status_cpu)
+        return u, status_cpu
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, d_u, _d_status):
+        A, cB, Bb, cQ, Qb, R, cQf, lA, lB, lQ, h0, lam0, M = ctx.saved_tensors
+        N, nh, d, du, rB, rQ, T = ctx.dims
+        dtype = ctx.dtype
+        dev = A.device
+        lib = _lib.load()
+        d_u = d_u.to(dtype).contiguous()
+        with torch.cuda.device(dev):
+            slices = int(lib.ttc_lqr_bwd_mix_slices(N, nh, d, du, rQ, _DTYPES[dtype]))
+        if slices <= 0:
+            _lib.check(-slices if slices < 0 else _lib.ERR_UNSUPPORTED)
+        gA, gcB, gcQ, gR, gcQf, glA, glB, glQ, gh0 = [torch.empty_like(t) for t in (A, cB, cQ, R, cQf, lA, lB, lQ, h0)]
+        part_q = torch.empty(slices, rQ, d, d, device=dev, dtype=torch.float32)
+        part_b = torch.empty(slices, rB, d, du, device=dev, dtype=torch.float32)
+        status = torch.zeros(1, device=dev, dtype=torch.int32)
+        with torch.cuda.device(dev), torch.profiler.record_function("bwd:ttc_lqr_bwd_lowrank"):
+            _launch("ttc_lqr_bwd", dev, lib.ttc_lqr_bwd_lowrank, _ptr(A), _ptr(cB), _ptr(Bb), rB, _ptr(cQ),
+                    _ptr(R), _ptr(cQf), _ptr(Qb), rQ, _ptr(lA), _ptr(lB), _ptr(lQ), _ptr(h0), _ptr(lam0),
+                    _ptr(M), _ptr(d_u), N, nh, d, du, T, _DTYPES[dtype], _ptr(gA), _ptr(gcB), _ptr(part_b),
+                    _ptr(gcQ), _ptr(gR), _ptr(gcQf), _ptr(part_q), slices, _ptr(glA), _ptr(glB), _ptr(glQ),
+                    _ptr(gh0), _ptr(status))
+        check_bwd_status(int(status.item()))
+        S = part_q.sum(0)
+        gQb = 0.5 * (S + S.transpose(-1, -2))
+        gBb = part_b.sum(0)
+        grads = [gA, gcB, gBb, gcQ, gQb, gR, gcQf, glA, glB, glQ, gh0]
+        grads = [g.to(dt) for g, dt in zip(grads, ctx.in_dtypes)]
+        return (*grads, None)
+
+
+def lqr_solve_lowrank_with_status(A_diag, coeff_B, B_basis, coeff_Q, Q_basis, R_inv_diag, coeff_Qf,
+                                  log_gamma_A, log_gamma_B, log_gamma_Q, h0, T):
+    """The solve with B, Q and Q_f given as the layer's mixtures (see LQRSolveLowRankFunction);
+    returns (u, status)."""
+    u, status = LQRSolveLowRankFunction.apply(A_diag, coeff_B, B_basis, coeff_Q, Q_basis, R_inv_diag,
+                                              coeff_Qf, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T)
+    return u, int(status.item())
+
+
 def _flags(inv_guard: bool) -> int:
     return _lib.FLAG_INV_GUARD if inv_guard else 0
 
