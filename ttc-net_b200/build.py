@@ -17,6 +17,7 @@ import os
 import shutil
 import subprocess
 import sys
+import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
@@ -50,39 +51,47 @@ def up_to_date() -> bool:
     return os.path.getmtime(LIB) >= max(os.path.getmtime(p) for p in deps)
 
 
-def _compile(nvcc: str, src: str) -> tuple[str, str]:
-    obj = os.path.join(OBJDIR, os.path.splitext(os.path.basename(src))[0] + ".o")
-    r = subprocess.run([nvcc, *CFLAGS, "-c", src, "-o", obj], capture_output=True, text=True)
+def _compile(nvcc: str, src: str, objdir: str = OBJDIR, extra=()) -> tuple[str, str]:
+    obj = os.path.join(objdir, os.path.splitext(os.path.basename(src))[0] + ".o")
+    r = subprocess.run([nvcc, *CFLAGS, *extra, "-c", src, "-o", obj], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{r.stderr}")
     return obj, r.stderr
 
 
-def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> str:
-    """Compile and link the library; returns its path."""
-    if not force and up_to_date():
+def build(force: bool = False, jobs: int | None = None, verbose: bool = False, out: str | None = None,
+          defines=()) -> str:
+    """Compile and link the library; returns its path.  `out` and `defines` (NAME=VALUE
+    macros, e.g. the kernels' tuning switches) build a variant elsewhere, always from scratch;
+    the package loads such a build when TTC_B200_LIB names it."""
+    lib = out or LIB
+    if out is None and not defines and not force and up_to_date():
         return LIB
     nvcc = _nvcc()
     srcs, _ = _inputs()
-    os.makedirs(OBJDIR, exist_ok=True)
+    objdir = OBJDIR if out is None else tempfile.mkdtemp(prefix="ttc_b200_obj_")
+    os.makedirs(objdir, exist_ok=True)
+    extra = [f"-D{d}" for d in defines]
     jobs = jobs or min(len(srcs), os.cpu_count() or 1)
     objs, logs = [], []
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
-        for obj, log in ex.map(lambda s: _compile(nvcc, s), srcs):
+        for obj, log in ex.map(lambda s: _compile(nvcc, s, objdir, extra), srcs):
             objs.append(obj)
             logs.append(log)
-    tmp = LIB + ".tmp"
+    tmp = lib + ".tmp"
     r = subprocess.run([nvcc, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", tmp, *objs],
                        capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")
-    os.replace(tmp, LIB)
+    os.replace(tmp, lib)
+    if out is not None:
+        shutil.rmtree(objdir, ignore_errors=True)
     if verbose:
         for log in logs:
             for line in log.splitlines():
                 if "registers" in line or "spill" in line or "Compiling entry" in line:
                     print(line)
-    return LIB
+    return lib
 
 
 def main(argv=None) -> int:
@@ -90,8 +99,10 @@ def main(argv=None) -> int:
     ap.add_argument("--force", action="store_true", help="rebuild even if up to date")
     ap.add_argument("-j", "--jobs", type=int, default=None)
     ap.add_argument("-v", "--verbose", action="store_true", help="print ptxas register/spill lines")
+    ap.add_argument("--out", default=None, help="build a variant library at this path")
+    ap.add_argument("-D", "--define", action="append", default=[], help="NAME=VALUE macro for the variant")
     a = ap.parse_args(argv)
-    print(build(force=a.force, jobs=a.jobs, verbose=a.verbose))
+    print(build(force=a.force, jobs=a.jobs, verbose=a.verbose, out=a.out, defines=a.define))
     return 0
 
 

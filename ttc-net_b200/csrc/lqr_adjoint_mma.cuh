@@ -21,6 +21,12 @@
 
 #include "lqr_kernels.cuh"
 
+// 1: the grad_B / grad_Q accumulation of step k - 1 runs after step k's products are issued
+// (overlapping the dependent chain); 0: right after step k's barrier.
+#ifndef TTC_BWD_DEFER
+#define TTC_BWD_DEFER 0
+#endif
+
 namespace ttc {
 
 namespace wmma {
@@ -447,6 +453,37 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[q][nj][r] = 0.f;
 
+    // grad_B += lambda (du e^lgB)^T + dlambda (u e^lgB)^T ;
+    // grad_Q += (h Dq)(dh Dq)^T + (dh Dq)(h Dq)^T  (the 1/2 is applied at the end; at
+    // d = 16 only the first term is accumulated and the transpose added at the end)
+    // for step ks, from the vectors every warp of the row staged for it.
+    auto accumulate_step = [&](int ks) {
+#pragma unroll
+      for (int q = 0; q < UPW; ++q) {
+        const int unit = C::kOwn ? q : hb + q * wpr;
+        if (unit < C::kUnits) {
+          const bool isq = unit >= MT;
+          if (!isq || ks < T - 1) {
+            const int mi = isq ? unit - MT : unit;
+            const int off = (ks & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : 0);
+            const int offy = (ks & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : C::kStage);
+            if constexpr (C::kOwn) {
+              // grad_Q as S = sum (h Dq)(dh Dq)^T, symmetrised at the end
+              if (isq) {
+                accumulate_unit<D, 1>(acc[q], stg + off, stg + offy, mi, g, t);
+              } else {
+                accumulate_unit<D>(acc[q], stg + off, stg + offy, mi, g, t);
+              }
+            } else {
+              for (int w = 0; w < wpr; ++w) {
+                const float* base = row_stage + (size_t)w * C::kWarp;
+                accumulate_unit<D>(acc[q], base + off, base + offy, mi, g, t);
+              }
+            }
+          }
+        }
+      }
+    };
     for (int k = 0; k < T; ++k) {
       const float ke = static_cast<float>(k + 1);
       float* S0 = stg + (k & 1) * 3 * C::kStage;  // [lambda; dlambda]
@@ -525,6 +562,12 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       {
         float BU[NT][4];
         frag_product<D>(UE, BU, Wbt, lane);
+#if TTC_BWD_DEFER
+        // step k - 1's grad_B / grad_Q terms right after step k's last product is issued:
+        // independent MMAs that run while it completes (step k - 1's buffers stay valid until
+        // every warp of the row has passed this step's barrier)
+        if (k > 0) accumulate_step(k - 1);
+#endif
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -549,35 +592,13 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       } else {
         __syncwarp();
       }
-      // grad_B += lambda (du e^lgB)^T + dlambda (u e^lgB)^T ;
-      // grad_Q += (h Dq)(dh Dq)^T + (dh Dq)(h Dq)^T  (the 1/2 is applied at the end; at
-      // d = 16 only the first term is accumulated and the transpose added at the end)
-#pragma unroll
-      for (int q = 0; q < UPW; ++q) {
-        const int unit = C::kOwn ? q : hb + q * wpr;
-        if (unit < C::kUnits) {
-          const bool isq = unit >= MT;
-          if (!isq || k < T - 1) {
-            const int mi = isq ? unit - MT : unit;
-            const int off = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : 0);
-            const int offy = (k & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : C::kStage);
-            if constexpr (C::kOwn) {
-              // grad_Q as S = sum (h Dq)(dh Dq)^T, symmetrised at the end
-              if (isq) {
-                accumulate_unit<D, 1>(acc[q], stg + off, stg + offy, mi, g, t);
-              } else {
-                accumulate_unit<D>(acc[q], stg + off, stg + offy, mi, g, t);
-              }
-            } else {
-              for (int w = 0; w < wpr; ++w) {
-                const float* base = row_stage + (size_t)w * C::kWarp;
-                accumulate_unit<D>(acc[q], base + off, base + offy, mi, g, t);
-              }
-            }
-          }
-        }
-      }
+#if !TTC_BWD_DEFER
+      accumulate_step(k);
+#endif
     }
+#if TTC_BWD_DEFER
+    accumulate_step(T - 1);
+#endif
 
     // grad_Qf = (h dh^T + dh h^T) / 2 at the final state (symplectic_iter.py:855-857), from
     // the staging buffer of step T (unused by the row's other warps); for a mixed Q_f its

@@ -54,6 +54,9 @@ template <typename TIn>
 __device__ __forceinline__ float mix_elem(const TIn* __restrict__ c, const TIn* __restrict__ basis, int rank,
                                           int len, int e) {
   float s = 0.f;
+  // unrolled so that the loads of eight ranks are in flight together (the sum stays in rank
+  // order); the bases are L2-resident, so this is latency, not bandwidth
+#pragma unroll 8
   for (int r = 0; r < rank; ++r) s = fmaf(ldf(c + r), ldf(basis + (int64_t)r * len + e), s);
   return round_to<TIn>(s);
 }

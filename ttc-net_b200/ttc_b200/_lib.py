@@ -9,7 +9,10 @@ import ctypes
 import os
 import threading
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libttc_b200.so")
+# The in-tree build; TTC_B200_LIB may name another build of the same sources (a variant
+# compiled with tuning macros by `build.py --out PATH -D NAME=VALUE`).
+LIB_PATH = os.environ.get("TTC_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                          "libttc_b200.so")
 ABI_VERSION = 6
 
 DTYPE_F32 = 0
