@@ -469,7 +469,7 @@ def main(argv=None):
         fp32_peak = SM_COUNT_B200 * FP32_LANES_PER_SM * 2 * sm_max * 1e6 / 1e12
         fwd_tflops = fwd_f * probs_per_launch / (statistics.mean(fwd_ms) / 1e3) / 1e12
         bwd_tflops = bwd_f * probs_per_launch / (statistics.mean(bwd_ms) / 1e3) / 1e12
-        traffic = load_traffic(cfg.name)
+        traffic = load_traffic(cfg.name, cfg.rows / calls_per_step)
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -630,14 +630,19 @@ def traj_bench(args, cfg):
     }), flush=True)
 
 
-def load_traffic(workload):
-    """DRAM bytes per launch of the roofline kernel from the committed ncu summary."""
+def load_traffic(workload, rows_per_launch):
+    """DRAM bytes per launch of the roofline kernel: the committed ncu capture's bytes per row
+    (profiles/traffic.json; the forward's traffic grows with the rows it solves) times the rows
+    of one launch."""
     p = os.path.join(REPO, "profiles", "traffic.json")
     try:
         with open(p) as f:
-            return json.load(f).get(workload)
+            entry = json.load(f).get(workload)
     except (OSError, ValueError):
         return None
+    if not entry:
+        return None
+    return entry["dram_bytes_per_row"] * rows_per_launch
 
 
 if __name__ == "__main__":

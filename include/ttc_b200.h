@@ -48,6 +48,7 @@ extern "C" {
 #define TTC_STATUS_U_NAN 8        /* NaN in u                     (ttc/layers/ttc_layer.py:139-140)  */
 #define TTC_STATUS_MMA_TIMEOUT 16 /* a tensor-core MMA did not complete within the kernel's poll limit */
 #define TTC_STATUS_TRAJ_NONFINITE 32 /* NaN or Inf in a trajectory written by ttc_lqr_rollout */
+#define TTC_STATUS_COPY_TIMEOUT 64 /* a bulk copy into shared memory did not complete within the kernel's wait limit */
 
 /* Option bits (`flags` argument). */
 #define TTC_FLAG_INV_GUARD 1 /* Y1 + 1e-6 I after the sweep, before the solve: the reference's
@@ -201,7 +202,8 @@ int ttc_lqr_bwd_mix_noalloc(const void* A_diag, const void* B, const void* Q, co
  * coeff_B [N,rB], B_basis [rB,d,du], coeff_Q [N,rQ] in the activation dtype; Q_basis [rQ,d,d]
  * is the basis of the Q_f mixture as well (the layer's Qs, or Qs Qs^T / sqrt(d) for its
  * cholesky reparametrisation).  Each sum runs in fp32 in rank order and is rounded to the
- * activation dtype, as the einsum it replaces.  Everything else as ttc_lqr_fwd_mix.
+ * activation dtype, as the einsum it replaces.  B_basis and Q_basis must be 16-byte aligned
+ * (TTC_ERR_INVALID otherwise).  Everything else as ttc_lqr_fwd_mix.
  */
 int ttc_lqr_fwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_basis, int rB,
                         const void* coeff_Q, const void* R_inv, const void* coeff_Qf, const void* Q_basis,
@@ -217,7 +219,8 @@ int ttc_lqr_fwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_b
  * grad_B_basis_partial [slices,rB,d,du] (the B-basis gradient is their sum) and
  * grad_basis_partial [slices,rQ,d,d] (the Q-basis gradient is (S + S^T) / 2 with S their sum:
  * the Q_f terms of ttc_lqr_bwd_mix plus sum_n coeff_Q[n,r] grad_Q[n]).  slices from
- * ttc_lqr_bwd_mix_slices; every slice is written.  Other outputs as ttc_lqr_bwd.
+ * ttc_lqr_bwd_mix_slices; every slice is written.  The bases and both partial buffers must be
+ * 16-byte aligned.  Other outputs as ttc_lqr_bwd.
  */
 int ttc_lqr_bwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_basis, int rB,
                         const void* coeff_Q, const void* R_inv, const void* coeff_Qf, const void* Q_basis,
@@ -244,10 +247,13 @@ int ttc_rownorm_bwd(const void* x, const void* g, int64_t rows, int n, int dtype
  *   coeff_Qf = l2norm(softplus(.)) [N,nh,d], lgA = -softplus(.) [N,nh], lgB [N,nh,du],
  *   lgQ [N,nh,d], h0 [N,nh,d], coeff_B = l2norm(.) [N,rB], coeff_Q = l2norm(softplus(.)) [N,rQ]
  * with l2norm(x) = x * rsqrt(sum(x^2) + 1e-6) in fp32 and torch's softplus (threshold 20).
- * d, du, rB, rQ <= 64. */
+ * d, du, rB, rQ <= 64.  With a status word (device int, may be NULL) and 16-byte aligned rows
+ * (Z and W * sizeof(dtype) multiples of 16 bytes) the rows are staged in shared memory by
+ * bulk copies (cp.async.bulk, two rows in flight per CTA); a copy that does not complete
+ * within about a second sets TTC_STATUS_COPY_TIMEOUT.  Otherwise the warps read Z directly. */
 int ttc_prologue_fwd(const void* Z, int64_t N, int nh, int d, int du, int rB, int rQ, int dtype,
                      void* A_diag, void* R_inv, void* coeff_Qf, void* lgA, void* lgB, void* lgQ,
-                     void* h0, void* coeff_B, void* coeff_Q, void* stream);
+                     void* h0, void* coeff_B, void* coeff_Q, int* status, void* stream);
 
 /* Backward of ttc_prologue_fwd: dZ [N, W] from the gradients of its nine outputs (same
  * shapes and dtype; any of them may be NULL, read as zero).  Z is the forward's input. */

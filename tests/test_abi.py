@@ -97,7 +97,7 @@ def test_prologue_rejects_bad_arguments_without_gpu(lib):
     P = 16  # never dereferenced: rejected before any launch
 
     def fwd(N=1, nh=1, d=16, du=16, rB=16, rQ=16, dtype=0, outs=P):
-        return lib.ttc_prologue_fwd(P, N, nh, d, du, rB, rQ, dtype, *([outs] * 9), None)
+        return lib.ttc_prologue_fwd(P, N, nh, d, du, rB, rQ, dtype, *([outs] * 9), None, None)
 
     def bwd(N=1, nh=1, d=16, du=16, rB=16, rQ=16, dtype=0, dZ=P):
         return lib.ttc_prologue_bwd(P, N, nh, d, du, rB, rQ, dtype, *([None] * 9), dZ, None)

@@ -8,8 +8,10 @@ from prologue_ref import prologue_torch
 pytestmark = pytest.mark.gpu
 
 
+# rows of 16-byte multiples (bulk-copy path: the config-1, -2, -3 and -4 widths) and others
 SHAPES = [(512, 16, 16, 16, 16, 16), (77, 3, 16, 16, 16, 16), (300, 5, 32, 32, 32, 32),
-          (64, 3, 64, 64, 64, 64), (100, 2, 16, 32, 8, 24), (40, 3, 32, 16, 64, 32)]
+          (64, 3, 64, 64, 64, 64), (100, 2, 16, 32, 8, 24), (40, 3, 32, 16, 64, 32),
+          (200, 8, 16, 16, 16, 16), (1000, 32, 32, 32, 32, 32), (37, 32, 64, 64, 64, 64)]
 
 
 def _z(N, nh, d, du, rB, rQ, dtype, seed):
@@ -64,3 +66,33 @@ def test_prologue_deterministic_and_empty():
         assert torch.equal(a, b)
     empty = prologue(torch.empty(0, Z.shape[1], device="cuda"), nh, d, du, rB, rQ)
     assert empty[0].shape == (0, nh, d)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("shape", [(1000, 32, 32, 32, 32, 32), (3001, 16, 16, 16, 16, 16), (5, 8, 16, 16, 16, 16)])
+def test_prologue_bulk_copy_path_equals_direct_loads(shape, dtype):
+    """The forward with its rows staged in shared memory by bulk copies (status word given,
+    aligned rows) writes bitwise the outputs of the direct-load kernel (no status word)."""
+    from ttc_b200 import _lib
+    from ttc_b200.solver import _DTYPES
+    lib = _lib.load()
+    N, nh, d, du, rB, rQ = shape
+    Z = _z(*shape, dtype, seed=N)
+    assert (Z.shape[1] * Z.element_size()) % 16 == 0 and Z.data_ptr() % 16 == 0
+
+    def run(with_status):
+        kw = dict(device="cuda", dtype=dtype)
+        outs = [torch.full(s_, float("nan"), **kw) for s_ in
+                ((N, nh, d), (N, nh, du), (N, nh, d), (N, nh), (N, nh, du), (N, nh, d), (N, nh, d), (N, rB), (N, rQ))]
+        status = torch.zeros(1, device="cuda", dtype=torch.int32) if with_status else None
+        rc = lib.ttc_prologue_fwd(Z.data_ptr(), N, nh, d, du, rB, rQ, _DTYPES[dtype], *[o.data_ptr() for o in outs],
+                                  None if status is None else status.data_ptr(),
+                                  torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, lib.ttc_last_error()
+        torch.cuda.synchronize()
+        if status is not None:
+            assert int(status.item()) == 0
+        return outs
+
+    for a, b in zip(run(True), run(False)):
+        assert torch.equal(a, b)

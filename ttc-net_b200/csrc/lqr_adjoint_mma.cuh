@@ -21,12 +21,6 @@
 
 #include "lqr_kernels.cuh"
 
-// 1: the grad_B / grad_Q accumulation of step k - 1 runs after step k's products are issued
-// (overlapping the dependent chain); 0: right after step k's barrier.
-#ifndef TTC_BWD_DEFER
-#define TTC_BWD_DEFER 0
-#endif
-
 namespace ttc {
 
 namespace wmma {
@@ -370,9 +364,9 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         float* tQ = warp_s + D * D;
         const TIn* cBn = lr.cB + nr * lr.rB;
         const TIn* cQn = lr.cQ + nr * rQ;
-        for (int e = tid; e < D * D; e += nthreads) {
-          tB[e] = mix_elem<TIn>(cBn, lr.Bb, lr.rB, D * D, e);
-          tQ[e] = mix_elem<TIn>(cQn, Qbasis, rQ, D * D, e);
+        for (int e4 = tid; e4 < D * D / 4; e4 += nthreads) {
+          *reinterpret_cast<float4*>(tB + 4 * e4) = mix4<TIn>(cBn, lr.Bb, lr.rB, D * D, 4 * e4);
+          *reinterpret_cast<float4*>(tQ + 4 * e4) = mix4<TIn>(cQn, Qbasis, rQ, D * D, 4 * e4);
         }
         __syncthreads();
         build_operand<D>(base, [&](int k, int c) { return tQ[c * D + k]; }, tid, nthreads);
@@ -562,12 +556,6 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       {
         float BU[NT][4];
         frag_product<D>(UE, BU, Wbt, lane);
-#if TTC_BWD_DEFER
-        // step k - 1's grad_B / grad_Q terms right after step k's last product is issued:
-        // independent MMAs that run while it completes (step k - 1's buffers stay valid until
-        // every warp of the row has passed this step's barrier)
-        if (k > 0) accumulate_step(k - 1);
-#endif
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -592,13 +580,8 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       } else {
         __syncwarp();
       }
-#if !TTC_BWD_DEFER
       accumulate_step(k);
-#endif
     }
-#if TTC_BWD_DEFER
-    accumulate_step(T - 1);
-#endif
 
     // grad_Qf = (h dh^T + dh h^T) / 2 at the final state (symplectic_iter.py:855-857), from
     // the staging buffer of step T (unused by the row's other warps); for a mixed Q_f its
@@ -733,33 +716,54 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     if (lowrank) {
       // grad_coeff_B / grad_coeff_Q of the group's rows and their terms of the basis
       // gradients.  Each basis index is handled by one warp (a CTA barrier separates this
-      // from the Q_f contractions, which update the same Q slices), rows in order:
-      // deterministic.
+      // from the Q_f contractions, which update the same Q slices), which reads its basis
+      // matrix and read-modify-writes its slice once for all the group's rows, four
+      // consecutive entries per lane and access (the slices are L2-resident), rows added in
+      // order: deterministic.
       __syncthreads();
       const int nw = nthreads >> 5;
-      for (int r = 0; r < rows_per_cta; ++r) {
-        const int64_t nr = n0 + r;
-        if (nr >= N) break;
-        const float* gBr = rows_s + r * C::kRow;
-        const float* gQr = gBr + D * D;
-        for (int k = warp; k < lr.rB + rQ; k += nw) {
-          const bool isb = k < lr.rB;
-          const int rr = isb ? k : k - lr.rB;
-          const float* gr = isb ? gBr : gQr;
-          const TIn* bas = (isb ? lr.Bb : Qbasis) + (int64_t)rr * D * D;
-          float* sl = (isb ? bslice : slice) + (int64_t)rr * D * D;
-          const float c = ldf((isb ? lr.cB + nr * lr.rB : lr.cQ + nr * rQ) + rr);
-          float dot = 0.f;
-          for (int e = lane; e < D * D; e += 32) {
-            const float gv = gr[e];
-            dot = fmaf(gv, ldf(bas + e), dot);
-            sl[e] = fmaf(c, gv, sl[e]);
-          }
+      const int nrows = static_cast<int>(N - n0 < rows_per_cta ? N - n0 : rows_per_cta);
+      for (int k = warp; k < lr.rB + rQ; k += nw) {
+        const bool isb = k < lr.rB;
+        const int rr = isb ? k : k - lr.rB;
+        const int rank = isb ? lr.rB : rQ;
+        const TIn* cf = (isb ? lr.cB : lr.cQ) + n0 * rank + rr;
+        const TIn* bas = (isb ? lr.Bb : Qbasis) + (int64_t)rr * D * D;
+        float* sl = (isb ? bslice : slice) + (int64_t)rr * D * D;
+        const int goff = isb ? 0 : D * D;
+        float c[C::kMaxWarps], dot[C::kMaxWarps];
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-          if (lane == 0) {
-            bad |= unstable(dot);
-            stf((isb ? lr.gcB + nr * lr.rB : lr.gcQ + nr * rQ) + rr, dot);
+        for (int r = 0; r < C::kMaxWarps; ++r) {
+          c[r] = r < nrows ? ldf(cf + (int64_t)r * rank) : 0.f;
+          dot[r] = 0.f;
+        }
+#pragma unroll 4
+        for (int e4 = lane; e4 < D * D / 4; e4 += 32) {
+          const float4 b = ld4(bas + 4 * e4);
+          float4 a = *reinterpret_cast<const float4*>(sl + 4 * e4);
+#pragma unroll
+          for (int r = 0; r < C::kMaxWarps; ++r) {
+            if (r < nrows) {
+              const float4 gv = *reinterpret_cast<const float4*>(rows_s + r * C::kRow + goff + 4 * e4);
+              dot[r] = fmaf(gv.x, b.x, fmaf(gv.y, b.y, fmaf(gv.z, b.z, fmaf(gv.w, b.w, dot[r]))));
+              a.x = fmaf(c[r], gv.x, a.x);
+              a.y = fmaf(c[r], gv.y, a.y);
+              a.z = fmaf(c[r], gv.z, a.z);
+              a.w = fmaf(c[r], gv.w, a.w);
+            }
+          }
+          *reinterpret_cast<float4*>(sl + 4 * e4) = a;
+        }
+#pragma unroll
+        for (int r = 0; r < C::kMaxWarps; ++r) {
+          if (r < nrows) {
+            float v = dot[r];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) {
+              bad |= unstable(v);
+              stf((isb ? lr.gcB : lr.gcQ) + (n0 + r) * rank + rr, v);
+            }
           }
         }
       }

@@ -47,6 +47,14 @@ struct LowRank {
   float* gBb = nullptr;  // [gridDim.x][rB][d][du]
 };
 
+// Four consecutive values as floats (16-byte aligned for float, 8-byte for bf16).
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
+                     __uint_as_float(v.y & 0xffff0000u));
+}
+
 // Element e of the mixture sum_r c[r] basis[r][e] (each basis matrix `len` elements),
 // summed in rank order in fp32 and rounded to the activation dtype like the einsum it
 // replaces.
@@ -59,6 +67,23 @@ __device__ __forceinline__ float mix_elem(const TIn* __restrict__ c, const TIn* 
 #pragma unroll 8
   for (int r = 0; r < rank; ++r) s = fmaf(ldf(c + r), ldf(basis + (int64_t)r * len + e), s);
   return round_to<TIn>(s);
+}
+
+// Four consecutive elements e..e+3 of the mixture (e a multiple of 4), as mix_elem.
+template <typename TIn>
+__device__ __forceinline__ float4 mix4(const TIn* __restrict__ c, const TIn* __restrict__ basis, int rank, int len,
+                                       int e) {
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+  for (int r = 0; r < rank; ++r) {
+    const float cr = ldf(c + r);
+    const float4 b = ld4(basis + (int64_t)r * len + e);
+    s.x = fmaf(cr, b.x, s.x);
+    s.y = fmaf(cr, b.y, s.y);
+    s.z = fmaf(cr, b.z, s.z);
+    s.w = fmaf(cr, b.w, s.w);
+  }
+  return make_float4(round_to<TIn>(s.x), round_to<TIn>(s.y), round_to<TIn>(s.z), round_to<TIn>(s.w));
 }
 
 // True for NaN, +-Inf and |v| >= 1e6: the reference's isnan | isinf | abs >= 1e6.

@@ -208,48 +208,144 @@ __device__ __forceinline__ int tasks_per_row(int nh) {
   return (nh + HPW - 1) / HPW + 1;
 }
 
+// Outputs of the forward prologue.
+template <typename T>
+struct FwdOut {
+  T *A, *R, *cQf, *lgA, *lgB, *lgQ, *h0, *cB, *cQ;
+};
+
+// Task `task` of row n (head group, or the row's coefficients for the last task) from the
+// row's projection zr (global or shared memory), by one warp.
 template <int SEG, int PER, typename T>
-__global__ void __launch_bounds__(256) prologue_fwd_kernel(
-    const T* __restrict__ Z, int64_t N, Dims D, T* __restrict__ A_out, T* __restrict__ R_out,
-    T* __restrict__ cQf_out, T* __restrict__ lgA_out, T* __restrict__ lgB_out,
-    T* __restrict__ lgQ_out, T* __restrict__ h0_out, T* __restrict__ cB_out,
-    T* __restrict__ cQ_out) {
+__device__ __forceinline__ void prologue_fwd_task(const T* zr, int64_t n, int task, int tpr, const Dims& D,
+                                                  const FwdOut<T>& o) {
   constexpr int HPW = 32 / SEG;
   const int lane = threadIdx.x & 31, seg = lane / SEG, ls = lane % SEG;
+  if (task == tpr - 1) {  // per-row mixture coefficients: the whole warp
+    Vec<2> y;
+    l2norm_fwd<32, 2, T>(load_vec<32, 2>(zr + D.nh * D.Hs, D.rB, lane), y);
+    store_vec<32, 2>(o.cB + n * D.rB, y, lane);
+    l2norm_fwd<32, 2, T>(softplus_vec<2, T>(load_vec<32, 2>(zr + D.nh * D.Hs + D.rB, D.rQ, lane)), y);
+    store_vec<32, 2>(o.cQ + n * D.rQ, y, lane);
+    return;
+  }
+  const int h = task * HPW + seg;
+  const bool valid = h < D.nh;
+  // A segment without a head runs the same shuffles on empty vectors and stores nothing.
+  const int nd = valid ? D.d : 0, ndu = valid ? D.du : 0;
+  const T* z = zr + (int64_t)(valid ? h : 0) * D.Hs;
+  const int64_t p = valid ? n * D.nh + h : 0;
+  Vec<PER> y;
+  store_vec<SEG, PER>(o.h0 + p * D.d, load_vec<SEG, PER>(z, nd, ls), ls);
+  l2norm_fwd<SEG, PER, T>(load_vec<SEG, PER>(z + D.oA, nd, ls), y);
+  store_vec<SEG, PER>(o.A + p * D.d, y, ls);
+  l2norm_fwd<SEG, PER, T>(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oR, ndu, ls)), y);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) y.v[k] = round_t<T>(fmaxf(y.v[k], kRinvMin));
+  store_vec<SEG, PER>(o.R + p * D.du, y, ls);
+  l2norm_fwd<SEG, PER, T>(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oQf, nd, ls)), y);
+  store_vec<SEG, PER>(o.cQf + p * D.d, y, ls);
+  if (valid && ls == 0) stf(o.lgA + p, -round_t<T>(softplus(ldf(z + D.oGA))));
+  store_vec<SEG, PER>(o.lgB + p * D.du, negated(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oGB, ndu, ls))), ls);
+  store_vec<SEG, PER>(o.lgQ + p * D.d, negated(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oGQ, nd, ls))), ls);
+}
+
+template <int SEG, int PER, typename T>
+__global__ void __launch_bounds__(256) prologue_fwd_kernel(const T* __restrict__ Z, int64_t N, Dims D,
+                                                           FwdOut<T> o) {
   const int tpr = tasks_per_row<SEG>(D.nh);
   const int64_t tasks = N * tpr;
   const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < tasks; w += stride) {
     const int64_t n = w / tpr;
-    const int task = static_cast<int>(w % tpr);
-    const T* zr = Z + n * D.W;
-    if (task == tpr - 1) {  // per-row mixture coefficients: the whole warp
-      Vec<2> y;
-      l2norm_fwd<32, 2, T>(load_vec<32, 2>(zr + D.nh * D.Hs, D.rB, lane), y);
-      store_vec<32, 2>(cB_out + n * D.rB, y, lane);
-      l2norm_fwd<32, 2, T>(softplus_vec<2, T>(load_vec<32, 2>(zr + D.nh * D.Hs + D.rB, D.rQ, lane)), y);
-      store_vec<32, 2>(cQ_out + n * D.rQ, y, lane);
-      continue;
+    prologue_fwd_task<SEG, PER, T>(Z + n * D.W, n, static_cast<int>(w % tpr), tpr, D, o);
+  }
+}
+
+// The same prologue with the projection rows staged in shared memory by the tensor memory
+// accelerator: a persistent CTA walks rows blockIdx.x, + gridDim.x, ...; one thread issues a
+// bulk copy (cp.async.bulk, W * sizeof(T) bytes, completion counted on an mbarrier) of the
+// row after next while the CTA's warps work on the current row from shared memory, two
+// stages deep.  Needs Z and the row pitch 16-byte aligned (the launcher checks).  Every wait
+// is bounded: a copy that does not complete in about a second sets TTC_STATUS_COPY_TIMEOUT
+// and the CTA stops.
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(mbar)), "r"(bytes)
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(mbar))
+      : "memory");
+}
+
+// Waits for phase `parity` of `mbar`, at most ~1 s of %globaltimer; false on timeout.
+__device__ __forceinline__ bool wait_phase(uint64_t* mbar, uint32_t parity) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(mbar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > 1000000000ull) return false;
+  }
+}
+
+template <int SEG, int PER, typename T>
+__global__ void __launch_bounds__(256) prologue_fwd_tma_kernel(const T* __restrict__ Z, int64_t N, Dims D,
+                                                               FwdOut<T> o, int* __restrict__ status) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem_raw);          // 2 mbarriers
+  T* stage0 = reinterpret_cast<T*>(smem_raw + 128);                 // 2 rows of W values
+  const uint32_t row_bytes = static_cast<uint32_t>(D.W * sizeof(T));
+  const size_t pitch = (static_cast<size_t>(row_bytes) + 127) / 128 * 128;
+  const int tpr = tasks_per_row<SEG>(D.nh);
+  const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  __shared__ int stop;
+  if (threadIdx.x == 0) {
+    stop = 0;
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&mbar[0])));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&mbar[1])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int s = 0; s < 2; ++s) {
+      const int64_t n = blockIdx.x + (int64_t)s * gridDim.x;
+      if (n < N) bulk_load(reinterpret_cast<unsigned char*>(stage0) + s * pitch, Z + n * D.W, row_bytes, &mbar[s]);
     }
-    const int h = task * HPW + seg;
-    const bool valid = h < D.nh;
-    // A segment without a head runs the same shuffles on empty vectors and stores nothing.
-    const int nd = valid ? D.d : 0, ndu = valid ? D.du : 0;
-    const T* z = zr + (int64_t)(valid ? h : 0) * D.Hs;
-    const int64_t p = valid ? n * D.nh + h : 0;
-    Vec<PER> y;
-    store_vec<SEG, PER>(h0_out + p * D.d, load_vec<SEG, PER>(z, nd, ls), ls);
-    l2norm_fwd<SEG, PER, T>(load_vec<SEG, PER>(z + D.oA, nd, ls), y);
-    store_vec<SEG, PER>(A_out + p * D.d, y, ls);
-    l2norm_fwd<SEG, PER, T>(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oR, ndu, ls)), y);
-#pragma unroll
-    for (int k = 0; k < PER; ++k) y.v[k] = round_t<T>(fmaxf(y.v[k], kRinvMin));
-    store_vec<SEG, PER>(R_out + p * D.du, y, ls);
-    l2norm_fwd<SEG, PER, T>(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oQf, nd, ls)), y);
-    store_vec<SEG, PER>(cQf_out + p * D.d, y, ls);
-    if (valid && ls == 0) stf(lgA_out + p, -round_t<T>(softplus(ldf(z + D.oGA))));
-    store_vec<SEG, PER>(lgB_out + p * D.du, negated(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oGB, ndu, ls))), ls);
-    store_vec<SEG, PER>(lgQ_out + p * D.d, negated(softplus_vec<PER, T>(load_vec<SEG, PER>(z + D.oGQ, nd, ls))), ls);
+  }
+  __syncthreads();
+  int64_t i = 0;
+  for (int64_t n = blockIdx.x; n < N; n += gridDim.x, ++i) {
+    const int s = static_cast<int>(i & 1);
+    const T* zr = reinterpret_cast<const T*>(reinterpret_cast<const unsigned char*>(stage0) + s * pitch);
+    const bool ok = wait_phase(&mbar[s], static_cast<uint32_t>((i >> 1) & 1));
+    if (!ok) stop = 1;
+    __syncthreads();
+    if (stop) break;
+    for (int task = warp; task < tpr; task += nwarps) prologue_fwd_task<SEG, PER, T>(zr, n, task, tpr, D, o);
+    __syncthreads();  // every warp is done with this stage
+    const int64_t next = n + 2 * (int64_t)gridDim.x;
+    if (threadIdx.x == 0 && next < N) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our reads before the copy's writes
+      bulk_load(reinterpret_cast<unsigned char*>(stage0) + s * pitch, Z + next * D.W, row_bytes, &mbar[s]);
+    }
+  }
+  if (stop && threadIdx.x == 0) {
+    atomicOr(status, TTC_STATUS_COPY_TIMEOUT);
+    // copies still in flight: give them (boundedly) time to land before the CTA exits
+    for (int s = 0; s < 2; ++s) {
+      const int64_t k = i + s;
+      const int64_t n = blockIdx.x + k * (int64_t)gridDim.x;
+      if (n < N) (void)wait_phase(&mbar[k & 1], static_cast<uint32_t>((k >> 1) & 1));
+    }
   }
 }
 
@@ -409,11 +505,33 @@ int rownorm_checks(const void* x, int64_t rows, int n, int dtype, const void* ou
 
 
 template <int SEG, int PER, typename T>
-int fwd_launch(const void* Z, int64_t N, const Dims& D, void* const* o, cudaStream_t st) {
+int fwd_launch(const void* Z, int64_t N, const Dims& D, void* const* o, int* status, cudaStream_t st) {
+  const FwdOut<T> out{(T*)o[0], (T*)o[1], (T*)o[2], (T*)o[3], (T*)o[4], (T*)o[5], (T*)o[6], (T*)o[7], (T*)o[8]};
+  const size_t row_bytes = (size_t)D.W * sizeof(T);
+  const size_t pitch = (row_bytes + 127) / 128 * 128;
+  const size_t smem = 128 + 2 * pitch;
+  // Bulk copies need 16-byte aligned rows (every BASELINE config's projection is); otherwise,
+  // or without a status word to report a stalled copy, the warps read Z directly.
+  const bool tma = status != nullptr && reinterpret_cast<uintptr_t>(Z) % 16 == 0 && row_bytes % 16 == 0 &&
+                   smem <= 200 * 1024;
+  if (tma) {
+    auto k = prologue_fwd_tma_kernel<SEG, PER, T>;
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return launched("prologue_fwd_tma_kernel attribute");
+    }
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 256, smem) != cudaSuccess)
+      return launched("prologue_fwd_tma_kernel occupancy");
+    const int64_t wave = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
+    const unsigned grid = static_cast<unsigned>(N < wave ? N : wave);
+    k<<<grid, 256, smem, st>>>((const T*)Z, N, D, out, status);
+    return launched("prologue_fwd_tma_kernel launch");
+  }
   const unsigned grid = grid_for(N * (int64_t)((D.nh + 32 / SEG - 1) / (32 / SEG) + 1));
-  prologue_fwd_kernel<SEG, PER, T><<<grid, 256, 0, st>>>((const T*)Z, N, D, (T*)o[0], (T*)o[1], (T*)o[2],
-                                                         (T*)o[3], (T*)o[4], (T*)o[5], (T*)o[6], (T*)o[7],
-                                                         (T*)o[8]);
+  prologue_fwd_kernel<SEG, PER, T><<<grid, 256, 0, st>>>((const T*)Z, N, D, out);
   return launched("prologue_fwd_kernel launch");
 }
 
@@ -434,11 +552,11 @@ int shape_of(const Dims& D) {
 }
 
 template <typename T>
-int fwd_typed(const void* Z, int64_t N, const Dims& D, void* const* o, cudaStream_t st) {
+int fwd_typed(const void* Z, int64_t N, const Dims& D, void* const* o, int* status, cudaStream_t st) {
   switch (shape_of(D)) {
-    case 0: return fwd_launch<16, 1, T>(Z, N, D, o, st);
-    case 1: return fwd_launch<32, 1, T>(Z, N, D, o, st);
-    default: return fwd_launch<32, 2, T>(Z, N, D, o, st);
+    case 0: return fwd_launch<16, 1, T>(Z, N, D, o, status, st);
+    case 1: return fwd_launch<32, 1, T>(Z, N, D, o, status, st);
+    default: return fwd_launch<32, 2, T>(Z, N, D, o, status, st);
   }
 }
 
@@ -455,7 +573,7 @@ int bwd_typed(const void* Z, int64_t N, const Dims& D, const void* const* g, voi
 
 extern "C" int ttc_prologue_fwd(const void* Z, int64_t N, int nh, int d, int du, int rB, int rQ, int dtype,
                                 void* A_diag, void* R_inv, void* coeff_Qf, void* lgA, void* lgB, void* lgQ,
-                                void* h0, void* coeff_B, void* coeff_Q, void* stream) {
+                                void* h0, void* coeff_B, void* coeff_Q, int* status, void* stream) {
   if (int rc = check_dims(N, nh, d, du, rB, rQ, dtype)) return rc;
   if (N == 0) return TTC_OK;
   if (!Z || !A_diag || !R_inv || !coeff_Qf || !lgA || !lgB || !lgQ || !h0 || !coeff_B || !coeff_Q)
@@ -463,7 +581,8 @@ extern "C" int ttc_prologue_fwd(const void* Z, int64_t N, int nh, int d, int du,
   const Dims D(nh, d, du, rB, rQ);
   void* const o[9] = {A_diag, R_inv, coeff_Qf, lgA, lgB, lgQ, h0, coeff_B, coeff_Q};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == TTC_DTYPE_F32 ? fwd_typed<float>(Z, N, D, o, st) : fwd_typed<__nv_bfloat16>(Z, N, D, o, st);
+  return dtype == TTC_DTYPE_F32 ? fwd_typed<float>(Z, N, D, o, status, st)
+                                : fwd_typed<__nv_bfloat16>(Z, N, D, o, status, st);
 }
 
 extern "C" int ttc_prologue_bwd(const void* Z, int64_t N, int nh, int d, int du, int rB, int rQ, int dtype,

@@ -32,6 +32,8 @@ bool supported(int d, int du) {
     X(64, 16, TT);                      \
   } while (0)
 
+bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
+
 int check_flags(int flags) {
   if (flags & ~TTC_FLAG_INV_GUARD) return fail(TTC_ERR_INVALID, "unknown flag bits");
   return TTC_OK;
@@ -227,6 +229,8 @@ int ttc_lqr_fwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_b
   if (!A_diag || !coeff_B || !B_basis || !coeff_Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A ||
       !log_gamma_B || !log_gamma_Q || !h0 || !u || !status)
     return fail(TTC_ERR_INVALID, "null pointer argument");
+  if (misaligned16(B_basis) || misaligned16(Q_basis))
+    return fail(TTC_ERR_INVALID, "B_basis and Q_basis must be 16-byte aligned");
   ttc::QMix mix;
   mix.basis = Q_basis;
   mix.rank = rQ;
@@ -258,6 +262,9 @@ int ttc_lqr_bwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_b
       !log_gamma_B || !log_gamma_Q || !h0 || !d_u || !status || !lam0 || !M || !grad_basis_partial ||
       !grad_B_basis_partial)
     return fail(TTC_ERR_INVALID, "null pointer argument (the low-rank backward needs lam0 and M)");
+  if (misaligned16(B_basis) || misaligned16(Q_basis) || misaligned16(grad_basis_partial) ||
+      misaligned16(grad_B_basis_partial))
+    return fail(TTC_ERR_INVALID, "the bases and the partial buffers must be 16-byte aligned");
   void* g[9] = {grad_A, nullptr, nullptr, grad_R_inv, nullptr, grad_lgA, grad_lgB, grad_lgQ, grad_h0};
   for (int i = 0; i < 9; ++i)
     if ((i == 0 || i == 3 || i > 4) && !g[i]) return fail(TTC_ERR_INVALID, "null gradient pointer");

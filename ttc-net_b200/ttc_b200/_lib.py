@@ -29,6 +29,7 @@ STATUS_BWD_UNSTABLE = 4
 STATUS_U_NAN = 8
 STATUS_MMA_TIMEOUT = 16
 STATUS_TRAJ_NONFINITE = 32
+STATUS_COPY_TIMEOUT = 64
 
 FLAG_INV_GUARD = 1
 
@@ -57,7 +58,7 @@ SIGNATURES = {
                             + [_P] * 4 + [_P, _P]),
     "ttc_rownorm_fwd": (_I, [_P, _I64, _I, _I, _P, _P]),
     "ttc_rownorm_bwd": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
-    "ttc_prologue_fwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P]),
+    "ttc_prologue_fwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P, _P]),
     "ttc_prologue_bwd": (_I, [_P, _I64] + [_I] * 6 + [_P] * 9 + [_P, _P]),
 }
 

@@ -20,6 +20,7 @@ import torch.nn.functional as F
 from torch.utils.checkpoint import checkpoint
 
 from .epilogue import rownorm
+from .prologue import check_status as check_prologue_status
 from .prologue import prologue
 from .reductions import linear, lowrank_mix
 from .solver import (LQR_SOLVER_IMPL_MAP, U_NAN_MSG, cuda_lqr_solve, lqr_solve_lowrank_with_status,
@@ -223,12 +224,14 @@ class TTCLayer(nn.Module):
                 u, status = lqr_solve_lowrank_with_status(*parts, T)
             else:
                 u, status = lqr_solve_with_status(*self._materialise(self._mix(parts)), T)
+            check_prologue_status()  # after the solver's status read: no extra wait
             if status & _lib.STATUS_U_NAN:
                 raise RuntimeError(U_NAN_MSG)
         else:
             u = self.solver(*self._materialise(self._mix(parts)), T)
             if torch.isnan(u).any():
                 raise RuntimeError(U_NAN_MSG)
+            check_prologue_status()
         if self.rescale == "l2_norm":
             u = rownorm(u)
         elif self.rescale == "h0_norm":
