@@ -56,6 +56,9 @@ def parse_args(argv=None):
                     help="rows (of B*L*H) per layer call inside a step (0: TTCLayer.rows_per_call)")
     ap.add_argument("--batch", type=int, default=0,
                     help="sequences per GPU (0: the config's B); smaller batches for ncu captures")
+    ap.add_argument("--seq-len", type=int, default=0,
+                    help="positions per sequence (0: the config's L); a fraction of a config's rows "
+                         "(rows are independent, so tokens/s carries over)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU time of the cpu_baseline sample")
@@ -272,7 +275,7 @@ STRONG_SCALING = {5}
 def workload_name(cfg, world, strong):
     base = (f"{cfg.name}: TTCLayer fwd+bwd, x[{cfg.B},{cfg.L},{cfg.H},{cfg.in_dim}] per GPU "
             f"as [B, L*H, in] rows, h_dim={cfg.h_dim}, rank={cfg.rank}, T={cfg.T}")
-    if cfg.name == "cfg3":
+    if cfg.name == "cfg3" and cfg.B == 8 and cfg.L == 4096:
         base += (f"; {cfg.B * world} sequences over {world} GPU(s) (config 5's geometry; at 8 GPUs "
                  "its global batch of 64)")
     elif strong:
@@ -300,6 +303,9 @@ def main(argv=None):
     if args.batch:
         import dataclasses
         cfg = dataclasses.replace(cfg, B=args.batch)
+    if args.seq_len:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, L=args.seq_len)
     if args.workload == "traj":
         if args.warmup < 3:
             raise SystemExit("--warmup must be >= 3")
@@ -313,7 +319,7 @@ def main(argv=None):
     device = torch.device("cuda", local)
     # Config 5 is defined at a fixed global batch (64 sequences split over the GPUs):
     # strong scaling.  The other configs keep their per-GPU batch (weak scaling).
-    strong = args.config in STRONG_SCALING and not args.batch
+    strong = args.config in STRONG_SCALING and not args.batch and not args.seq_len
     if strong:
         import dataclasses
         if cfg.B % world:
