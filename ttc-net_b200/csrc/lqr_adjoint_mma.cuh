@@ -365,8 +365,10 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         const TIn* cBn = lr.cB + nr * lr.rB;
         const TIn* cQn = lr.cQ + nr * rQ;
         for (int e4 = tid; e4 < D * D / 4; e4 += nthreads) {
-          *reinterpret_cast<float4*>(tB + 4 * e4) = mix4<TIn>(cBn, lr.Bb, lr.rB, D * D, 4 * e4);
-          *reinterpret_cast<float4*>(tQ + 4 * e4) = mix4<TIn>(cQn, Qbasis, rQ, D * D, 4 * e4);
+          float4 vb, vq;
+          mix4_pair<TIn>(cBn, lr.Bb, lr.rB, cQn, Qbasis, rQ, D * D, 4 * e4, vb, vq);
+          *reinterpret_cast<float4*>(tB + 4 * e4) = vb;
+          *reinterpret_cast<float4*>(tQ + 4 * e4) = vq;
         }
         __syncthreads();
         build_operand<D>(base, [&](int k, int c) { return tQ[c * D + k]; }, tid, nthreads);
@@ -723,6 +725,7 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       __syncthreads();
       const int nw = nthreads >> 5;
       const int nrows = static_cast<int>(N - n0 < rows_per_cta ? N - n0 : rows_per_cta);
+      constexpr int kQuads = D * D / 128;  // float4 quads of a d x d matrix per lane
       for (int k = warp; k < lr.rB + rQ; k += nw) {
         const bool isb = k < lr.rB;
         const int rr = isb ? k : k - lr.rB;
@@ -731,41 +734,37 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         const TIn* bas = (isb ? lr.Bb : Qbasis) + (int64_t)rr * D * D;
         float* sl = (isb ? bslice : slice) + (int64_t)rr * D * D;
         const int goff = isb ? 0 : D * D;
-        float c[C::kMaxWarps], dot[C::kMaxWarps];
+        // all of the lane's basis and slice quads in flight at once (one L2 round trip)
+        float4 b[kQuads], a[kQuads];
 #pragma unroll
-        for (int r = 0; r < C::kMaxWarps; ++r) {
-          c[r] = r < nrows ? ldf(cf + (int64_t)r * rank) : 0.f;
-          dot[r] = 0.f;
-        }
-#pragma unroll 4
-        for (int e4 = lane; e4 < D * D / 4; e4 += 32) {
-          const float4 b = ld4(bas + 4 * e4);
-          float4 a = *reinterpret_cast<const float4*>(sl + 4 * e4);
-#pragma unroll
-          for (int r = 0; r < C::kMaxWarps; ++r) {
-            if (r < nrows) {
-              const float4 gv = *reinterpret_cast<const float4*>(rows_s + r * C::kRow + goff + 4 * e4);
-              dot[r] = fmaf(gv.x, b.x, fmaf(gv.y, b.y, fmaf(gv.z, b.z, fmaf(gv.w, b.w, dot[r]))));
-              a.x = fmaf(c[r], gv.x, a.x);
-              a.y = fmaf(c[r], gv.y, a.y);
-              a.z = fmaf(c[r], gv.z, a.z);
-              a.w = fmaf(c[r], gv.w, a.w);
-            }
-          }
-          *reinterpret_cast<float4*>(sl + 4 * e4) = a;
+        for (int q = 0; q < kQuads; ++q) {
+          b[q] = ld4(bas + 4 * (lane + 32 * q));
+          a[q] = *reinterpret_cast<const float4*>(sl + 4 * (lane + 32 * q));
         }
 #pragma unroll
         for (int r = 0; r < C::kMaxWarps; ++r) {
           if (r < nrows) {
-            float v = dot[r];
+            const float c = ldf(cf + (int64_t)r * rank);
+            float dot = 0.f;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            for (int q = 0; q < kQuads; ++q) {
+              const float4 gv = *reinterpret_cast<const float4*>(rows_s + r * C::kRow + goff + 4 * (lane + 32 * q));
+              dot = fmaf(gv.x, b[q].x, fmaf(gv.y, b[q].y, fmaf(gv.z, b[q].z, fmaf(gv.w, b[q].w, dot))));
+              a[q].x = fmaf(c, gv.x, a[q].x);
+              a[q].y = fmaf(c, gv.y, a[q].y);
+              a[q].z = fmaf(c, gv.z, a[q].z);
+              a[q].w = fmaf(c, gv.w, a[q].w);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
             if (lane == 0) {
-              bad |= unstable(v);
-              stf((isb ? lr.gcB : lr.gcQ) + (n0 + r) * rank + rr, v);
+              bad |= unstable(dot);
+              stf((isb ? lr.gcB : lr.gcQ) + (n0 + r) * rank + rr, dot);
             }
           }
         }
+#pragma unroll
+        for (int q = 0; q < kQuads; ++q) *reinterpret_cast<float4*>(sl + 4 * (lane + 32 * q)) = a[q];
       }
     }
     __syncthreads();  // the next row group reuses the shared operands and staging

@@ -86,6 +86,36 @@ __device__ __forceinline__ float4 mix4(const TIn* __restrict__ c, const TIn* __r
   return make_float4(round_to<TIn>(s.x), round_to<TIn>(s.y), round_to<TIn>(s.z), round_to<TIn>(s.w));
 }
 
+// mix4 of two mixtures at once (B and Q of a row): their loads interleave in one rank loop.
+template <typename TIn>
+__device__ __forceinline__ void mix4_pair(const TIn* __restrict__ c1, const TIn* __restrict__ b1, int rank1,
+                                          const TIn* __restrict__ c2, const TIn* __restrict__ b2, int rank2,
+                                          int len, int e, float4& o1, float4& o2) {
+  float4 s1 = make_float4(0.f, 0.f, 0.f, 0.f), s2 = s1;
+  const int rank = rank1 > rank2 ? rank1 : rank2;
+#pragma unroll 8
+  for (int r = 0; r < rank; ++r) {
+    if (r < rank1) {
+      const float cr = ldf(c1 + r);
+      const float4 b = ld4(b1 + (int64_t)r * len + e);
+      s1.x = fmaf(cr, b.x, s1.x);
+      s1.y = fmaf(cr, b.y, s1.y);
+      s1.z = fmaf(cr, b.z, s1.z);
+      s1.w = fmaf(cr, b.w, s1.w);
+    }
+    if (r < rank2) {
+      const float cr = ldf(c2 + r);
+      const float4 b = ld4(b2 + (int64_t)r * len + e);
+      s2.x = fmaf(cr, b.x, s2.x);
+      s2.y = fmaf(cr, b.y, s2.y);
+      s2.z = fmaf(cr, b.z, s2.z);
+      s2.w = fmaf(cr, b.w, s2.w);
+    }
+  }
+  o1 = make_float4(round_to<TIn>(s1.x), round_to<TIn>(s1.y), round_to<TIn>(s1.z), round_to<TIn>(s1.w));
+  o2 = make_float4(round_to<TIn>(s2.x), round_to<TIn>(s2.y), round_to<TIn>(s2.z), round_to<TIn>(s2.w));
+}
+
 // True for NaN, +-Inf and |v| >= 1e6: the reference's isnan | isinf | abs >= 1e6.
 __device__ __forceinline__ bool unstable(float v) { return !(fabsf(v) < kUnstable); }
 
