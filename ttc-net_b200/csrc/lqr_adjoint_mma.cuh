@@ -354,23 +354,28 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     // The CTA's rows: constant operands Q^T, B, B^T, Q in fragment order, symmetry flag.
     if (tid < rows_per_cta) reinterpret_cast<int*>(rows_s + tid * C::kRow + 4 * C::kFrag)[0] = 1;
     __syncthreads();
+    if (lowrank) {
+      // B and Q of every row of the group, mixed into the (still unused) staging area first:
+      // row r's [B | Q] at warp_s + 2 r d^2 (a row's own warps' staging holds more than 2 d^2)
+      static_assert(2 * D * D <= C::kWarp, "mixing area");
+      const int nrows = static_cast<int>(N - n0 < rows_per_cta ? N - n0 : rows_per_cta);
+      for (int idx = tid; idx < nrows * (D * D / 4); idx += nthreads) {
+        const int r = idx / (D * D / 4), e4 = idx % (D * D / 4);
+        float4 vb, vq;
+        mix4_pair<TIn>(lr.cB + (n0 + r) * lr.rB, lr.Bb, lr.rB, lr.cQ + (n0 + r) * rQ, Qbasis, rQ, D * D, 4 * e4, vb,
+                       vq);
+        *reinterpret_cast<float4*>(warp_s + 2 * r * D * D + 4 * e4) = vb;
+        *reinterpret_cast<float4*>(warp_s + (2 * r + 1) * D * D + 4 * e4) = vq;
+      }
+      __syncthreads();
+    }
     for (int r = 0; r < rows_per_cta; ++r) {
       const int64_t nr = n0 + r;
       if (nr >= N) break;
       float* base = rows_s + r * C::kRow;
       if (lowrank) {
-        // B and Q of the row, mixed into the (still unused) staging area first
-        float* tB = warp_s;
-        float* tQ = warp_s + D * D;
-        const TIn* cBn = lr.cB + nr * lr.rB;
-        const TIn* cQn = lr.cQ + nr * rQ;
-        for (int e4 = tid; e4 < D * D / 4; e4 += nthreads) {
-          float4 vb, vq;
-          mix4_pair<TIn>(cBn, lr.Bb, lr.rB, cQn, Qbasis, rQ, D * D, 4 * e4, vb, vq);
-          *reinterpret_cast<float4*>(tB + 4 * e4) = vb;
-          *reinterpret_cast<float4*>(tQ + 4 * e4) = vq;
-        }
-        __syncthreads();
+        const float* tB = warp_s + 2 * r * D * D;
+        const float* tQ = tB + D * D;
         build_operand<D>(base, [&](int k, int c) { return tQ[c * D + k]; }, tid, nthreads);
         build_operand<D>(base + C::kFrag, [&](int k, int c) { return tB[k * D + c]; }, tid, nthreads);
         build_operand<D>(base + 2 * C::kFrag, [&](int k, int c) { return tB[c * D + k]; }, tid, nthreads);
@@ -378,7 +383,6 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         bool asym = false;
         for (int e = tid; e < D * D; e += nthreads) asym |= tQ[e] != tQ[(e % D) * D + e / D];
         if (asym) reinterpret_cast<int*>(base + 4 * C::kFrag)[0] = 0;
-        __syncthreads();
         continue;
       }
       const TIn* Bn = Bm + nr * (D * D);
