@@ -78,6 +78,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False, o
         for obj, log in ex.map(lambda s: _compile(nvcc, s, objdir, extra), srcs):
             objs.append(obj)
             logs.append(log)
+    os.makedirs(os.path.dirname(os.path.abspath(lib)), exist_ok=True)
     tmp = lib + ".tmp"
     r = subprocess.run([nvcc, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", tmp, *objs],
                        capture_output=True, text=True)
