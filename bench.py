@@ -206,13 +206,43 @@ def run_step(layer, x, dy, T, chunk, world, reducer=None):
 
 
 # ------------------------------------------------------------------------- CPU legs
+REFERENCE_INSTALL = os.path.join(REPO, "baseline", "_ref")
+
+
+def reference_cpu_layer(cfg):
+    """The reference's own TTCLayer(solver_impl="riccati") from its unmodified install in
+    baseline/_ref (pip install --target), with fla's l2norm -- a Triton wrapper that does not
+    run on CPU tensors -- replaced by its formula x / sqrt(sum x^2 + 1e-6) in fp32
+    (fla/modules/l2norm.py:42); None when the install is absent.  Returns (layer, kind)."""
+    if not os.path.isdir(os.path.join(REFERENCE_INSTALL, "ttc")):
+        return None
+    if REFERENCE_INSTALL not in sys.path:
+        sys.path.insert(0, REFERENCE_INSTALL)
+    try:
+        import ttc.layers.ttc_layer as ref_mod
+    except Exception:  # noqa: BLE001 - any import failure means: use the port
+        return None
+
+    def l2norm_cpu(x, eps=1e-6):
+        xf = x.float()
+        return (xf / torch.sqrt((xf * xf).sum(-1, keepdim=True) + eps)).to(x.dtype)
+
+    ref_mod.l2norm = l2norm_cpu
+    return ref_mod.TTCLayer(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
+                            solver_impl="riccati")
+
+
 def cpu_sample(cfg, target_s, threads, rows=None):
-    """Reference algorithm on the host: oracle riccati layer fwd + autograd bwd on a row
-    sample sized to ~target_s seconds (or of `rows` rows).  Returns (tokens/s, rows, seconds)."""
-    from oracle import ttc_oracle as O
+    """Reference algorithm on the host: the riccati layer fwd + autograd bwd (the reference's
+    own TTCLayer from baseline/_ref when installed, else the oracle's restatement of it) on a
+    row sample sized to ~target_s seconds (or of `rows` rows).  Returns (tokens/s, rows,
+    seconds, kind) with kind "reference" or "port"."""
     torch.set_num_threads(threads)
-    layer = O.TTCLayerOracle(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
-                             solver_impl="riccati")
+    layer, kind = reference_cpu_layer(cfg), "reference"
+    if layer is None:
+        from oracle import ttc_oracle as O
+        layer, kind = O.TTCLayerOracle(cfg.in_dim, cfg.out_dim, cfg.h_dim, cfg.H, cfg.rank, cfg.rank,
+                                       solver_impl="riccati"), "port"
     layer.load_state_dict({k: torch.from_numpy(v) for k, v in layer_weights(cfg).items()})
 
     def once(rows):
@@ -226,7 +256,7 @@ def cpu_sample(cfg, target_s, threads, rows=None):
 
     if rows is not None:
         dt = once(rows)
-        return (rows / cfg.H) / dt, rows, dt
+        return (rows / cfg.H) / dt, rows, dt, kind
     # A tiny probe is dominated by per-step Python overhead and overestimates the cost of a
     # row; one more rescale from the first real sample brings the sample to ~target_s.
     probe = max(1, cfg.H // 8)
@@ -236,7 +266,7 @@ def cpu_sample(cfg, target_s, threads, rows=None):
     if dt < 0.5 * target_s and rows < cfg.rows:
         rows = int(min(cfg.rows, rows * target_s / max(dt, 1e-6)))
         dt = once(rows)
-    return (rows / cfg.H) / dt, rows, dt
+    return (rows / cfg.H) / dt, rows, dt, kind
 
 
 def reference_arm(args, cfg):
@@ -248,21 +278,24 @@ def reference_arm(args, cfg):
     budget = 150.0 / max(1, args.steps + args.warmup)
     vals = []
     rows_used = None
+    kind = "port"
     for k in range(args.warmup + args.steps):
-        v, rows_used, _ = cpu_sample(cfg, budget, threads, rows_used)
+        v, rows_used, _, kind = cpu_sample(cfg, budget, threads, rows_used)
         if k >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
+    what = ("the reference's TTCLayer from baseline/_ref, fla l2norm as its formula" if kind == "reference"
+            else "oracle port")
     sample = (f"{rows_used} of {cfg.rows} rows per step ({cfg.name}: riccati fwd + autograd "
-              f"bwd, fp32, oracle port)")
+              f"bwd, fp32, {what})")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * (rows_used / cfg.H) / value, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {**workload_config(cfg, world, args, chunk=None),
-                   "solver_impl": "riccati (oracle port, CPU)"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "solver_impl": f"riccati ({what}, CPU)"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -510,11 +543,13 @@ def main(argv=None):
         }
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            v, rows_used, dt = cpu_sample(cfg, args.cpu_seconds, threads)
+            v, rows_used, dt, kind = cpu_sample(cfg, args.cpu_seconds, threads)
+            what = ("the reference's TTCLayer (baseline/_ref, fla l2norm as its formula)" if kind == "reference"
+                    else "oracle port of the reference's")
             out["cpu_baseline"] = {
-                "value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
                 "sample": f"{rows_used} of {cfg.rows} rows ({rows_used / cfg.H:.1f} tokens), "
-                          f"{dt:.1f} s: oracle riccati layer fwd + autograd bwd, fp32"}
+                          f"{dt:.1f} s: {what} riccati layer fwd + autograd bwd, fp32"}
         print(json.dumps(out), flush=True)
     if world > 1:
         import torch.distributed as dist
