@@ -140,7 +140,7 @@ int ttc_lqr_rollout(const void* A_diag, const void* B, const void* Q, const void
 /* ttc_lqr_fwd with Q_f given as the layer's rank-rQ mixture (ttc_layer.py:119-123,
  * Q_f[n,h] = sum_r coeff_Qf[n,h,r] Q_basis[r]) instead of the [N,nh,d,d] tensor:
  * coeff_Qf [N,nh,rQ], Q_basis [rQ,d,d], both in the activation dtype; each kernel mixes the
- * rows of Q_f it needs.  Everything else as ttc_lqr_fwd. */
+ * rows of Q_f it needs.  Q_basis must be 16-byte aligned.  Everything else as ttc_lqr_fwd. */
 int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                     const void* coeff_Qf, const void* Q_basis, int rQ, const void* log_gamma_A,
                     const void* log_gamma_B, const void* log_gamma_Q, const void* h0, int64_t N, int nh,

@@ -30,6 +30,13 @@ __device__ __forceinline__ void split(float x, uint32_t& hi, uint32_t& lo) {
   lo = __float_as_uint(x - __uint_as_float(hi));
 }
 
+// x rounded to tf32 (nearest, ties away from zero): the operand of a single-pass tf32 MMA.
+__device__ __forceinline__ uint32_t rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
 // D (16x8, f32) += A (16x8, tf32, row) * B (8x8, tf32, col).
 __device__ __forceinline__ void m16n8k8(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -218,6 +225,10 @@ __device__ __forceinline__ bool qmix_cta(const float* warp_s, int stage_off, int
                                          const TIn* __restrict__ coeff, TIn* __restrict__ gcoeff,
                                          float* __restrict__ slice, int warp, int g, int t) {
   constexpr int SS = AdjMma<D>::SS, NT = D / 8, MT = D / 16, kWarp = AdjMma<D>::kWarp;
+  // bf16 activations: single-pass tf32 with round-to-nearest operands (relative error ~2^-11
+  // per product, unbiased, below the bf16 rounding of the einsum backward it replaces);
+  // float: 3xTF32
+  constexpr bool kOne = sizeof(TIn) == 2;
   bool bad = false;
   for (int r = warp; r < rQ; r += nwarps) {
     // basis[r] as the constant operand: W[k][n] = basis[r][k][n], K rows permuted as the
@@ -228,8 +239,15 @@ __device__ __forceinline__ bool qmix_cta(const float* warp_s, int stage_off, int
     for (int kk = 0; kk < NT; ++kk)
 #pragma unroll
       for (int nj = 0; nj < NT; ++nj) {
-        wmma::split(ldf(Wr + (8 * kk + 2 * t) * D + 8 * nj + g), wh[kk][nj][0], wl[kk][nj][0]);
-        wmma::split(ldf(Wr + (8 * kk + 2 * t + 1) * D + 8 * nj + g), wh[kk][nj][1], wl[kk][nj][1]);
+        const float w0 = ldf(Wr + (8 * kk + 2 * t) * D + 8 * nj + g);
+        const float w1 = ldf(Wr + (8 * kk + 2 * t + 1) * D + 8 * nj + g);
+        if constexpr (kOne) {
+          wh[kk][nj][0] = wmma::rna(w0);
+          wh[kk][nj][1] = wmma::rna(w1);
+        } else {
+          wmma::split(w0, wh[kk][nj][0], wl[kk][nj][0]);
+          wmma::split(w1, wh[kk][nj][1], wl[kk][nj][1]);
+        }
       }
     float acc[MT][NT][4];
 #pragma unroll
@@ -260,15 +278,24 @@ __device__ __forceinline__ bool qmix_cta(const float* warp_s, int stage_off, int
 #pragma unroll
       for (int kk = 0; kk < NT; ++kk) {
         uint32_t ah[4], al[4];
-        wmma::split(Hs[kk][0], ah[0], al[0]);
-        wmma::split(Hs[kk][2], ah[1], al[1]);
-        wmma::split(Hs[kk][1], ah[2], al[2]);
-        wmma::split(Hs[kk][3], ah[3], al[3]);
+        if constexpr (kOne) {
+          ah[0] = wmma::rna(Hs[kk][0]);
+          ah[1] = wmma::rna(Hs[kk][2]);
+          ah[2] = wmma::rna(Hs[kk][1]);
+          ah[3] = wmma::rna(Hs[kk][3]);
 #pragma unroll
-        for (int nj = 0; nj < NT; ++nj) {
-          wmma::m16n8k8(P[nj], al, wh[kk][nj][0], wh[kk][nj][1]);
-          wmma::m16n8k8(P[nj], ah, wl[kk][nj][0], wl[kk][nj][1]);
-          wmma::m16n8k8(P[nj], ah, wh[kk][nj][0], wh[kk][nj][1]);
+          for (int nj = 0; nj < NT; ++nj) wmma::m16n8k8(P[nj], ah, wh[kk][nj][0], wh[kk][nj][1]);
+        } else {
+          wmma::split(Hs[kk][0], ah[0], al[0]);
+          wmma::split(Hs[kk][2], ah[1], al[1]);
+          wmma::split(Hs[kk][1], ah[2], al[2]);
+          wmma::split(Hs[kk][3], ah[3], al[3]);
+#pragma unroll
+          for (int nj = 0; nj < NT; ++nj) {
+            wmma::m16n8k8(P[nj], al, wh[kk][nj][0], wh[kk][nj][1]);
+            wmma::m16n8k8(P[nj], ah, wl[kk][nj][0], wl[kk][nj][1]);
+            wmma::m16n8k8(P[nj], ah, wh[kk][nj][0], wh[kk][nj][1]);
+          }
         }
       }
       float sdot = 0.f;
@@ -292,21 +319,37 @@ __device__ __forceinline__ bool qmix_cta(const float* warp_s, int stage_off, int
       uint32_t xh[MT][4], xl[MT][4];
 #pragma unroll
       for (int mi = 0; mi < MT; ++mi) {
-        wmma::split(S[t * SS + 16 * mi + g], xh[mi][0], xl[mi][0]);
-        wmma::split(S[t * SS + 16 * mi + g + 8], xh[mi][1], xl[mi][1]);
-        wmma::split(S[(t + 4) * SS + 16 * mi + g], xh[mi][2], xl[mi][2]);
-        wmma::split(S[(t + 4) * SS + 16 * mi + g + 8], xh[mi][3], xl[mi][3]);
+        const float x0 = S[t * SS + 16 * mi + g], x1 = S[t * SS + 16 * mi + g + 8];
+        const float x2 = S[(t + 4) * SS + 16 * mi + g], x3 = S[(t + 4) * SS + 16 * mi + g + 8];
+        if constexpr (kOne) {
+          xh[mi][0] = wmma::rna(x0);
+          xh[mi][1] = wmma::rna(x1);
+          xh[mi][2] = wmma::rna(x2);
+          xh[mi][3] = wmma::rna(x3);
+        } else {
+          wmma::split(x0, xh[mi][0], xl[mi][0]);
+          wmma::split(x1, xh[mi][1], xl[mi][1]);
+          wmma::split(x2, xh[mi][2], xl[mi][2]);
+          wmma::split(x3, xh[mi][3], xl[mi][3]);
+        }
       }
 #pragma unroll
       for (int nj = 0; nj < NT; ++nj) {
-        uint32_t bh0, bl0, bh1, bl1;
-        wmma::split(c0 * S[(8 + t) * SS + 8 * nj + g], bh0, bl0);
-        wmma::split(c1 * S[(12 + t) * SS + 8 * nj + g], bh1, bl1);
+        const float y0 = c0 * S[(8 + t) * SS + 8 * nj + g], y1 = c1 * S[(12 + t) * SS + 8 * nj + g];
+        if constexpr (kOne) {
+          const uint32_t b0 = wmma::rna(y0), b1 = wmma::rna(y1);
 #pragma unroll
-        for (int mi = 0; mi < MT; ++mi) {
-          wmma::m16n8k8(acc[mi][nj], xl[mi], bh0, bh1);
-          wmma::m16n8k8(acc[mi][nj], xh[mi], bl0, bl1);
-          wmma::m16n8k8(acc[mi][nj], xh[mi], bh0, bh1);
+          for (int mi = 0; mi < MT; ++mi) wmma::m16n8k8(acc[mi][nj], xh[mi], b0, b1);
+        } else {
+          uint32_t bh0, bl0, bh1, bl1;
+          wmma::split(y0, bh0, bl0);
+          wmma::split(y1, bh1, bl1);
+#pragma unroll
+          for (int mi = 0; mi < MT; ++mi) {
+            wmma::m16n8k8(acc[mi][nj], xl[mi], bh0, bh1);
+            wmma::m16n8k8(acc[mi][nj], xh[mi], bl0, bl1);
+            wmma::m16n8k8(acc[mi][nj], xh[mi], bh0, bh1);
+          }
         }
       }
     }
@@ -442,6 +485,19 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     float a[NT][2], lgQ2[NT][2], lgB2[NT][2], rinv[NT][2];
     float L[NT][4], H[NT][4];
     const float lgA2 = valid ? ldf(lgA + p) * kLog2e : 0.f;
+    // d_p = M d_u (fused_lqr.py:185-187): the head's d_u once, the rows of M as 16-byte loads,
+    // each row's sum in column order
+    float du_row[FROM_M ? D : 1];
+    if constexpr (FROM_M) {
+#pragma unroll
+      for (int c4 = 0; c4 < D / 4; ++c4) {
+        const float4 v = valid ? ld4(dU + p * D + 4 * c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        du_row[4 * c4] = v.x;
+        du_row[4 * c4 + 1] = v.y;
+        du_row[4 * c4 + 2] = v.z;
+        du_row[4 * c4 + 3] = v.w;
+      }
+    }
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -457,8 +513,15 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         float dl = 0.f;
         if (valid) {
           if constexpr (FROM_M) {
-            const float* mrow = M_or_dp + (p * D + e) * D;
-            for (int c = 0; c < D; ++c) dl = fmaf(mrow[c], ldf(dU + p * D + c), dl);
+            const float4* m4 = reinterpret_cast<const float4*>(M_or_dp + (p * D + e) * D);
+#pragma unroll
+            for (int c4 = 0; c4 < D / 4; ++c4) {
+              const float4 mv = m4[c4];
+              dl = fmaf(mv.x, du_row[4 * c4], dl);
+              dl = fmaf(mv.y, du_row[4 * c4 + 1], dl);
+              dl = fmaf(mv.z, du_row[4 * c4 + 2], dl);
+              dl = fmaf(mv.w, du_row[4 * c4 + 3], dl);
+            }
           } else {
             dl = M_or_dp[p * D + e];
           }

@@ -64,6 +64,76 @@ __device__ __forceinline__ int gauss_jordan_regs(const Group<D>& G, float (&y1)[
   return pc;
 }
 
+// gauss_jordan_regs with the pivot row published in group shared memory instead of by warp
+// shuffles (D <= 32): the pivot thread writes its row of Y1 and of the right-hand sides
+// (16-byte stores), every thread of the group reads it back as 16-byte broadcasts.  Same
+// pivots, same arithmetic in the same order: bitwise the results of gauss_jordan_regs with a
+// quarter of the instructions for the row transfer.  pbuf: 2 * (D + NR) floats, 16-byte
+// aligned, double-buffered by step parity.
+template <int D, int NR>
+__device__ __forceinline__ int gauss_jordan_smem(const Group<D>& G, float (&y1)[D], float (&rhs)[NR],
+                                                 float& piv, float* pbuf) {
+  static_assert(D <= 32 && D % 4 == 0 && NR % 4 == 0, "shared-row Gauss-Jordan: one warp, quads");
+  constexpr int kRow = D + NR;
+  const int i = G.i;
+  bool done = false;
+  int pc = 0;
+  piv = 1.0f;
+#pragma unroll
+  for (int k = 0; k < D; ++k) {
+    float bv = done ? -1.0f : fmaxf(fabsf(y1[k]), 0.0f);
+    int bi = i;
+#pragma unroll
+    for (int o = D / 2; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(G.mask, bv, o, D);
+      const int oi = __shfl_xor_sync(G.mask, bi, o, D);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    const bool me = (i == bi);
+    float4* pr = reinterpret_cast<float4*>(pbuf + (k & 1) * kRow);
+    if (me) {
+#pragma unroll
+      for (int c4 = k / 4; c4 < D / 4; ++c4)
+        pr[c4] = make_float4(y1[4 * c4], y1[4 * c4 + 1], y1[4 * c4 + 2], y1[4 * c4 + 3]);
+#pragma unroll
+      for (int c4 = 0; c4 < NR / 4; ++c4)
+        pr[D / 4 + c4] = make_float4(rhs[4 * c4], rhs[4 * c4 + 1], rhs[4 * c4 + 2], rhs[4 * c4 + 3]);
+    }
+    __syncwarp(G.mask);
+    const float4 pk4 = pr[k / 4];
+    const float pk = (k & 3) == 0 ? pk4.x : ((k & 3) == 1 ? pk4.y : ((k & 3) == 2 ? pk4.z : pk4.w));
+    const float f = me ? 0.0f : y1[k] * recip(pk);
+    if (me) {
+      done = true;
+      pc = k;
+      piv = y1[k];
+    } else {
+      y1[k] = 0.0f;
+    }
+#pragma unroll
+    for (int c4 = (k + 1) / 4; c4 < D / 4; ++c4) {
+      const float4 v = pr[c4];
+      if (4 * c4 > k) y1[4 * c4] = fmaf(-f, v.x, y1[4 * c4]);
+      if (4 * c4 + 1 > k) y1[4 * c4 + 1] = fmaf(-f, v.y, y1[4 * c4 + 1]);
+      if (4 * c4 + 2 > k) y1[4 * c4 + 2] = fmaf(-f, v.z, y1[4 * c4 + 2]);
+      if (4 * c4 + 3 > k) y1[4 * c4 + 3] = fmaf(-f, v.w, y1[4 * c4 + 3]);
+    }
+#pragma unroll
+    for (int c4 = 0; c4 < NR / 4; ++c4) {
+      const float4 v = pr[D / 4 + c4];
+      rhs[4 * c4] = fmaf(-f, v.x, rhs[4 * c4]);
+      rhs[4 * c4 + 1] = fmaf(-f, v.y, rhs[4 * c4 + 1]);
+      rhs[4 * c4 + 2] = fmaf(-f, v.z, rhs[4 * c4 + 2]);
+      rhs[4 * c4 + 3] = fmaf(-f, v.w, rhs[4 * c4 + 3]);
+    }
+  }
+  __syncwarp(G.mask);
+  return pc;
+}
+
 // The same elimination for a group spanning several warps (D = 64): the pivot search
 // combines the warps' shuffle results through shared memory and the pivot row is published
 // in a double-buffered shared row.  pbuf holds GjBcast<D, NR>::kSize floats.
@@ -137,15 +207,26 @@ __device__ __forceinline__ int gauss_jordan_bcast(const Group<D>& G, float (&y1)
   return pc;
 }
 
-// Register Gauss-Jordan for any supported D; pbuf (GjBcast<D, NR>::kSize floats of group
-// shared memory) is only touched when the group spans several warps.
+// Shared floats the group's pivot-row buffer needs (GjRow<D, NR>::kSize, 16-byte aligned):
+// the shared-row elimination for D > 32, or for D <= 32 with quads of right-hand sides.
+template <int D, int NR>
+struct GjRow {
+  static constexpr bool kShared = D > 32 || NR % 4 == 0;
+  static constexpr int kSize = D > 32 ? GjBcast<D, NR>::kSize : (kShared ? 2 * (D + NR) : 0);
+};
+
+// Gauss-Jordan for any supported D; pbuf (GjRow<D, NR>::kSize floats of group shared memory)
+// carries the pivot row when the group spans several warps, or when the right-hand sides come
+// in quads (16-byte transfers instead of one shuffle per value; bitwise the same results).
 template <int D, int NR>
 __device__ __forceinline__ int gauss_jordan_group(const Group<D>& G, float (&y1)[D], float (&rhs)[NR],
                                                   float& piv, float* pbuf) {
-  if constexpr (D <= 32) {
-    return gauss_jordan_regs<D, NR>(G, y1, rhs, piv);
-  } else {
+  if constexpr (D > 32) {
     return gauss_jordan_bcast<D, NR>(G, y1, rhs, piv, pbuf);
+  } else if constexpr (NR % 4 == 0) {
+    return gauss_jordan_smem<D, NR>(G, y1, rhs, piv, pbuf);
+  } else {
+    return gauss_jordan_regs<D, NR>(G, y1, rhs, piv);
   }
 }
 

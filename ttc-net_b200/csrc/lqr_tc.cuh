@@ -68,15 +68,15 @@ struct TcFwdLayout {
   using C = TcCfg<D, DU>;
   // per head: sweep vectors (double-buffered), h0, lambda1 hand-over, spare, and the
   // pivot-row buffer of the cross-warp Gauss-Jordan (d = 64 only)
-  static constexpr int kPb = D > 32 ? GjBcast<D, D>::kSize : 0;
+  static constexpr int kPb = GjRow<D, D>::kSize;
   static constexpr int kGroup = round4(2 * SweepVec<D, DU>::kSize + 3 * D + kPb);
   static size_t bytes(int slots) {
     return sizeof(float) * (size_t)(C::kOps + C::kHeader + slots * C::kHeadsPerTile * kGroup);
   }
   // A mixed Q_f keeps its rank-rQ basis in shared memory behind the groups, rows padded to
-  // D + 1 floats (conflict-free row reads by the D threads of a head).
+  // D + 4 floats (16-byte row reads by the D threads of a head, conflict-free).
   __host__ __device__ static int basis_offset(int slots) { return C::kOps + C::kHeader + slots * C::kHeadsPerTile * kGroup; }
-  static size_t basis_bytes(int rQ) { return sizeof(float) * (size_t)rQ * D * (D + 1); }
+  static size_t basis_bytes(int rQ) { return sizeof(float) * (size_t)rQ * D * (D + 4); }
 };
 
 // OR of `pred` over the `count` threads of named barrier `id` (also a barrier).
@@ -367,7 +367,7 @@ __device__ __forceinline__ void add_inv_guard(float (&y1)[D], int i, int opts) {
 // This thread's row i of the terminal cost Q_f of problem p: read from Q_f [N*nh, D, D], or,
 // when `basis_s` is given, mixed from the rank-rQ basis as the layer does
 // (Q_f = sum_r coeff_Qf[r] basis[r], ttc_layer.py:119-123): `qf` is then coeff_Qf [N*nh, rQ],
-// basis_s the basis in shared memory (rows padded to D + 1), and the sum is rounded to the
+// basis_s the basis in shared memory (rows padded to D + 4), and the sum is rounded to the
 // activation dtype like the einsum it replaces.
 template <int D, typename TIn>
 __device__ __forceinline__ void load_qf_row(float (&y2)[D], bool valid, const TIn* __restrict__ qf,
@@ -386,11 +386,29 @@ __device__ __forceinline__ void load_qf_row(float (&y2)[D], bool valid, const TI
 #pragma unroll
   for (int k = 0; k < D; ++k) y2[k] = 0.0f;
   const TIn* c = qf + p * rQ;
-  for (int r = 0; r < rQ; ++r) {
-    const float cr = ldf(c + r);
-    const float* row = basis_s + (r * D + i) * (D + 1);
+  auto add_rank = [&](int r, float cr) {
+    const float4* row = reinterpret_cast<const float4*>(basis_s + (r * D + i) * (D + 4));
 #pragma unroll
-    for (int k = 0; k < D; ++k) y2[k] = fmaf(cr, row[k], y2[k]);
+    for (int k4 = 0; k4 < D / 4; ++k4) {
+      const float4 b = row[k4];
+      y2[4 * k4] = fmaf(cr, b.x, y2[4 * k4]);
+      y2[4 * k4 + 1] = fmaf(cr, b.y, y2[4 * k4 + 1]);
+      y2[4 * k4 + 2] = fmaf(cr, b.z, y2[4 * k4 + 2]);
+      y2[4 * k4 + 3] = fmaf(cr, b.w, y2[4 * k4 + 3]);
+    }
+  };
+  if ((rQ & 3) == 0 && (reinterpret_cast<uintptr_t>(c) & (4 * sizeof(TIn) - 1)) == 0) {
+    // the head's coefficients four at a time (the ranks still added in order)
+#pragma unroll 2
+    for (int r4 = 0; r4 < rQ / 4; ++r4) {
+      const float4 cc = ld4(c + 4 * r4);
+      add_rank(4 * r4, cc.x);
+      add_rank(4 * r4 + 1, cc.y);
+      add_rank(4 * r4 + 2, cc.z);
+      add_rank(4 * r4 + 3, cc.w);
+    }
+  } else {
+    for (int r = 0; r < rQ; ++r) add_rank(r, ldf(c + r));
   }
   if constexpr (sizeof(TIn) == 2) {
 #pragma unroll
@@ -398,12 +416,16 @@ __device__ __forceinline__ void load_qf_row(float (&y2)[D], bool valid, const TI
   }
 }
 
-// Cooperative copy of a rank-rQ basis [rQ, D, D] (activation dtype) into shared memory as
-// fp32 rows of D + 1.
+// Cooperative copy of a rank-rQ basis [rQ, D, D] (activation dtype, 16-byte aligned) into
+// shared memory as fp32 rows of D + 4, four values per load and store.
 template <int D, typename TIn>
 __device__ __forceinline__ void stage_basis(float* basis_s, const TIn* __restrict__ basis, int rQ, int tid,
                                             int nthreads) {
-  for (int e = tid; e < rQ * D * D; e += nthreads) basis_s[(e / D) * (D + 1) + e % D] = ldf(basis + e);
+#pragma unroll 4
+  for (int e4 = tid; e4 < rQ * D * D / 4; e4 += nthreads) {
+    const int e = 4 * e4;
+    *reinterpret_cast<float4*>(basis_s + (e / D) * (D + 4) + e % D) = ld4(basis + e);
+  }
 }
 
 template <int D, int DU, typename TIn, bool SAVE_M>
@@ -556,9 +578,11 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         break;
       }
       if (valid) {
-        float* mrow = M_out + (p * D + pc) * DU;
+        float4* mrow = reinterpret_cast<float4*>(M_out + (p * D + pc) * DU);
 #pragma unroll
-        for (int j = 0; j < DU; ++j) mrow[j] = -m[j] * v1[V::kEBR + j];
+        for (int j4 = 0; j4 < DU / 4; ++j4)
+          mrow[j4] = make_float4(-m[4 * j4] * v1[V::kEBR + 4 * j4], -m[4 * j4 + 1] * v1[V::kEBR + 4 * j4 + 1],
+                                 -m[4 * j4 + 2] * v1[V::kEBR + 4 * j4 + 2], -m[4 * j4 + 3] * v1[V::kEBR + 4 * j4 + 3]);
       }
     }
     G.sync();
@@ -591,7 +615,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
 template <int D, int DU>
 struct TcBwdLayout {
   using CF = TcCfg<D, DU>;
-  static constexpr int kPb = D > 32 ? GjBcast<D, 2>::kSize : 0;
+  static constexpr int kPb = GjRow<D, 2>::kSize;
   static constexpr int kGroup =
       round4(2 * SweepVec<D, DU>::kSize + AdjLayout<D, DU>::kSize + 4 * D + 4 + kPb);
   static constexpr int kAcc = D * DU + D * D;  // per slot

@@ -137,6 +137,8 @@ extern "C" int ttc_lqr_bwd_mix_noalloc(const void* A_diag, const void* B, const 
       !log_gamma_Q || !h0 || !lam0 || !M || !d_u || !grad_A || !grad_B || !grad_Q || !grad_R_inv ||
       !grad_coeff_Qf || !grad_basis || !grad_lgA || !grad_lgB || !grad_lgQ || !grad_h0 || !status)
     return ttc::set_error(TTC_ERR_INVALID, "null pointer argument");
+  if ((reinterpret_cast<uintptr_t>(M) | reinterpret_cast<uintptr_t>(d_u)) & 15u)
+    return ttc::set_error(TTC_ERR_INVALID, "M and d_u must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_NA(DD, TT)                                                                                 \
   return launch_noalloc<DD, TT>(A_diag, B, Q, R_inv, coeff_Qf, Q_basis, rQ, log_gamma_A, log_gamma_B,     \

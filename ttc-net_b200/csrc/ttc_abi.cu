@@ -79,6 +79,7 @@ int ttc_lqr_fwd(const void* A_diag, const void* B, const void* Q, const void* R_
   if (!A_diag || !B || !Q || !R_inv || !Q_f || !log_gamma_A || !log_gamma_B || !log_gamma_Q ||
       !h0 || !u || !status)
     return fail(TTC_ERR_INVALID, "null pointer argument");
+  if (misaligned16(M)) return fail(TTC_ERR_INVALID, "M must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_FWD(DD, DDU, TT)                                                                 \
   return ttc::launch_fwd<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,        \
@@ -105,6 +106,7 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
     return fail(TTC_ERR_INVALID, "Q_f is required when M is NULL (sweep recompute)");
   if (M != nullptr && lam0 == nullptr)
     return fail(TTC_ERR_INVALID, "lam0 is required together with M");
+  if (misaligned16(M) || misaligned16(d_u)) return fail(TTC_ERR_INVALID, "M and d_u must be 16-byte aligned");
   void* g[9] = {grad_A, grad_B, grad_Q, grad_R_inv, grad_Q_f, grad_lgA, grad_lgB, grad_lgQ, grad_h0};
   for (void* p : g)
     if (!p) return fail(TTC_ERR_INVALID, "null gradient pointer");
@@ -156,6 +158,8 @@ int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void
   if (!A_diag || !B || !Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A || !log_gamma_B ||
       !log_gamma_Q || !h0 || !u || !status)
     return fail(TTC_ERR_INVALID, "null pointer argument");
+  if (misaligned16(Q_basis) || misaligned16(M))
+    return fail(TTC_ERR_INVALID, "Q_basis and M must be 16-byte aligned");
   ttc::QMix mix;
   mix.basis = Q_basis;
   mix.rank = rQ;
@@ -190,6 +194,7 @@ int ttc_lqr_bwd_mix(const void* A_diag, const void* B, const void* Q, const void
   if (!A_diag || !B || !Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A || !log_gamma_B ||
       !log_gamma_Q || !h0 || !d_u || !status || !lam0 || !M || !grad_basis_partial)
     return fail(TTC_ERR_INVALID, "null pointer argument (the mixed-Q_f backward needs lam0 and M)");
+  if (misaligned16(M) || misaligned16(d_u)) return fail(TTC_ERR_INVALID, "M and d_u must be 16-byte aligned");
   void* g[9] = {grad_A, grad_B, grad_Q, grad_R_inv, nullptr, grad_lgA, grad_lgB, grad_lgQ, grad_h0};
   for (int i = 0; i < 9; ++i)
     if (i != 4 && !g[i]) return fail(TTC_ERR_INVALID, "null gradient pointer");
@@ -229,8 +234,8 @@ int ttc_lqr_fwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_b
   if (!A_diag || !coeff_B || !B_basis || !coeff_Q || !R_inv || !coeff_Qf || !Q_basis || !log_gamma_A ||
       !log_gamma_B || !log_gamma_Q || !h0 || !u || !status)
     return fail(TTC_ERR_INVALID, "null pointer argument");
-  if (misaligned16(B_basis) || misaligned16(Q_basis))
-    return fail(TTC_ERR_INVALID, "B_basis and Q_basis must be 16-byte aligned");
+  if (misaligned16(B_basis) || misaligned16(Q_basis) || misaligned16(M))
+    return fail(TTC_ERR_INVALID, "B_basis, Q_basis and M must be 16-byte aligned");
   ttc::QMix mix;
   mix.basis = Q_basis;
   mix.rank = rQ;
@@ -263,8 +268,8 @@ int ttc_lqr_bwd_lowrank(const void* A_diag, const void* coeff_B, const void* B_b
       !grad_B_basis_partial)
     return fail(TTC_ERR_INVALID, "null pointer argument (the low-rank backward needs lam0 and M)");
   if (misaligned16(B_basis) || misaligned16(Q_basis) || misaligned16(grad_basis_partial) ||
-      misaligned16(grad_B_basis_partial))
-    return fail(TTC_ERR_INVALID, "the bases and the partial buffers must be 16-byte aligned");
+      misaligned16(grad_B_basis_partial) || misaligned16(M) || misaligned16(d_u))
+    return fail(TTC_ERR_INVALID, "the bases, the partial buffers, M and d_u must be 16-byte aligned");
   void* g[9] = {grad_A, nullptr, nullptr, grad_R_inv, nullptr, grad_lgA, grad_lgB, grad_lgQ, grad_h0};
   for (int i = 0; i < 9; ++i)
     if ((i == 0 || i == 3 || i > 4) && !g[i]) return fail(TTC_ERR_INVALID, "null gradient pointer");

@@ -111,12 +111,18 @@ def check_bwd_status(st: int) -> None:
         raise RuntimeError(BWD_UNSTABLE_MSG)
 
 
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """t itself, or a copy when its data does not start on a 16-byte boundary (the kernels
+    read M, d_u and the bases with 16-byte loads)."""
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def _prepare(tensors, dtype):
     out = []
     for t in tensors:
         if not t.is_cuda:
             raise ValueError("ttc_b200 'cuda' solver needs CUDA tensors (there is no CPU path)")
-        out.append(t.detach().to(dtype).contiguous())
+        out.append(_aligned(t.detach().to(dtype).contiguous()))
     return out
 
 
@@ -165,7 +171,7 @@ class LQRSolveFunction(torch.autograd.Function):
         N, nh, d, du, T = ctx.dims
         dtype = ctx.dtype
         dev = Q.device
-        d_u = d_u.to(dtype).contiguous()
+        d_u = _aligned(d_u.to(dtype).contiguous())
         grads = [torch.empty_like(t) for t in (A, B, Q, R)]
         grads.append(torch.empty(N, nh, d, d, device=dev, dtype=dtype))
         grads += [torch.empty_like(t) for t in (lA, lB, lQ, h0)]
@@ -239,7 +245,7 @@ class LQRSolveMixFunction(torch.autograd.Function):
         dtype = ctx.dtype
         dev = Q.device
         lib = _lib.load()
-        d_u = d_u.to(dtype).contiguous()
+        d_u = _aligned(d_u.to(dtype).contiguous())
         with torch.cuda.device(dev):
             slices = int(lib.ttc_lqr_bwd_mix_slices(N, nh, d, du, rQ, _DTYPES[dtype]))
         if slices <= 0:
@@ -327,7 +333,7 @@ class LQRSolveLowRankFunction(torch.autograd.Function):
         dtype = ctx.dtype
         dev = A.device
         lib = _lib.load()
-        d_u = d_u.to(dtype).contiguous()
+        d_u = _aligned(d_u.to(dtype).contiguous())
         with torch.cuda.device(dev):
             slices = int(lib.ttc_lqr_bwd_mix_slices(N, nh, d, du, rQ, _DTYPES[dtype]))
         if slices <= 0:
