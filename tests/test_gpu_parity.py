@@ -67,6 +67,7 @@ def test_solver_matches_reference_golden(case, save_budget):
 
 @pytest.mark.parametrize("d,nh,N,T", [(16, 16, 24, 64), (16, 3, 7, 33), (16, 20, 5, 16),
                                       (32, 32, 6, 128), (32, 5, 9, 40), (32, 1, 3, 7),
+                                      (32, 64, 2, 9), (32, 28, 3, 1), (32, 30, 5, 2),
                                       (64, 3, 2, 24), (64, 1, 3, 5)])
 def test_solver_matches_oracle_seeded(d, nh, N, T):
     """Seeded synthetic problems, head counts that leave CTA groups idle, odd sizes."""
