@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define TTC_ABI_VERSION 6
+#define TTC_ABI_VERSION 7
 
 #define TTC_DTYPE_F32 0
 #define TTC_DTYPE_BF16 1
@@ -112,18 +112,22 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
                 void* stream);
 
 /*
- * Closed-loop trajectory of a solved problem, with an optional affine action cost on step 0.
+ * Closed-loop trajectory of a solved problem, with an optional affine action cost.
  * Replaces solve_traj_actions(..., r_traj, return_traj=True) and solve_traj_states
- * (ttc/solvers/lin_solver_lqr.py:13-110,113-212) for r_traj zero after step 0 -- the form
- * the reference's kkt backward solves (ttc/solvers/torch_lqr.py:41-47) and the affine term
- * of its symplectic sweep (IS_AFFINE, y3 = Y3 r; ttc/solvers/symplectic_iter.py:211-238,
- * 336-345) -- integrated forward in time as the primal half of its adjoint
- * (symplectic_iter.py:766-845).
+ * (ttc/solvers/lin_solver_lqr.py:13-110,113-212), integrated forward in time as the primal
+ * half of the reference's adjoint (symplectic_iter.py:766-845).
  *
  * Inputs: the forward's nine inputs (activation dtype; Q_f is read only for the cost and
- *   may be NULL without it), the forward's lam0 and M (float32), and r0 [N,nh,du]
- *   (activation dtype; NULL = no affine term, M may then be NULL).
- *   lambda0 = lam0 + M r0; u_0 gets the extra -R_inv r0.
+ *   may be NULL without it), the forward's lam0 (float32), and the affine term r0
+ *   (activation dtype; NULL = none) with r_steps:
+ *   r_steps = 1: r0 [N,nh,du] on step 0 only -- the form the reference's kkt backward solves
+ *     (ttc/solvers/torch_lqr.py:41-47) and the affine term of its symplectic sweep
+ *     (IS_AFFINE, y3 = Y3 r; symplectic_iter.py:211-238,336-345).  lam0 and M from
+ *     ttc_lqr_fwd; lambda0 = lam0 + M r0 and u_0 gets the extra -R_inv r0 (M may be NULL
+ *     without r0).
+ *   r_steps = T: r0 [N,nh,T,du], a cost r_t^T u_t on every step t (the reference's r_traj,
+ *     lin_solver_lqr.py:143-145).  lam0 from ttc_lqr_fwd_affine on the same r0, M must be
+ *     NULL; u_t gets the extra -R_inv r_t on every step.
  * Outputs: u_traj [N,nh,T,du] (activation dtype; u_t, t = 0..T-1); float32, each may be
  *   NULL: h_traj [N,nh,T,d] (h_{t+1}), lam_traj [N,nh,T,d] (lambda_{t+1}, the costates of
  *   solve_traj_states), lam0_out [N,nh,d] (lambda0), cost [N,nh] (the total cost
@@ -133,9 +137,24 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
 int ttc_lqr_rollout(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                     const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
                     const void* log_gamma_Q, const void* h0, const float* lam0, const float* M,
-                    const void* r0, int64_t N, int nh, int d, int du, int T, int dtype,
+                    const void* r0, int r_steps, int64_t N, int nh, int d, int du, int T, int dtype,
                     void* u_traj, float* h_traj, float* lam_traj, float* lam0_out, float* cost,
                     int* status, void* stream);
+
+/*
+ * The forward of a problem with an affine action cost on every step, r_traj [N,nh,T,du]
+ * (activation dtype; the reference's solve_traj_actions(..., r_traj),
+ * ttc/solvers/lin_solver_lqr.py:113-212).  The sweep carries one more value per state row,
+ * the offset c of Y1 lambda = Y2 h + c, and lambda0 solves Y1 lambda0 = Y2 h0 + c; with
+ * r_traj zero after step 0 this is the IS_AFFINE y3 = Y3 r0 of symplectic_iter.py:211-243.
+ * Outputs: u [N,nh,du] = u_0 (activation dtype, with the -R_inv r_0 term), lam0 [N,nh,d]
+ * (float32, for ttc_lqr_rollout with r_steps = T).  No M.  Flags and status as ttc_lqr_fwd.
+ */
+int ttc_lqr_fwd_affine(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                       const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
+                       const void* log_gamma_Q, const void* h0, const void* r_traj, int64_t N, int nh,
+                       int d, int du, int T, int dtype, int flags, void* u, float* lam0, int* status,
+                       void* stream);
 
 /* ttc_lqr_fwd with Q_f given as the layer's rank-rQ mixture (ttc_layer.py:119-123,
  * Q_f[n,h] = sum_r coeff_Qf[n,h,r] Q_basis[r]) instead of the [N,nh,d,d] tensor:

@@ -255,7 +255,7 @@ def kkt_solve(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h
 # Fused (symplectic) solver restatement
 # ---------------------------------------------------------------------------
 def fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
-                  normalize_threshold: float = 1e3, inv_guard: bool = False):
+                  normalize_threshold: float = 1e3, inv_guard: bool = False, r_traj=None):
     """Symplectic Riccati sweep + LU solve + first-step decode (fused_lqr.py:18-146).
 
     Y1 = I, Y2 = Q_f (fused_lqr.py:50-52); for s = 0..T-1 with tau = T-s (A/B
@@ -271,6 +271,13 @@ def fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_
     P = Y1^-1 Y2 (LU, :104-105); lambda0 = P h0; lambda1 = lambda0 / (1 + A_diag e^lgA);
     u = -R_inv * (B diag(e^lgB))^T lambda1 (symplectic_iter.py:437,472-517).
     Returns u, lam0, Y1, Y2, Y3, P (all in the working dtype).
+
+    r_traj [N,nh,T,du]: an affine action cost r_t^T u_t on every step (the restatement of the
+    CUDA path's per-step affine forward, not a reference kernel).  Row i of the sweep is the
+    constraint Y1_i . lambda = Y2_i . h + c_i; each step adds c -= Y2BR r_{T-1-s} (Y2BR of
+    the step, before Y2's update) and the normalisation divides c with its rows.  Then
+    lambda0 = Y1^-1 (Y2 h0 + c) and u gets -R_inv r_0; with r_traj zero after step 0,
+    c = Y3 r_0, the IS_AFFINE y3 (symplectic_iter.py:211-243).
     """
     N, nh, d = A_diag.shape
     dt = Q_f.dtype
@@ -279,11 +286,14 @@ def fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_
     Bh = B[:, None]
     Qh = Q[:, None]
     Y3 = None
+    c = None if r_traj is None else torch.zeros(N, nh, d, dtype=dt)
     for s in range(T):
         tau = float(T - s)
         tq = float(T - 1 - s)
         Bt = Bh * torch.exp(log_gamma_B * tau)[:, :, None, :]
         Y2BR = (Y2 @ Bt) * R_inv[:, :, None, :]
+        if c is not None:
+            c = c - (Y2BR @ r_traj[:, :, T - 1 - s, :, None])[..., 0]
         Y1 = Y1 + Y2BR @ Bt.transpose(-1, -2)
         At = 1.0 + A_diag * torch.exp(log_gamma_A * tau)[..., None]
         Y1 = Y1 / At[:, :, None, :]
@@ -298,15 +308,21 @@ def fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_
         sc = torch.where(m > normalize_threshold, m, torch.ones_like(m))[..., None, None]
         Y1 = Y1 / sc
         Y2 = Y2 / sc
+        if c is not None:
+            c = c / sc[..., 0]
         if s == T - 1:
             Y3 = Y3 / sc
     if inv_guard:
         Y1 = Y1 + 1e-6 * torch.eye(d, dtype=dt)
     P = torch.linalg.solve(Y1, Y2)
     lam0 = (P @ h0[..., None])[..., 0]
+    if c is not None:
+        lam0 = torch.linalg.solve(Y1, (Y2 @ h0[..., None])[..., 0] + c)
     lam1 = lam0 / (1.0 + A_diag * torch.exp(log_gamma_A)[..., None])
     B1 = Bh * torch.exp(log_gamma_B)[:, :, None, :]
     u = -R_inv * (B1.transpose(-1, -2) @ lam1[..., None])[..., 0]
+    if c is not None:
+        u = u - R_inv * r_traj[:, :, 0]
     return u, lam0, Y1, Y2, Y3, P
 
 
@@ -437,7 +453,7 @@ def riccati_trajectory(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_g
 
 
 def fused_trajectory(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gamma_Q, h0, T,
-                     r0=None, inv_guard: bool = False):
+                     r0=None, inv_guard: bool = False, r_traj=None):
     """The trajectory as the CUDA path computes it: the symplectic forward (fused_forward)
     gives lambda0 = P h0 and M = Y1^-1 Y3; an affine action cost r0 [N,nh,du] on step 0 adds
     M r0 to lambda0 (Y1^-1 y3 with the y3 = Y3 r of the reference's IS_AFFINE sweep,
@@ -445,11 +461,13 @@ def fused_trajectory(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gam
     forward in time as in the primal half of the reference's adjoint
     (symplectic_iter.py:766-845; the same recursion as fused_backward):
         k > 0: lam -= Q_k h;  lam /= A_{k+1};  u_k = -R_inv B_{k+1}^T lam;  h = A_{k+1} h + B_{k+1} u_k
+    r_traj [N,nh,T,du] (instead of r0): an affine cost on every step; lambda0 from
+    fused_forward(r_traj=...) and u_k -= R_inv r_k on every step.
     Returns (u_traj, states, costates, lambda0, cost) as riccati_trajectory."""
     N, nh, d = A_diag.shape
     du = B.shape[-1]
     _, lam, Y1, _, Y3, _ = fused_forward(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,
-                                         log_gamma_Q, h0, T, inv_guard=inv_guard)
+                                         log_gamma_Q, h0, T, inv_guard=inv_guard, r_traj=r_traj)
     if r0 is not None:
         lam = lam + torch.linalg.solve(Y1, Y3 @ r0[..., None])[..., 0]
     lam0 = lam
@@ -467,9 +485,12 @@ def fused_trajectory(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B, log_gam
         lam = lam / At
         Bt = Bh * torch.exp(log_gamma_B * float(k + 1))[:, :, None, :]
         u = -R_inv * (Bt.transpose(-1, -2) @ lam[..., None])[..., 0]
-        if k == 0 and r0 is not None:
-            u = u - R_inv * r0
-            cost = cost + (r0 * u).sum(-1)
+        rk = r0 if k == 0 else None
+        if r_traj is not None:
+            rk = r_traj[:, :, k]
+        if rk is not None:
+            u = u - R_inv * rk
+            cost = cost + (rk * u).sum(-1)
         cost = cost + 0.5 * (u * u / R_inv).sum(-1)
         h = h * At + (Bt @ u[..., None])[..., 0]
         us.append(u)

@@ -119,8 +119,8 @@ def test_rollout_rejects_bad_arguments_without_gpu(lib):
     from ttc_b200 import _lib
     P = 16  # never dereferenced: rejected before any launch
 
-    def roll(Qf=P, lam0=P, M=P, r0=None, u=P, cost=None, N=1, nh=1, d=16, du=16, T=4, dtype=0):
-        return lib.ttc_lqr_rollout(P, P, P, P, Qf, P, P, P, P, lam0, M, r0, N, nh, d, du, T, dtype,
+    def roll(Qf=P, lam0=P, M=P, r0=None, u=P, cost=None, N=1, nh=1, d=16, du=16, T=4, dtype=0, r_steps=1):
+        return lib.ttc_lqr_rollout(P, P, P, P, Qf, P, P, P, P, lam0, M, r0, r_steps, N, nh, d, du, T, dtype,
                                    u, None, None, None, cost, P, None)
 
     assert roll(N=-1) == _lib.ERR_INVALID
@@ -133,3 +133,24 @@ def test_rollout_rejects_bad_arguments_without_gpu(lib):
     assert roll(cost=P, Qf=None) == _lib.ERR_INVALID       # cost needs Q_f
     assert roll(N=1 << 20, nh=64, T=64) == _lib.ERR_INVALID  # N * nh * T >= 2^31
     assert roll(N=0) == _lib.OK
+    assert roll(r_steps=2) == _lib.ERR_INVALID             # r_steps is 1 or T
+    assert roll(r0=P, r_steps=4) == _lib.ERR_INVALID       # every-step affine term: no M
+    assert b"ttc_lqr_fwd_affine" in lib.ttc_last_error()
+
+
+def test_affine_forward_rejects_bad_arguments_without_gpu(lib):
+    from ttc_b200 import _lib
+    P = 16
+
+    def fwd(r=P, lam0=P, N=1, nh=1, d=16, du=16, T=4, dtype=0, flags=0):
+        return lib.ttc_lqr_fwd_affine(P, P, P, P, P, P, P, P, P, r, N, nh, d, du, T, dtype, flags, P, lam0, P,
+                                      None)
+
+    assert fwd(N=-1) == _lib.ERR_INVALID
+    assert fwd(T=0) == _lib.ERR_INVALID
+    assert fwd(d=16, du=32) == _lib.ERR_UNSUPPORTED
+    assert fwd(r=None) == _lib.ERR_INVALID
+    assert fwd(lam0=None) == _lib.ERR_INVALID
+    assert fwd(flags=8) == _lib.ERR_INVALID
+    assert fwd(N=1 << 20, nh=64, T=64) == _lib.ERR_INVALID
+    assert fwd(N=0) == _lib.OK

@@ -1,8 +1,8 @@
-"""GPU parity of the trajectory path (ttc_lqr_fwd + ttc_lqr_rollout through
-``ttc_b200.lqr_trajectory``): closed-loop actions, states, costates, lambda0 and total cost
-against the golden vectors of the reference's solve_traj_actions(return_traj=True) and
-solve_traj_states (lin_solver_lqr.py:13-212), with and without the affine step-0 cost, and
-against the oracle's restatement at layer-like sizes."""
+"""GPU parity of the trajectory path (ttc_lqr_fwd or ttc_lqr_fwd_affine + ttc_lqr_rollout
+through ``ttc_b200.lqr_trajectory``): closed-loop actions, states, costates, lambda0 and total
+cost against the golden vectors of the reference's solve_traj_actions(return_traj=True) and
+solve_traj_states (lin_solver_lqr.py:13-212), without an affine cost, with one on step 0 and
+with one on every step, and against the oracle's restatement at layer-like sizes."""
 import pytest
 import torch
 
@@ -21,13 +21,14 @@ def _cuda(args, dtype=torch.float32):
 
 
 @pytest.mark.parametrize("case", TRAJ_CASES)
-@pytest.mark.parametrize("tag", ["", "_r0"])
+@pytest.mark.parametrize("tag", ["", "_r0", "_rfull"])
 def test_trajectory_matches_reference_golden(case, tag):
     from ttc_b200 import lqr_trajectory
     z = load(case)
     T = int(z["T"])
-    r0 = torch.from_numpy(z["r0"]).cuda() if tag else None
-    got = lqr_trajectory(*_cuda(solver_args(z)), T, r0=r0, **ALL)
+    r0 = torch.from_numpy(z["r0"]).cuda() if tag == "_r0" else None
+    r_traj = torch.from_numpy(z["r_full"]).cuda() if tag == "_rfull" else None
+    got = lqr_trajectory(*_cuda(solver_args(z)), T, r0=r0, r_traj=r_traj, **ALL)
     for name, g in zip(OUTS, got):
         ref = torch.from_numpy(z[name + tag])
         assert O.max_rel(g.cpu().double(), ref.double()) < 1e-4, name
@@ -56,6 +57,36 @@ def test_trajectory_matches_oracle(d, du, nh, N, T):
     got = lqr_trajectory(*_cuda(host), T, r0=r0.cuda(), **ALL)
     for name, a, b in zip(OUTS, got, ref):
         assert O.max_rel(a.cpu().double(), b) < 1e-4, name
+
+
+@pytest.mark.parametrize("d,du,nh,N,T", [(16, 16, 16, 40, 64), (32, 32, 32, 5, 128),
+                                        (64, 32, 4, 3, 40), (32, 16, 8, 7, 33), (16, 16, 3, 4, 1)])
+def test_trajectory_with_cost_on_every_step_matches_oracle(d, du, nh, N, T):
+    """The per-step affine forward and rollout against the oracle's fp64 restatement (itself
+    pinned to the reference's r_traj trajectories), at layer-like sizes."""
+    from ttc_b200 import lqr_trajectory
+    host = [torch.from_numpy(a) for a in solver_inputs_synthetic(N, nh, d, du, seed=70 + d + du)]
+    g = torch.Generator().manual_seed(d * du + T)
+    r = torch.randn(N, nh, T, du, generator=g, dtype=torch.float64)
+    ref = O.fused_trajectory(*host, T, r_traj=r)
+    got = lqr_trajectory(*_cuda(host), T, r_traj=r.cuda(), **ALL)
+    for name, a, b in zip(OUTS, got, ref):
+        assert O.max_rel(a.cpu().double(), b) < 1e-4, name
+
+
+def test_cost_on_step_zero_only_agrees_with_the_r0_form():
+    """r_traj zero after step 0 through ttc_lqr_fwd_affine equals r0 through M: two forwards."""
+    from ttc_b200 import lqr_trajectory
+    host = [torch.from_numpy(a) for a in solver_inputs_synthetic(9, 8, 32, 32, seed=81)]
+    args = _cuda(host)
+    T = 48
+    r0 = torch.randn(9, 8, 32, device="cuda")
+    r = torch.zeros(9, 8, T, 32, device="cuda")
+    r[:, :, 0] = r0
+    a = lqr_trajectory(*args, T, r0=r0, **ALL)
+    b = lqr_trajectory(*args, T, r_traj=r, **ALL)
+    for name, x, y in zip(OUTS, a, b):
+        assert O.max_rel(y.cpu().double(), x.cpu().double()) < 1e-5, name
 
 
 def test_row_chunks_give_the_same_trajectory():
@@ -103,8 +134,13 @@ def test_trajectory_errors():
     from ttc_b200 import lqr_trajectory
     host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(2, 2, 16, 16, seed=63)]
     args = _cuda(host)
-    with pytest.raises(NotImplementedError):
-        lqr_trajectory(*args, 8, r0=torch.zeros(2, 2, 8, 16, device="cuda"))
+    with pytest.raises(AssertionError, match="r_traj"):
+        lqr_trajectory(*args, 8, r0=torch.zeros(2, 2, 8, 16, device="cuda"))  # every step: r_traj
+    with pytest.raises(AssertionError, match="r_traj must be"):
+        lqr_trajectory(*args, 8, r_traj=torch.zeros(2, 2, 7, 16, device="cuda"))
+    with pytest.raises(ValueError, match="not both"):
+        lqr_trajectory(*args, 8, r0=torch.zeros(2, 2, 16, device="cuda"),
+                       r_traj=torch.zeros(2, 2, 8, 16, device="cuda"))
     with pytest.raises(ValueError):
         lqr_trajectory(*host, 8)  # CPU tensors: there is no CPU path
     bad = list(args)

@@ -89,15 +89,22 @@ def test_registry_has_gpu_kkt():
 
 
 def test_trajectory_host_checks():
-    """lqr_trajectory validates before any launch: an affine cost on every step is not
-    supported, a wrong r0 shape is an error, and CPU tensors have no path."""
+    """lqr_trajectory validates before any launch: a per-step cost passed as r0 points to
+    r_traj, wrong r0 / r_traj shapes and both at once are errors, and CPU tensors have no
+    path."""
     from ttc_b200 import kkt_lqr_solve, lqr_trajectory
     from ttc_cases import solver_inputs_synthetic
     host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(2, 2, 16, 16, seed=1)]
-    with pytest.raises(NotImplementedError, match="every step"):
+    with pytest.raises(AssertionError, match="every step goes in r_traj"):
         lqr_trajectory(*host, 4, r0=torch.zeros(2, 2, 4, 16))
     with pytest.raises(AssertionError, match="r0 must be"):
         lqr_trajectory(*host, 4, r0=torch.zeros(2, 16))
+    with pytest.raises(AssertionError, match="r_traj must be"):
+        lqr_trajectory(*host, 4, r_traj=torch.zeros(2, 2, 5, 16))
+    with pytest.raises(ValueError, match="not both"):
+        lqr_trajectory(*host, 4, r0=torch.zeros(2, 2, 16), r_traj=torch.zeros(2, 2, 4, 16))
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        lqr_trajectory(*host, 4, r_traj=torch.zeros(2, 2, 4, 16))
     with pytest.raises(ValueError, match="CUDA tensors"):
         lqr_trajectory(*host, 4)
     with pytest.raises(ValueError, match="CUDA tensors"):

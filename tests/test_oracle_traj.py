@@ -47,6 +47,34 @@ def test_fused_trajectory_matches_reference(case, tag, dtype):
         assert O.max_rel(g.double(), ref) < 1e-4, name
 
 
+@pytest.mark.parametrize("case", TRAJ_CASES)
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+def test_fused_trajectory_with_cost_on_every_step_matches_reference(case, dtype):
+    """The per-step affine sweep (the offset c of each row, lambda0 = Y1^-1 (Y2 h0 + c)) and
+    the rollout with -R_inv r_k on every step reproduce the reference's Riccati trajectories
+    with r_traj on every step."""
+    z = load(case)
+    T = int(z["T"])
+    r = torch.from_numpy(z["r_full"]).to(dtype)
+    got = O.fused_trajectory(*solver_args(z, dtype), T, r_traj=r)
+    for name, g, ref in zip(OUTS, got, _golden(z, "_rfull")):
+        assert O.max_rel(g.double(), ref) < 1e-4, name
+
+
+def test_fused_forward_per_step_affine_reduces_to_step0_form():
+    """With r_traj zero after step 0 the per-step offset c is Y3 r0 (IS_AFFINE)."""
+    z = load("traj_bench_d16")
+    args = solver_args(z, torch.float64)
+    T = int(z["T"])
+    r0 = torch.from_numpy(z["r0"]).double()
+    r = torch.zeros(*r0.shape[:2], T, r0.shape[-1], dtype=torch.float64)
+    r[:, :, 0] = r0
+    u_a, lam_a = O.fused_forward(*args, T, r_traj=r)[:2]
+    _, lam, Y1, _, Y3, _ = O.fused_forward(*args, T)
+    lam_b = lam + torch.linalg.solve(Y1, Y3 @ r0[..., None])[..., 0]
+    assert O.max_rel(lam_a, lam_b) < 1e-10
+
+
 def test_fused_trajectory_first_action_is_the_solve():
     """u_traj[..., 0, :] is the solver output u of the same inputs."""
     z = load("traj_bench_d16")

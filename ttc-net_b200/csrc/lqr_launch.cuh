@@ -84,12 +84,21 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
 template <int D, int DU, typename TIn>
 int64_t bwd_mix_slices(int64_t N, int nh, int rQ);
 
-// Closed-loop trajectory from the forward's lambda0 (and M r0 for an affine step-0 cost).
+// Forward with an affine action cost on every step (r_traj [N, nh, T, du]): lambda0 of the
+// affine problem and u_0, no M.
+template <int D, int DU, typename TIn>
+int launch_fwd_affine(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+                      const void* lA, const void* lB, const void* lQ, const void* h0, const void* r_traj,
+                      int64_t N, int nh, int T, void* u, float* lam0, int* status, int opts, cudaStream_t st);
+
+// Closed-loop trajectory from the forward's lambda0: r_steps = 1, an affine cost r0 on step 0
+// (lambda0 += M r0); r_steps = T, one on every step (r [N, nh, T, du], lambda0 from
+// launch_fwd_affine, no M).
 template <int D, int DU, typename TIn>
 int launch_rollout(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                    const void* lA, const void* lB, const void* lQ, const void* h0,
-                   const float* lam0, const float* M, const void* r0, int64_t N, int nh, int T,
-                   void* u, float* hs, float* lams, float* lam0_out, float* cost, int* status,
+                   const float* lam0, const float* M, const void* r0, int r_steps, int64_t N, int nh,
+                   int T, void* u, float* hs, float* lams, float* lam0_out, float* cost, int* status,
                    cudaStream_t st);
 
 #ifdef TTC_DEFINE_LAUNCHERS
@@ -126,11 +135,11 @@ int set_smem(Kern k, size_t bytes) {
                     "cudaFuncSetAttribute");
 }
 
-template <int D, int DU, typename TIn, bool SAVE_M>
+template <int D, int DU, typename TIn, bool SAVE_M, bool AFF = false>
 int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                   const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N,
                   int nh, int T, void* u, float* lam0, float* M, int* status, const QMix& mix,
-                  int opts, cudaStream_t st) {
+                  int opts, cudaStream_t st, const void* r_traj = nullptr) {
   using CF = TcCfg<D, DU>;
   using L = TcFwdLayout<D, DU, SAVE_M>;
   int slots = tc_slots<D, DU, SAVE_M>(nh);
@@ -140,13 +149,21 @@ int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, co
     return set_error(TTC_ERR_UNSUPPORTED, "the Q_f basis does not fit in shared memory");
   const uint32_t cols = tmem_cols_for(slots * CF::kSlotCols);
   const size_t smem = L::bytes(slots) + extra;
-  auto k = ttc::lqr_fwd_tc_kernel<D, DU, TIn, SAVE_M>;
+  auto k = ttc::lqr_fwd_tc_kernel<D, DU, TIn, SAVE_M, AFF>;
   if (int rc = set_smem(k, smem)) return rc;
   k<<<dim3((unsigned)N), dim3(slots * 128), smem, st>>>(
       (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf,
       (const TIn*)mix.basis, mix.rank, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0,
-      nh, T, opts, cols, (TIn*)u, lam0, M, status, mix.lowrank<TIn>());
+      nh, T, opts, cols, (TIn*)u, lam0, M, status, mix.lowrank<TIn>(), (const TIn*)r_traj);
   return cuda_check(cudaGetLastError(), "lqr_fwd_tc_kernel launch");
+}
+
+template <int D, int DU, typename TIn>
+int launch_fwd_affine(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
+                      const void* lA, const void* lB, const void* lQ, const void* h0, const void* r_traj,
+                      int64_t N, int nh, int T, void* u, float* lam0, int* status, int opts, cudaStream_t st) {
+  return launch_fwd_tc<D, DU, TIn, false, true>(A, B, Q, R, Qf, lA, lB, lQ, h0, N, nh, T, u, lam0, nullptr,
+                                                status, QMix{}, opts, st, r_traj);
 }
 
 template <int D, int DU, typename TIn>
@@ -276,8 +293,8 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
 template <int D, int DU, typename TIn>
 int launch_rollout(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                    const void* lA, const void* lB, const void* lQ, const void* h0,
-                   const float* lam0, const float* M, const void* r0, int64_t N, int nh, int T,
-                   void* u, float* hs, float* lams, float* lam0_out, float* cost, int* status,
+                   const float* lam0, const float* M, const void* r0, int r_steps, int64_t N, int nh,
+                   int T, void* u, float* hs, float* lams, float* lam0_out, float* cost, int* status,
                    cudaStream_t st) {
 #ifndef TTC_ROLL_MMA
 #define TTC_ROLL_MMA 1
@@ -287,7 +304,8 @@ int launch_rollout(const void* A, const void* B, const void* Q, const void* R, c
     // (d = 32, 32 heads) the CUDA-core rollout; with fewer than 16 heads at d = 16 half of
     // each warp's MMA rows would idle and the CUDA-core kernel is faster.
     using C = RollMma<D>;
-    if (C::fits(nh) && (D > 16 || nh >= 16)) {
+    // (an affine cost on every step runs on the CUDA-core rollout)
+    if (r_steps == 1 && C::fits(nh) && (D > 16 || nh >= 16)) {
       const int rpc = C::rows_per_cta(nh);
       const size_t smem = C::bytes(nh);
       auto k = ttc::lqr_rollout_mma_kernel<D, TIn>;
@@ -309,7 +327,7 @@ int launch_rollout(const void* A, const void* B, const void* Q, const void* R, c
   if (int rc = set_smem(k, smem)) return rc;
   k<<<dim3((unsigned)N), dim3(G * D), smem, st>>>(
       (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)lA, (const TIn*)lB,
-      (const TIn*)lQ, (const TIn*)h0, (const TIn*)Qf, lam0, M, (const TIn*)r0, nh, T, (TIn*)u,
+      (const TIn*)lQ, (const TIn*)h0, (const TIn*)Qf, lam0, M, (const TIn*)r0, r_steps, nh, T, (TIn*)u,
       hs, lams, lam0_out, cost, status);
   return cuda_check(cudaGetLastError(), "lqr_rollout_kernel launch");
 }
@@ -332,6 +350,11 @@ int launch_rollout(const void* A, const void* B, const void* Q, const void* R, c
   template int ttc::launch_rollout<D, DU, TIn>(const void*, const void*, const void*,         \
                                                const void*, const void*, const void*,         \
                                                const void*, const void*, const void*,         \
-                                               const float*, const float*, const void*,       \
+                                               const float*, const float*, const void*, int,  \
                                                int64_t, int, int, void*, float*, float*,      \
-                                               float*, float*, int*, cudaStream_t);
+                                               float*, float*, int*, cudaStream_t);           \
+  template int ttc::launch_fwd_affine<D, DU, TIn>(const void*, const void*, const void*,      \
+                                                  const void*, const void*, const void*,      \
+                                                  const void*, const void*, const void*,      \
+                                                  const void*, int64_t, int, int, void*, float*, \
+                                                  int*, int, cudaStream_t);

@@ -11,7 +11,9 @@
 //     h   = A_{k+1} h + B_{k+1} u_k
 // which gives the actions of solve_traj_actions(..., r_traj, return_traj=True) and the
 // states / costates / total cost of solve_traj_states (lin_solver_lqr.py:13-110,187-203)
-// with r_traj zero after step 0.  Per head and step it writes u_k [du] (activation dtype)
+// with r_traj zero after step 0.  With an affine cost on every step (r_steps = T, the
+// CUDA-core kernel) lambda0 comes from the per-step affine forward, which already holds every
+// r_t's offset, and u_k -= R_inv r_k on every step.  Per head and step it writes u_k [du] (activation dtype)
 // and, optionally, h_{k+1} [d] and lambda_{k+1} [d] (fp32, as the reference's fp32
 // buffers); per head, optionally, lambda0 and the total cost
 //     sum_k 0.5 h_{k+1}^T Q_k h_{k+1} + 0.5 u_k^T R u_k + r_k^T u_k      (Q_{T-1} = Q_f).
@@ -87,7 +89,7 @@ lqr_rollout_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                    const TIn* __restrict__ lgA, const TIn* __restrict__ lgB,
                    const TIn* __restrict__ lgQ, const TIn* __restrict__ H0,
                    const TIn* __restrict__ Qf, const float* __restrict__ lam0_in,
-                   const float* __restrict__ M_in, const TIn* __restrict__ R0, int nh, int T,
+                   const float* __restrict__ M_in, const TIn* __restrict__ R0, int r_steps, int nh, int T,
                    TIn* __restrict__ u_out, float* __restrict__ h_out,
                    float* __restrict__ lam_out, float* __restrict__ lam0_out,
                    float* __restrict__ cost_out, int* __restrict__ status) {
@@ -150,7 +152,7 @@ lqr_rollout_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       if (i < DU) {
         lgB2[m] = ldf(lgB + p[m] * DU + i) * kLog2e;
         rinv[m] = ldf(Rinv + p[m] * DU + i);
-        if (R0 != nullptr) r0i[m] = ldf(R0 + p[m] * DU + i);
+        if (R0 != nullptr) r0i[m] = ldf(R0 + p[m] * r_steps * DU + i);
         sr0[m * DU + i] = r0i[m];
       }
       rrinv[m] = i < DU ? recip(rinv[m]) : 0.f;
@@ -160,7 +162,7 @@ lqr_rollout_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       dq_prev[m] = 1.0f;  // exp(lgQ_i k) at the top of step k
     }
     G.sync();  // sr0 visible to the group
-    if (R0 != nullptr) {
+    if (R0 != nullptr && M_in != nullptr) {
       // lambda0 += M r0: the affine offset Y1^-1 (Y3 r0).
 #pragma unroll
       for (int m = 0; m < H; ++m) {
@@ -213,9 +215,12 @@ lqr_rollout_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
           }
           const float eB = exp_scaled(lgB2[m], ke);
           float u = -((sum2(s0) + sum2(s1)) * eB) * rinv[m];
-          if (k == 0) u = fmaf(r0i[m], -rinv[m], u);
+          // the affine cost of step k: r0 on step 0, or row k of r [T][DU]
+          float rk = k == 0 ? r0i[m] : 0.f;
+          if (k > 0 && k < r_steps && R0 != nullptr) rk = ldf(R0 + (p[m] * r_steps + k) * DU + i);
+          u = fmaf(rk, -rinv[m], u);
           cost[m] = fmaf(0.5f * u, u * rrinv[m], cost[m]);
-          if (k == 0) cost[m] = fmaf(r0i[m], u, cost[m]);
+          cost[m] = fmaf(rk, u, cost[m]);
           cb[m * kB + 2 * D + i] = u * eB;
           bad |= nonfinite(u);
           if (valid[m]) stf(u_out + (p[m] * T + k) * DU + i, u);

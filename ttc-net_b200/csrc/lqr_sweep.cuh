@@ -18,12 +18,40 @@ struct SweepVec {
   static constexpr int kSize = 3 * D + 2 * DU;
 };
 
+// The pivot row of Gauss-Jordan step k: the largest |y| among the rows not yet used, lowest
+// index on ties; NaN counts as 0 (so every thread gets exactly one pivot column whatever the
+// data).  A whole-warp group (D = 32) reduces one 32-bit key with redux.sync: |y|'s bits with
+// the low five replaced by 31 - row (rows whose |y| agree to 2^-18 relative count as tied, so
+// the lowest index wins), plus 32 so that a candidate never ties with a used row (key 0).
+// Narrower groups reduce (|y|, row) pairs with shuffles.
+template <int D>
+__device__ __forceinline__ int pivot_row(const Group<D>& G, float y, bool done) {
+  const int i = G.i;
+  if constexpr (D == 32) {
+    const uint32_t mag = __float_as_uint(fmaxf(fabsf(y), 0.0f));
+    const uint32_t key = done ? 0u : (((mag & ~31u) + 32u) | static_cast<uint32_t>(31 - i));
+    return 31 - static_cast<int>(__reduce_max_sync(0xffffffffu, key) & 31u);
+  } else {
+    float bv = done ? -1.0f : fmaxf(fabsf(y), 0.0f);
+    int bi = i;
+#pragma unroll
+    for (int o = D / 2; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(G.mask, bv, o, D);
+      const int oi = __shfl_xor_sync(G.mask, bi, o, D);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    return bi;
+  }
+}
+
 // Gauss-Jordan with partial pivoting in registers (D <= 32, one group = D lanes of a
 // warp): thread i holds row i of Y1 in y1 and of NR right-hand sides in rhs; the pivot
 // row is broadcast by warp shuffles.  Pivot rows are never swapped: each step picks the
-// largest |entry| of the current column among the rows not yet used (lowest index on
-// ties; NaN counts as 0, so every thread gets exactly one pivot column whatever the data)
-// and eliminates that column from every other row.  On return rhs holds piv * (row pc
+// pivot row of the current column (pivot_row) and eliminates that column from every other
+// row.  On return rhs holds piv * (row pc
 // of Y1^-1 RHS); returns pc and writes piv.
 template <int D, int NR>
 __device__ __forceinline__ int gauss_jordan_regs(const Group<D>& G, float (&y1)[D], float (&rhs)[NR],
@@ -35,17 +63,7 @@ __device__ __forceinline__ int gauss_jordan_regs(const Group<D>& G, float (&y1)[
   piv = 1.0f;
 #pragma unroll
   for (int k = 0; k < D; ++k) {
-    float bv = done ? -1.0f : fmaxf(fabsf(y1[k]), 0.0f);
-    int bi = i;
-#pragma unroll
-    for (int o = D / 2; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(G.mask, bv, o, D);
-      const int oi = __shfl_xor_sync(G.mask, bi, o, D);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
+    const int bi = pivot_row<D>(G, y1[k], done);
     const float pk = __shfl_sync(G.mask, y1[k], bi, D);
     const bool me = (i == bi);
     const float f = me ? 0.0f : y1[k] * recip(pk);
@@ -81,17 +99,7 @@ __device__ __forceinline__ int gauss_jordan_smem(const Group<D>& G, float (&y1)[
   piv = 1.0f;
 #pragma unroll
   for (int k = 0; k < D; ++k) {
-    float bv = done ? -1.0f : fmaxf(fabsf(y1[k]), 0.0f);
-    int bi = i;
-#pragma unroll
-    for (int o = D / 2; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(G.mask, bv, o, D);
-      const int oi = __shfl_xor_sync(G.mask, bi, o, D);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
+    const int bi = pivot_row<D>(G, y1[k], done);
     const bool me = (i == bi);
     float4* pr = reinterpret_cast<float4*>(pbuf + (k & 1) * kRow);
     if (me) {

@@ -12,6 +12,8 @@
 // so that one slot's MMAs overlap the others' elementwise work.
 #pragma once
 
+#include <type_traits>
+
 #include "lqr_kernels.cuh"
 #include "tc_primitives.cuh"
 
@@ -220,16 +222,43 @@ __device__ __forceinline__ float renormalize_rows(const Group<D>& G, float (&y1)
 // Where the sweep's last step puts this thread's row of Y3 = -Y2BR (symplectic_iter.py:
 // 241-243): put(j, value) per column, then scale(r) if the last renormalisation divided
 // the row block by 1/r.
+// kEveryStep: put(j, -(Y2 B)_ij e^{lgB tau} R_inv_j) on every step instead (stage(t, i) having
+// published step t's vector for it), and scale(r) at every renormalisation.
 struct Y3Discard {  // the caller does not need Y3
+  static constexpr bool kEveryStep = false;
+  __device__ __forceinline__ void stage(int, int) {}
   __device__ __forceinline__ void put(int, float) {}
   __device__ __forceinline__ void scale(float) {}
 };
 template <int DU>
 struct Y3DotDu {  // contracted with the upstream gradient: acc = (Y3 d_u)_i (fused_lqr.py:185)
+  static constexpr bool kEveryStep = false;
   const float* du;
   float acc;
+  __device__ __forceinline__ void stage(int, int) {}
   __device__ __forceinline__ void put(int j, float v) { acc = fmaf(v, du[j], acc); }
   __device__ __forceinline__ void scale(float r) { acc *= r; }
+};
+// An affine action cost r_t^T u_t on every step t (r_traj of solve_traj_actions,
+// lin_solver_lqr.py:143-145).  A row i of the sweep is the constraint
+// Y1_i . lambda = Y2_i . h + c_i between the costate and the state at the current time;
+// eliminating u_t = -R_t^-1 (B_t^T lambda_{t+1} + r_t) from h_{t+1} = A_t h_t + B_t u_t
+// transforms Y1, Y2 as the sweep does and adds -(Y2 B_t R_t^-1 r_t)_i to c_i, so that at the
+// end Y1 lambda0 = Y2 h0 + c.  The step-0 term alone is the reference's IS_AFFINE y3 = Y3 r0
+// (symplectic_iter.py:211-243).  acc holds c_i; rs is the head's du floats of group shared
+// memory holding the current step's r (written one step ahead, during the step's last
+// product, after every thread of the head has read the previous one).
+template <typename TIn, int DU>
+struct Y3AffineSteps {
+  static constexpr bool kEveryStep = true;
+  const TIn* r;  // this head's r_traj [T][DU]; nullptr for a padding head
+  float* rs;
+  float acc;
+  __device__ __forceinline__ void stage(int t, int i) {
+    if (i < DU) rs[i] = r != nullptr ? ldf(r + (int64_t)t * DU + i) : 0.f;
+  }
+  __device__ __forceinline__ void put(int j, float v) { acc = fmaf(v, rs[j], acc); }
+  __device__ __forceinline__ void scale(float f) { acc *= f; }
 };
 
 // The sweep of symplectic_iter.py:226-300 for this thread's row: (Y1, Y2) from (I, Q_f),
@@ -267,6 +296,7 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
       w[V::kS2 + i] = eb * eb * rinv;
       w[V::kEBR + i] = eb * rinv;
     }
+    y3.stage(T - 1 - s, i);  // the affine cost of time step T - 1 - s (sweep step s: tau)
   };
   step_vectors(0);
   for (int s = 0; s < T; ++s) {
@@ -277,7 +307,7 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
     // run on fp32 pairs (bitwise the scalar results; 1-3 % faster).
     float t[DU];
     if (!tile_product<D, DU, D, kPairs>(X, y2, t, o1h, o1l)) return false;
-    if (last) {
+    if (Y3::kEveryStep || last) {
 #pragma unroll
       for (int j4 = 0; j4 < DU / 4; ++j4) {
         const float4 e = v4[V::kEBR / 4 + j4];
@@ -336,7 +366,12 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
       // costs 2.4 % (d = 16) to 5 % (d = 64) of the forward.  With an inverse guard (a fixed
       // ridge added to the final, scaled Y1) the scale matters: every step then, as the
       // reference.
-      if ((s & 3) == 3 || every_step) renormalize_rows<D>(G, y1, y2);
+      if ((s & 3) == 3 || every_step) {
+        const float r = renormalize_rows<D>(G, y1, y2);
+        if constexpr (Y3::kEveryStep) {
+          if (r != 1.0f) y3.scale(r);
+        }
+      }
     } else {
 #pragma unroll
       for (int k4 = 0; k4 < D / 4; ++k4) {
@@ -428,7 +463,9 @@ __device__ __forceinline__ void stage_basis(float* basis_s, const TIn* __restric
   }
 }
 
-template <int D, int DU, typename TIn, bool SAVE_M>
+// AFF: an affine action cost on every step, r_traj [N, nh, T, DU] (Y3AffineSteps): lambda0
+// solves Y1 lambda0 = Y2 h0 + c (one right-hand side), u includes -R_inv r_0, no M.
+template <int D, int DU, typename TIn, bool SAVE_M, bool AFF = false>
 __global__ void __launch_bounds__(TcLaunch<D>::kMaxThreads, TcLaunch<D>::kMinBlocks)
 lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                   const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
@@ -437,7 +474,8 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                   const TIn* __restrict__ lgB, const TIn* __restrict__ lgQ,
                   const TIn* __restrict__ H0, int nh, int T, int opts, uint32_t tmem_cols,
                   TIn* __restrict__ u_out, float* __restrict__ lam0_out, float* __restrict__ M_out,
-                  int* __restrict__ status, LowRank<TIn> lr) {
+                  int* __restrict__ status, LowRank<TIn> lr, const TIn* __restrict__ r_traj = nullptr) {
+  static_assert(!(AFF && SAVE_M), "the per-step affine forward saves no M");
   using CF = TcCfg<D, DU>;
   using L = TcFwdLayout<D, DU, SAVE_M>;
   using V = SweepVec<D, DU>;
@@ -533,7 +571,9 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
 #pragma unroll
     for (int k = 0; k < D; ++k) y1[k] = (k == i) ? 1.0f : 0.0f;
     load_qf_row<D, TIn>(y2, valid, Qf, basis_s, rQ, p, i);
-    Y3Discard y3;  // M is formed from P below instead of from Y3
+    using Y3T = std::conditional_t<AFF, Y3AffineSteps<TIn, DU>, Y3Discard>;
+    Y3T y3;  // without AFF, M is formed from P below instead of from Y3
+    if constexpr (AFF) y3 = Y3T{valid ? r_traj + p * T * DU : nullptr, sh0 + 2 * D, 0.f};
     const bool swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T,
                                               (opts & TTC_FLAG_INV_GUARD) != 0);
     // Uniform over the slot: a late timeout on the last product surfaces here too.
@@ -546,17 +586,29 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
 #pragma unroll
     for (int k = 0; k < D; ++k) bad |= unstable(y1[k]) | unstable(y2[k]);
     if (bad && valid) flags |= TTC_STATUS_FWD_UNSTABLE;
-    // P = Y1^-1 Y2 (fused_lqr.py:104-105): this thread ends up with row pc of P in y2.
-    float piv;
-    const int pc = gauss_jordan_group<D, D>(G, y1, y2, piv, pbuf);
-    bool lbad = unstable(piv);
-    const float rpiv = recip(piv);
-    float lam0 = 0.f;
+    float piv, lam0 = 0.f;
+    int pc;
+    bool lbad;
+    if constexpr (AFF) {
+      // Y1 lambda0 = Y2 h0 + c: one right-hand side
+      float rhs[1] = {y3.acc};
 #pragma unroll
-    for (int c = 0; c < D; ++c) {
-      y2[c] *= rpiv;
-      lbad |= unstable(y2[c]);
-      lam0 = fmaf(y2[c], sh0[c], lam0);  // lambda0 = P h0 (symplectic_iter.py:437)
+      for (int c = 0; c < D; ++c) rhs[0] = fmaf(y2[c], sh0[c], rhs[0]);
+      pc = gauss_jordan_group<D, 1>(G, y1, rhs, piv, pbuf);
+      lbad = unstable(piv);
+      lam0 = rhs[0] * recip(piv);
+      lbad |= unstable(lam0);
+    } else {
+      // P = Y1^-1 Y2 (fused_lqr.py:104-105): this thread ends up with row pc of P in y2.
+      pc = gauss_jordan_group<D, D>(G, y1, y2, piv, pbuf);
+      lbad = unstable(piv);
+      const float rpiv = recip(piv);
+#pragma unroll
+      for (int c = 0; c < D; ++c) {
+        y2[c] *= rpiv;
+        lbad |= unstable(y2[c]);
+        lam0 = fmaf(y2[c], sh0[c], lam0);  // lambda0 = P h0 (symplectic_iter.py:437)
+      }
     }
     if (lbad && valid) flags |= TTC_STATUS_LU_UNSTABLE;
     if (valid && lam0_out != nullptr) lam0_out[p * D + pc] = lam0;
@@ -593,7 +645,8 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         const int idx = tc::canon(k, i, D);  // B[k][i] from the hi/lo operand O2
         acc = fmaf(ops[CF::kO2 + idx] + ops[CF::kO2 + D * DU + idx], slam[k], acc);
       }
-      const float u = -(acc * exp_scaled(lgB2, 1.0f)) * rinv;
+      float u = -(acc * exp_scaled(lgB2, 1.0f)) * rinv;
+      if constexpr (AFF) u = fmaf(ldf(r_traj + p * T * DU + i), -rinv, u);  // u_0 -= R_inv r_0
       if (isnan(u)) flags |= TTC_STATUS_U_NAN;
       stf(u_out + p * DU + i, u);
     }

@@ -122,16 +122,20 @@ int ttc_lqr_bwd(const void* A_diag, const void* B, const void* Q, const void* R_
 int ttc_lqr_rollout(const void* A_diag, const void* B, const void* Q, const void* R_inv,
                     const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
                     const void* log_gamma_Q, const void* h0, const float* lam0, const float* M,
-                    const void* r0, int64_t N, int nh, int d, int du, int T, int dtype,
+                    const void* r0, int r_steps, int64_t N, int nh, int d, int du, int T, int dtype,
                     void* u_traj, float* h_traj, float* lam_traj, float* lam0_out, float* cost,
                     int* status, void* stream) {
   if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (r_steps != 1 && r_steps != T) return fail(TTC_ERR_INVALID, "r_steps must be 1 or T");
   if (N == 0) return TTC_OK;
   if (!A_diag || !B || !Q || !R_inv || !log_gamma_A || !log_gamma_B || !log_gamma_Q || !h0 ||
       !lam0 || !u_traj || !status)
     return fail(TTC_ERR_INVALID, "null pointer argument");
-  if (r0 != nullptr && M == nullptr)
-    return fail(TTC_ERR_INVALID, "an affine term r0 needs the forward's M");
+  // (T = 1: both forms coincide; without M, lam0 is taken to hold r0's offset already)
+  if (r_steps == 1 && T > 1 && r0 != nullptr && M == nullptr)
+    return fail(TTC_ERR_INVALID, "an affine term r0 on step 0 needs the forward's M");
+  if (r_steps > 1 && M != nullptr)
+    return fail(TTC_ERR_INVALID, "an affine term on every step takes lam0 from ttc_lqr_fwd_affine, not M");
   if (cost != nullptr && Q_f == nullptr)
     return fail(TTC_ERR_INVALID, "the total cost needs Q_f");
   if (N * nh * (int64_t)T > 0x7fffffffLL)
@@ -139,11 +143,33 @@ int ttc_lqr_rollout(const void* A_diag, const void* B, const void* Q, const void
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define TTC_ROLL(DD, DDU, TT)                                                                 \
   return ttc::launch_rollout<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,     \
-                                     log_gamma_Q, h0, lam0, M, r0, N, nh, T, u_traj, h_traj,      \
+                                     log_gamma_Q, h0, lam0, M, r0, r_steps, N, nh, T, u_traj, h_traj, \
                                      lam_traj, lam0_out, cost, status, st)
   if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_ROLL, float);
   TTC_FOR_DIMS(TTC_ROLL, __nv_bfloat16);
 #undef TTC_ROLL
+}
+
+int ttc_lqr_fwd_affine(const void* A_diag, const void* B, const void* Q, const void* R_inv,
+                       const void* Q_f, const void* log_gamma_A, const void* log_gamma_B,
+                       const void* log_gamma_Q, const void* h0, const void* r_traj, int64_t N, int nh,
+                       int d, int du, int T, int dtype, int flags, void* u, float* lam0, int* status,
+                       void* stream) {
+  if (int rc = check_common(N, nh, d, du, T, dtype)) return rc;
+  if (int rc = check_flags(flags)) return rc;
+  if (N == 0) return TTC_OK;
+  if (!A_diag || !B || !Q || !R_inv || !Q_f || !log_gamma_A || !log_gamma_B || !log_gamma_Q ||
+      !h0 || !r_traj || !u || !lam0 || !status)
+    return fail(TTC_ERR_INVALID, "null pointer argument");
+  if (N * nh * (int64_t)T > 0x7fffffffLL)
+    return fail(TTC_ERR_INVALID, "N * num_heads * T must be below 2^31");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define TTC_FWDA(DD, DDU, TT)                                                                  \
+  return ttc::launch_fwd_affine<DD, DDU, TT>(A_diag, B, Q, R_inv, Q_f, log_gamma_A, log_gamma_B,   \
+                                        log_gamma_Q, h0, r_traj, N, nh, T, u, lam0, status, flags, st)
+  if (dtype == TTC_DTYPE_F32) TTC_FOR_DIMS(TTC_FWDA, float);
+  TTC_FOR_DIMS(TTC_FWDA, __nv_bfloat16);
+#undef TTC_FWDA
 }
 
 int ttc_lqr_fwd_mix(const void* A_diag, const void* B, const void* Q, const void* R_inv,

@@ -13,7 +13,7 @@ import threading
 # compiled with tuning macros by `build.py --out PATH -D NAME=VALUE`).
 LIB_PATH = os.environ.get("TTC_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)),
                                                           "libttc_b200.so")
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -44,7 +44,8 @@ SIGNATURES = {
     "ttc_last_error": (ctypes.c_char_p, []),
     "ttc_lqr_fwd": (_I, [_P] * 9 + [_I64, _I, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
     "ttc_lqr_bwd": (_I, [_P] * 9 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I, _I] + [_P] * 9 + [_P, _P]),
-    "ttc_lqr_rollout": (_I, [_P] * 9 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I] + [_P] + [_FP] * 4 + [_P, _P]),
+    "ttc_lqr_rollout": (_I, [_P] * 9 + [_FP, _FP, _P, _I, _I64, _I, _I, _I, _I, _I] + [_P] + [_FP] * 4 + [_P, _P]),
+    "ttc_lqr_fwd_affine": (_I, [_P] * 10 + [_I64, _I, _I, _I, _I, _I, _I, _P, _FP, _P, _P]),
     "ttc_lqr_fwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_I64, _I, _I, _I, _I, _I, _I, _P, _FP, _FP, _P, _P]),
     "ttc_lqr_bwd_mix_slices": (_I64, [_I64, _I, _I, _I, _I, _I]),
     "ttc_lqr_bwd_mix": (_I, [_P] * 6 + [_I] + [_P] * 4 + [_FP, _FP, _P, _I64, _I, _I, _I, _I, _I]

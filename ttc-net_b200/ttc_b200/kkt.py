@@ -61,12 +61,12 @@ def _rollouts(args, T, d_u, budget):
                     _F32, 0, _ptr(u1), _ptr(lam0), _ptr(M), _ptr(status[0:1]))
             # forward problem: lambda0 = P h0
             _launch("ttc_lqr_rollout", dev, lib.ttc_lqr_rollout, *[_ptr(t) for t in ins], _ptr(lam0),
-                    None, None, n, nh, d, du, T, _F32, *[_ptr(o[a:a + n]) for o in out_f], None, None,
+                    None, None, 1, n, nh, d, du, T, _F32, *[_ptr(o[a:a + n]) for o in out_f], None, None,
                     _ptr(status[1:2]))
             # second problem: h0 = 0, lambda0 = M d_u, u_0 gets -R_inv d_u
             ins_b = ins[:8] + [zeros[:n]]
             _launch("ttc_lqr_rollout", dev, lib.ttc_lqr_rollout, *[_ptr(t) for t in ins_b], _ptr(zeros[:n]),
-                    _ptr(M), _ptr(d_u[a:a + n]), n, nh, d, du, T, _F32, *[_ptr(o[a:a + n]) for o in out_b],
+                    _ptr(M), _ptr(d_u[a:a + n]), 1, n, nh, d, du, T, _F32, *[_ptr(o[a:a + n]) for o in out_b],
                     _ptr(lam0_b[a:a + n]), None, _ptr(status[1:2]))
     st = status.tolist()
     check_fwd_status(st[0])
