@@ -535,6 +535,15 @@ def main(argv=None):
                 **{k: {"launches": len(v), "mean_ms": statistics.mean(v)} for k, v in kern.items()
                    if k not in ("ttc_lqr_fwd", "ttc_lqr_bwd")},
             },
+            # whole-job rates of the device-resident step (all ranks) and the solver's
+            # algorithmic FLOPs (fwd + bwd, solver_flops) per second against the FP32 peak
+            "throughput": {
+                "rows_per_s": cfg.rows * world * args.steps / (ms / 1000.0),
+                "problems_per_s": cfg.problems * world * args.steps / (ms / 1000.0),
+                "solver_tflops": (fwd_f + bwd_f) * cfg.problems * world * args.steps / (ms / 1000.0) / 1e12,
+                "solver_frac_fp32_peak": (fwd_f + bwd_f) * cfg.problems * args.steps / (ms / 1000.0) / 1e12
+                / fp32_peak,
+            },
             "clocks": clock_summary,
             "e2e": {"value": tokens_per_step * e2e_steps / (e2e_ms / 1000.0), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
