@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 
 #include "lqr_adjoint_mma.cuh"
@@ -135,6 +136,20 @@ int set_smem(Kern k, size_t bytes) {
                     "cudaFuncSetAttribute");
 }
 
+// Two CTAs of two slots per SM at d = 32 (TcLaunch NARROW) when both fit the SM's shared
+// memory (TTC_FWD_NARROW=0 builds keep one CTA of four slots).
+#ifndef TTC_FWD_NARROW
+#define TTC_FWD_NARROW 1
+#endif
+constexpr size_t kSmPerSm = 228 * 1024;  // shared memory of an SM (each CTA also reserves 1 KB)
+// Launch epochs of the forward kernels of this translation unit (for their staggering words).
+static std::atomic<unsigned> g_fwd_epoch{0};
+inline unsigned next_fwd_epoch() {
+  unsigned e = ++g_fwd_epoch;
+  while (e == 0) e = ++g_fwd_epoch;
+  return e;
+}
+
 template <int D, int DU, typename TIn, bool SAVE_M, bool AFF = false>
 int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                   const void* lA, const void* lB, const void* lQ, const void* h0, int64_t N,
@@ -142,19 +157,30 @@ int launch_fwd_tc(const void* A, const void* B, const void* Q, const void* R, co
                   int opts, cudaStream_t st, const void* r_traj = nullptr) {
   using CF = TcCfg<D, DU>;
   using L = TcFwdLayout<D, DU, SAVE_M>;
+  const size_t extra = mix.basis != nullptr ? BasisSmem<D, TIn>::bytes(mix.rank) : 0;
+  const int tiles = (nh * D + 127) / 128;
+  bool narrow = false;
   int slots = tc_slots<D, DU, SAVE_M>(nh);
-  const size_t extra = mix.basis != nullptr ? L::basis_bytes(mix.rank) : 0;
+  if constexpr (D == 32 && TTC_FWD_NARROW) {
+    const int s2 = tiles < 2 ? tiles : 2;
+    if (tiles > 1 && 2 * (L::bytes(s2) + extra + 1024) <= kSmPerSm) {
+      narrow = true;
+      slots = s2;
+    }
+  }
   while (slots > 1 && L::bytes(slots) + extra > kMaxSmem) --slots;
   if (L::bytes(slots) + extra > kMaxSmem)
     return set_error(TTC_ERR_UNSUPPORTED, "the Q_f basis does not fit in shared memory");
   const uint32_t cols = tmem_cols_for(slots * CF::kSlotCols);
   const size_t smem = L::bytes(slots) + extra;
-  auto k = ttc::lqr_fwd_tc_kernel<D, DU, TIn, SAVE_M, AFF>;
+  auto k = narrow ? ttc::lqr_fwd_tc_kernel<D, DU, TIn, SAVE_M, AFF, true>
+                  : ttc::lqr_fwd_tc_kernel<D, DU, TIn, SAVE_M, AFF, false>;
   if (int rc = set_smem(k, smem)) return rc;
   k<<<dim3((unsigned)N), dim3(slots * 128), smem, st>>>(
       (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)Qf,
       (const TIn*)mix.basis, mix.rank, (const TIn*)lA, (const TIn*)lB, (const TIn*)lQ, (const TIn*)h0,
-      nh, T, opts, cols, (TIn*)u, lam0, M, status, mix.lowrank<TIn>(), (const TIn*)r_traj);
+      nh, T, opts, cols, (TIn*)u, lam0, M, status, mix.lowrank<TIn>(), (const TIn*)r_traj,
+      narrow ? next_fwd_epoch() : 0u);
   return cuda_check(cudaGetLastError(), "lqr_fwd_tc_kernel launch");
 }
 
@@ -236,7 +262,7 @@ int64_t bwd_mix_slices(int64_t N, int nh, int rQ) {
     // the backward stages each warp's [8][rQ] coefficients in one staging buffer
     if (8 * rQ > 3 * AdjMma<D>::kStage) return 0;
     // the forward keeps the basis in shared memory next to one tile slot at least
-    if (TcFwdLayout<D, DU, true>::bytes(1) + TcFwdLayout<D, DU, true>::basis_bytes(rQ) > kMaxSmem) return 0;
+    if (TcFwdLayout<D, DU, true>::bytes(1) + BasisSmem<D, TIn>::bytes(rQ) > kMaxSmem) return 0;
     const int64_t grid = bwd_mma_grid<D, TIn, true>(N, nh, true);
     if (grid == 0) return -TTC_ERR_CUDA;
     return grid;

@@ -55,13 +55,19 @@ struct TcCfg {
 
 // Launch shape: at d = 16 a thread needs ~80 registers, so 256-thread CTAs with three
 // resident per SM (6 tiles in flight) beat 512-thread CTAs at 128 registers (measured
-// 14 % on config 2); at d = 32 the 128-register budget of 4 tiles per SM is needed.
-// At d = 64 a thread holds two 64-wide state rows plus a product row (~220 registers):
-// 256-thread CTAs, one per SM.
-template <int D>
+// 14 % on config 2); at d = 32 the 128-register budget of 4 tiles per SM is needed: one
+// 512-thread CTA of four slots, or (NARROW) two 256-thread CTAs of two slots.  The two CTAs
+// of an SM drift apart, so one CTA's per-tile tail (Gauss-Jordan, M, u, the next tile's loads,
+// all without MMAs) overlaps the other's sweep: 1.9 % faster at T = 128 and 3 % at T = 32
+// (materialised Q_f, 8 192 rows), two tiles alone keeping 77 % of the four-tile throughput.
+// NARROW needs both CTAs' shared memory on the SM, hence the layer's Q_f basis staged in its
+// own bf16.  At d = 64 a thread holds two 64-wide state rows plus a product row (~220
+// registers): 256-thread CTAs, one per SM.
+template <int D, bool NARROW = false>
 struct TcLaunch {
-  static constexpr int kMaxThreads = D == 32 ? 512 : 256;
-  static constexpr int kMinBlocks = D <= 16 ? 3 : 1;
+  static constexpr bool kNarrow = NARROW && D == 32;
+  static constexpr int kMaxThreads = (D == 32 && !kNarrow) ? 512 : 256;
+  static constexpr int kMinBlocks = D <= 16 ? 3 : (kNarrow ? 2 : 1);
   static constexpr int kMaxSlots = kMaxThreads / 128;
 };
 
@@ -75,10 +81,24 @@ struct TcFwdLayout {
   static size_t bytes(int slots) {
     return sizeof(float) * (size_t)(C::kOps + C::kHeader + slots * C::kHeadsPerTile * kGroup);
   }
-  // A mixed Q_f keeps its rank-rQ basis in shared memory behind the groups, rows padded to
-  // D + 4 floats (16-byte row reads by the D threads of a head, conflict-free).
+  // A mixed Q_f keeps its rank-rQ basis in shared memory behind the groups (BasisSmem).
   __host__ __device__ static int basis_offset(int slots) { return C::kOps + C::kHeader + slots * C::kHeadsPerTile * kGroup; }
-  static size_t basis_bytes(int rQ) { return sizeof(float) * (size_t)rQ * D * (D + 4); }
+};
+
+// The layer's rank-rQ Q_f basis [rQ, D, D] in shared memory, read one row per thread with
+// 16-byte loads (the D threads of a head read rows 0..D-1 of one basis matrix at once).
+// float: rows padded to D + 4 floats, conflict-free.  bf16: the activation dtype as is (half
+// the bytes, so that two d = 32 CTAs fit on an SM), rows of D / 8 16-byte chunks with chunk
+// c of row i stored at c ^ swz(i), which spreads any 8 consecutive rows' same chunk over the
+// eight 16-byte bank groups.
+template <int D, typename TIn>
+struct BasisSmem {
+  static constexpr bool kHalf = sizeof(TIn) == 2;
+  static constexpr int kChunks = D / 8;  // 16-byte chunks of a bf16 row
+  static size_t bytes(int rQ) {
+    return kHalf ? (size_t)rQ * D * D * 2 : sizeof(float) * (size_t)rQ * D * (D + 4);
+  }
+  __host__ __device__ static constexpr int swz(int i) { return ((i * kChunks) >> 3) & (kChunks - 1); }
 };
 
 // OR of `pred` over the `count` threads of named barrier `id` (also a barrier).
@@ -266,11 +286,14 @@ struct Y3AffineSteps {
 // the NORMALIZE_TYPE=2 renormalisation (per warp row block, see renormalize_rows) on the
 // CUDA cores, and Y3 handed to `y3` on the last step.  Returns false, on every thread of the
 // slot alike, after an MMA timeout.
-template <int D, int DU, typename Y3>
+struct NoMark {
+  __device__ __forceinline__ void operator()(int) const {}
+};
+template <int D, int DU, typename Y3, typename Mark = NoMark>
 __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&y1)[D],
                                          float (&y2)[D], Y3& y3, const float* ops, float* vec,
                                          float a, float lgA2, float lgQ2, float lgB2, float rinv,
-                                         int T, bool every_step) {
+                                         int T, bool every_step, Mark&& mark = Mark()) {
   using V = SweepVec<D, DU>;
   using CF = TcCfg<D, DU>;
   constexpr bool kPairs = D <= 32;
@@ -300,6 +323,7 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
   };
   step_vectors(0);
   for (int s = 0; s < T; ++s) {
+    mark(s);
     const float* v = vec + (s & 1) * V::kSize;
     const bool last = (s == T - 1);
     const float4* v4 = reinterpret_cast<const float4*>(v);  // 16-byte aligned sections
@@ -402,11 +426,11 @@ __device__ __forceinline__ void add_inv_guard(float (&y1)[D], int i, int opts) {
 // This thread's row i of the terminal cost Q_f of problem p: read from Q_f [N*nh, D, D], or,
 // when `basis_s` is given, mixed from the rank-rQ basis as the layer does
 // (Q_f = sum_r coeff_Qf[r] basis[r], ttc_layer.py:119-123): `qf` is then coeff_Qf [N*nh, rQ],
-// basis_s the basis in shared memory (rows padded to D + 4), and the sum is rounded to the
-// activation dtype like the einsum it replaces.
+// basis_s the basis in shared memory (BasisSmem), and the sum is rounded to the activation
+// dtype like the einsum it replaces.
 template <int D, typename TIn>
 __device__ __forceinline__ void load_qf_row(float (&y2)[D], bool valid, const TIn* __restrict__ qf,
-                                            const float* basis_s, int rQ, int64_t p, int i) {
+                                            const void* basis_s, int rQ, int64_t p, int i) {
   if (!valid) {
 #pragma unroll
     for (int k = 0; k < D; ++k) y2[k] = 0.0f;
@@ -421,15 +445,31 @@ __device__ __forceinline__ void load_qf_row(float (&y2)[D], bool valid, const TI
 #pragma unroll
   for (int k = 0; k < D; ++k) y2[k] = 0.0f;
   const TIn* c = qf + p * rQ;
+  using BS = BasisSmem<D, TIn>;
   auto add_rank = [&](int r, float cr) {
-    const float4* row = reinterpret_cast<const float4*>(basis_s + (r * D + i) * (D + 4));
+    if constexpr (BS::kHalf) {
+      const uint4* row = reinterpret_cast<const uint4*>(basis_s) + (r * D + i) * BS::kChunks;
+      const int sw = BS::swz(i);
 #pragma unroll
-    for (int k4 = 0; k4 < D / 4; ++k4) {
-      const float4 b = row[k4];
-      y2[4 * k4] = fmaf(cr, b.x, y2[4 * k4]);
-      y2[4 * k4 + 1] = fmaf(cr, b.y, y2[4 * k4 + 1]);
-      y2[4 * k4 + 2] = fmaf(cr, b.z, y2[4 * k4 + 2]);
-      y2[4 * k4 + 3] = fmaf(cr, b.w, y2[4 * k4 + 3]);
+      for (int c = 0; c < BS::kChunks; ++c) {
+        const uint4 q = row[c ^ sw];
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          y2[8 * c + 2 * h] = fmaf(cr, __uint_as_float(w[h] << 16), y2[8 * c + 2 * h]);
+          y2[8 * c + 2 * h + 1] = fmaf(cr, __uint_as_float(w[h] & 0xffff0000u), y2[8 * c + 2 * h + 1]);
+        }
+      }
+    } else {
+      const float4* row = reinterpret_cast<const float4*>(basis_s) + (r * D + i) * (D / 4 + 1);
+#pragma unroll
+      for (int k4 = 0; k4 < D / 4; ++k4) {
+        const float4 b = row[k4];
+        y2[4 * k4] = fmaf(cr, b.x, y2[4 * k4]);
+        y2[4 * k4 + 1] = fmaf(cr, b.y, y2[4 * k4 + 1]);
+        y2[4 * k4 + 2] = fmaf(cr, b.z, y2[4 * k4 + 2]);
+        y2[4 * k4 + 3] = fmaf(cr, b.w, y2[4 * k4 + 3]);
+      }
     }
   };
   if ((rQ & 3) == 0 && (reinterpret_cast<uintptr_t>(c) & (4 * sizeof(TIn) - 1)) == 0) {
@@ -452,21 +492,71 @@ __device__ __forceinline__ void load_qf_row(float (&y2)[D], bool valid, const TI
 }
 
 // Cooperative copy of a rank-rQ basis [rQ, D, D] (activation dtype, 16-byte aligned) into
-// shared memory as fp32 rows of D + 4, four values per load and store.
+// shared memory in the BasisSmem layout, 16 bytes per load and store.
 template <int D, typename TIn>
-__device__ __forceinline__ void stage_basis(float* basis_s, const TIn* __restrict__ basis, int rQ, int tid,
+__device__ __forceinline__ void stage_basis(void* basis_s, const TIn* __restrict__ basis, int rQ, int tid,
                                             int nthreads) {
+  using BS = BasisSmem<D, TIn>;
+  if constexpr (BS::kHalf) {
+    const uint4* src = reinterpret_cast<const uint4*>(basis);
+    uint4* dst = reinterpret_cast<uint4*>(basis_s);
 #pragma unroll 4
-  for (int e4 = tid; e4 < rQ * D * D / 4; e4 += nthreads) {
-    const int e = 4 * e4;
-    *reinterpret_cast<float4*>(basis_s + (e / D) * (D + 4) + e % D) = ld4(basis + e);
+    for (int e8 = tid; e8 < rQ * D * D / 8; e8 += nthreads) {
+      const int row = e8 / BS::kChunks, c = e8 % BS::kChunks;
+      dst[row * BS::kChunks + (c ^ BS::swz(row % D))] = src[e8];
+    }
+  } else {
+    float* dst = static_cast<float*>(basis_s);
+#pragma unroll 4
+    for (int e4 = tid; e4 < rQ * D * D / 4; e4 += nthreads) {
+      const int e = 4 * e4;
+      *reinterpret_cast<float4*>(dst + (e / D) * (D + 4) + e % D) = ld4(basis + e);
+    }
   }
+}
+
+// Staggering of the P co-resident CTAs of an SM (P = TcLaunch::kMinBlocks; used for the two
+// CTAs of d = 32 NARROW: 0.6 % on top of their natural drift; at d = 16, three CTAs of one
+// tile each, it cost 5 %).  They run the same per-tile sequence, a sweep on the tensor cores
+// then a tail without MMAs, and started together they would stay in step, their tails
+// coinciding.
+// So the a-th CTA to arrive on an SM in a launch (a = 2..P) waits until the first one has
+// swept (a - 1) / P of its first tile; CTAs that replace them later inherit the offsets.
+// Arrivals are counted per SM in a word tagged with the launch's epoch (no reset between
+// launches), and the first CTA posts its progress (epoch, marks passed) in another; the wait
+// is bounded (2 ms) and only ever on a CTA resident on the same SM.  Each translation unit
+// has its own words.
+#ifndef TTC_FWD_STAGGER
+#define TTC_FWD_STAGGER 1
+#endif
+constexpr int kStaggerSMs = 1024;
+static __device__ unsigned long long g_tc_arrivals[kStaggerSMs];
+static __device__ unsigned long long g_tc_progress[kStaggerSMs];
+
+__device__ __forceinline__ unsigned smid() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
+
+// This CTA's arrival number on SM `sm` in launch `epoch` (1, 2, ...; 0 if undecided).
+__device__ __forceinline__ unsigned stagger_arrival(unsigned sm, unsigned epoch) {
+  unsigned long long* w = &g_tc_arrivals[sm % kStaggerSMs];
+  unsigned long long old = atomicAdd(w, 0ull);
+  for (int it = 0; it < 64; ++it) {
+    const unsigned long long nv =
+        (old >> 32) == epoch ? old + 1ull : ((static_cast<unsigned long long>(epoch) << 32) | 1ull);
+    const unsigned long long seen = atomicCAS(w, old, nv);
+    if (seen == old) return static_cast<unsigned>(nv & 0xffffffffull);
+    old = seen;
+  }
+  return 0;
 }
 
 // AFF: an affine action cost on every step, r_traj [N, nh, T, DU] (Y3AffineSteps): lambda0
 // solves Y1 lambda0 = Y2 h0 + c (one right-hand side), u includes -R_inv r_0, no M.
-template <int D, int DU, typename TIn, bool SAVE_M, bool AFF = false>
-__global__ void __launch_bounds__(TcLaunch<D>::kMaxThreads, TcLaunch<D>::kMinBlocks)
+template <int D, int DU, typename TIn, bool SAVE_M, bool AFF = false, bool NARROW = false>
+__global__ void __launch_bounds__(TcLaunch<D, NARROW>::kMaxThreads, TcLaunch<D, NARROW>::kMinBlocks)
 lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                   const TIn* __restrict__ Qm, const TIn* __restrict__ Rinv,
                   const TIn* __restrict__ Qf, const TIn* __restrict__ Qbasis, int rQ,
@@ -474,8 +564,11 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                   const TIn* __restrict__ lgB, const TIn* __restrict__ lgQ,
                   const TIn* __restrict__ H0, int nh, int T, int opts, uint32_t tmem_cols,
                   TIn* __restrict__ u_out, float* __restrict__ lam0_out, float* __restrict__ M_out,
-                  int* __restrict__ status, LowRank<TIn> lr, const TIn* __restrict__ r_traj = nullptr) {
+                  int* __restrict__ status, LowRank<TIn> lr, const TIn* __restrict__ r_traj = nullptr,
+                  unsigned epoch = 0) {
   static_assert(!(AFF && SAVE_M), "the per-step affine forward saves no M");
+  constexpr int kParts = TcLaunch<D, NARROW>::kMinBlocks;
+  constexpr bool kStagger = TcLaunch<D, NARROW>::kNarrow && TTC_FWD_STAGGER;
   using CF = TcCfg<D, DU>;
   using L = TcFwdLayout<D, DU, SAVE_M>;
   using V = SweepVec<D, DU>;
@@ -484,7 +577,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   uint64_t* mbars = reinterpret_cast<uint64_t*>(smem + CF::kOps);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + CF::kOps + 16);
   float* groups = smem + CF::kOps + CF::kHeader;
-  float* basis_s = Qbasis != nullptr ? smem + L::basis_offset(blockDim.x / 128) : nullptr;
+  void* basis_s = Qbasis != nullptr ? smem + L::basis_offset(blockDim.x / 128) : nullptr;
 
   const int tid = threadIdx.x;
   const int nslots = blockDim.x / 128;
@@ -523,6 +616,23 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
+  // the a-th CTA of the launch on this SM starts (a - 1) / kParts into the first one's first tile
+  unsigned stag_sm = 0, stag_arrival = 0;
+  if constexpr (kStagger) {
+    if (epoch != 0 && tid == 0) {
+      stag_sm = smid() % kStaggerSMs;
+      stag_arrival = stagger_arrival(stag_sm, epoch);
+      if (stag_arrival >= 2 && stag_arrival <= static_cast<unsigned>(kParts)) {
+        const uint64_t t0 = tc::global_ns();
+        while (tc::global_ns() - t0 < 2000000ull) {
+          const unsigned long long w = atomicAdd(&g_tc_progress[stag_sm], 0ull);
+          if ((w >> 32) == epoch && (w & 0xffffffffull) + 1 >= stag_arrival) break;
+          __nanosleep(500);
+        }
+      }
+    }
+    __syncthreads();
+  }
 
   const uint32_t tbase = *tmem_base_s;
   TileCtx X;
@@ -574,8 +684,17 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     using Y3T = std::conditional_t<AFF, Y3AffineSteps<TIn, DU>, Y3Discard>;
     Y3T y3;  // without AFF, M is formed from P below instead of from Y3
     if constexpr (AFF) y3 = Y3T{valid ? r_traj + p * T * DU : nullptr, sh0 + 2 * D, 0.f};
+    const bool marker = kStagger && stag_arrival == 1 && tile == 0 && tid == 0;
     const bool swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T,
-                                              (opts & TTC_FLAG_INV_GUARD) != 0);
+                                       (opts & TTC_FLAG_INV_GUARD) != 0, [&](int s) {
+                                         if (marker) {
+#pragma unroll
+                                           for (int m = 1; m < kParts; ++m)
+                                             if (s == m * T / kParts)
+                                               atomicExch(&g_tc_progress[stag_sm],
+                                                          (static_cast<unsigned long long>(epoch) << 32) | m);
+                                         }
+                                       });
     // Uniform over the slot: a late timeout on the last product surfaces here too.
     if (slot_sync_or(X.bar_id, 128, X.timed_out || !swept)) {
       flags |= TTC_STATUS_MMA_TIMEOUT;
