@@ -68,9 +68,12 @@ def test_solver_matches_reference_golden(case, save_budget):
 @pytest.mark.parametrize("d,nh,N,T", [(16, 16, 24, 64), (16, 3, 7, 33), (16, 20, 5, 16),
                                       (32, 32, 6, 128), (32, 5, 9, 40), (32, 1, 3, 7),
                                       (32, 64, 2, 9), (32, 28, 3, 1), (32, 30, 5, 2),
-                                      (64, 3, 2, 24), (64, 1, 3, 5)])
+                                      (64, 3, 2, 24), (64, 1, 3, 5), (64, 32, 2, 24), (64, 16, 3, 20),
+                                      (64, 12, 2, 9), (64, 20, 3, 5), (64, 25, 2, 3), (64, 32, 1, 1)])
 def test_solver_matches_oracle_seeded(d, nh, N, T):
-    """Seeded synthetic problems, head counts that leave CTA groups idle, odd sizes."""
+    """Seeded synthetic problems, head counts that leave CTA groups idle, odd sizes.  At
+    d = 64 the head counts above 8 run the split-pair MMA adjoint (one and two grad units per
+    warp, partial last groups), the others the CUDA-core adjoint."""
     host = [torch.from_numpy(a) for a in solver_inputs_synthetic(N, nh, d, d, seed=100 + d + nh)]
     dy = torch.randn(N, nh, d, dtype=torch.float64, generator=torch.Generator().manual_seed(7))
     leaves = [a.clone().requires_grad_(True) for a in host]
@@ -80,6 +83,25 @@ def test_solver_matches_oracle_seeded(d, nh, N, T):
     args = [a.to("cuda", torch.float32).requires_grad_(True) for a in host]
     u, grads = run_cuda(args, T, dy.float().cuda())
     assert O.max_rel(u.cpu(), u_ric) < FWD_TOL_F32
+    for name, g, leaf in zip(SOLVER_ARG_NAMES, grads, leaves):
+        assert O.max_rel(g.cpu(), leaf.grad) < GRAD_TOL_F32, name
+
+
+@pytest.mark.parametrize("d,nh,N,T", [(16, 16, 3, 12), (32, 32, 2, 10), (64, 32, 2, 10), (64, 16, 2, 7)])
+def test_solver_nonsymmetric_Q_matches_oracle(d, nh, N, T):
+    """A Q with an antisymmetric part (the plug-in signature accepts any Q): the adjoint
+    kernels then also need Q^T h for the log_gamma_Q gradient.  Checked against the oracle's
+    restatement of the fused solver, which uses Q as given in both directions."""
+    host = [torch.from_numpy(a) for a in solver_inputs_synthetic(N, nh, d, d, seed=500 + d + nh)]
+    G = torch.randn(N, d, d, dtype=torch.float64, generator=torch.Generator().manual_seed(11))
+    host[2] = host[2] + 0.05 * (G - G.transpose(1, 2)) / d ** 0.5
+    dy = torch.randn(N, nh, d, dtype=torch.float64, generator=torch.Generator().manual_seed(8))
+    leaves = [a.clone().requires_grad_(True) for a in host]
+    u_ref = O.fused_solve(*leaves, T)
+    (u_ref * dy).sum().backward()
+    args = [a.to("cuda", torch.float32).requires_grad_(True) for a in host]
+    u, grads = run_cuda(args, T, dy.float().cuda())
+    assert O.max_rel(u.cpu(), u_ref.detach()) < FWD_TOL_F32
     for name, g, leaf in zip(SOLVER_ARG_NAMES, grads, leaves):
         assert O.max_rel(g.cpu(), leaf.grad) < GRAD_TOL_F32, name
 
@@ -102,6 +124,27 @@ def test_saved_and_recompute_backward_agree():
     assert torch.equal(u1, u2)
     for a, b in zip(g1, g2):
         assert O.max_rel(a.cpu(), b.cpu()) < 1e-5
+
+
+def test_split_adjoint_d64_agrees_with_recompute_and_repeats():
+    """d = 64, 32 heads: the saved-state backward (split-pair MMA adjoint from M) against the
+    recompute backward (the sweep again, CUDA-core adjoint); bitwise repeatable, and a row's
+    gradients do not depend on the rows around it."""
+    host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(5, 32, 64, 64, seed=77)]
+    dy = torch.randn(5, 32, 64, generator=torch.Generator().manual_seed(5)).cuda()
+
+    def run(rows, budget):
+        return run_cuda([a[rows].cuda().requires_grad_(True) for a in host], 40, dy[rows], budget)
+
+    u1, g1 = run(slice(0, 5), None)
+    u2, g2 = run(slice(0, 5), None)
+    u3, g3 = run(slice(0, 5), 0)
+    u4, g4 = run(slice(2, 4), None)
+    assert torch.equal(u1, u2) and all(torch.equal(a, b) for a, b in zip(g1, g2))
+    assert torch.equal(u1, u3)
+    for name, a, b in zip(SOLVER_ARG_NAMES, g1, g3):
+        assert O.max_rel(a.cpu(), b.cpu()) < 2e-5, name
+    assert torch.equal(u4, u1[2:4]) and all(torch.equal(a, b[2:4]) for a, b in zip(g4, g1))
 
 
 def test_deterministic_and_batch_invariant():

@@ -8,6 +8,7 @@
 #include <cstdio>
 
 #include "lqr_adjoint_mma.cuh"
+#include "lqr_adjoint_split.cuh"
 #include "lqr_rollout.cuh"
 #include "lqr_tc.cuh"
 
@@ -255,6 +256,29 @@ int launch_bwd_mma(const void* A, const void* B, const void* Q, const void* R, c
   return cuda_check(cudaGetLastError(), "lqr_bwd_mma_kernel launch");
 }
 
+// Saved-state backward at d = 64 on the warp-MMA adjoint with each 8-head group split over a
+// warp pair (TTC_ADJ_SPLIT=0 builds keep the CUDA-core adjoint there).
+#ifndef TTC_ADJ_SPLIT
+#define TTC_ADJ_SPLIT 1
+#endif
+
+template <int D, typename TIn>
+int launch_bwd_split(const void* A, const void* B, const void* Q, const void* R, const void* lA,
+                     const void* lB, const void* lQ, const void* h0, const float* lam0, const float* M,
+                     const void* dU, int64_t N, int nh, int T, void* const* g, int* status, cudaStream_t st) {
+  using C = AdjSplit<D>;
+  const int rpc = C::rows_per_cta(nh);
+  const size_t smem = C::bytes(nh);
+  auto k = C::units_per_warp(nh) == 1 ? ttc::lqr_bwd_split_kernel<D, TIn, 1> : ttc::lqr_bwd_split_kernel<D, TIn, 2>;
+  if (int rc = set_smem(k, smem)) return rc;
+  const int64_t grid = (N + rpc - 1) / rpc;
+  k<<<dim3((unsigned)grid), dim3(32 * C::warps(nh)), smem, st>>>(
+      (const TIn*)A, (const TIn*)B, (const TIn*)Q, (const TIn*)R, (const TIn*)lA, (const TIn*)lB,
+      (const TIn*)lQ, (const TIn*)h0, lam0, M, (const TIn*)dU, N, nh, T, rpc, (TIn*)g[0], (TIn*)g[1],
+      (TIn*)g[2], (TIn*)g[3], (TIn*)g[4], (TIn*)g[5], (TIn*)g[6], (TIn*)g[7], (TIn*)g[8], status);
+  return cuda_check(cudaGetLastError(), "lqr_bwd_split_kernel launch");
+}
+
 template <int D, int DU, typename TIn>
 int64_t bwd_mix_slices(int64_t N, int nh, int rQ) {
   if constexpr (D == DU && D <= TTC_ADJ_MMA_MAXD) {
@@ -283,6 +307,10 @@ int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const
     if (M != nullptr && AdjMma<D>::fits(nh))
       return launch_bwd_mma<D, TIn, true>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status,
                                           mix, Qf, st);
+  }
+  if constexpr (TTC_ADJ_SPLIT && D == DU && D == 64) {
+    if (M != nullptr && mix.basis == nullptr && AdjSplit<D>::fits(nh))
+      return launch_bwd_split<D, TIn>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status, st);
   }
   if (mix.basis != nullptr)
     return set_error(TTC_ERR_UNSUPPORTED,
