@@ -30,8 +30,16 @@ struct AdjSplit {
   static constexpr int NT = D / 8;             // k-steps of a product = n-tiles of a vector
   static constexpr int NH = NT / 2;            // n-tiles a warp of the pair owns
   static constexpr int MT = D / 16;            // m-tiles of grad_B / grad_Q
-  static constexpr int kUnits = 2 * MT;        // (grad_B | grad_Q, m-tile) units of NT tiles
-  static constexpr int kFrag = NT * NT * 64;   // floats of one constant operand (fp32 pairs)
+  // grad_B / grad_Q work units: (matrix, m-tile, part) of NTU n-tiles; at d = 32 each m-tile
+  // row is cut in two so that the eight warps of a 32-head row all get one
+  static constexpr int kParts = D == 32 ? 2 : 1;
+  static constexpr int NTU = NT / kParts;
+  static constexpr int kUnits = 2 * MT * kParts;
+  // constant operands in fragment order: at d = 32 pre-split tf32 hi / lo (float4 per lane,
+  // shared memory is not the limit); at d = 64 fp32 pairs split while loading (16 KB each)
+  static constexpr bool kPreSplit = D <= 32;
+  static constexpr int kFrag = NT * NT * (kPreSplit ? 128 : 64);
+  static constexpr int kMinBlocks = D <= 32 ? 2 : 1;
   static constexpr int SS = AdjMma<D>::SS;     // staging row stride (bank-conflict free)
   static constexpr int kStage = 16 * SS;
   // per group: [lambda; dlambda], [u e^lgB; du e^lgB], [h Dq; dh Dq], double-buffered by step
@@ -79,16 +87,18 @@ __device__ __forceinline__ void build_operand_pairs(float* dst, Get get, int tid
 }
 
 // Warp c's n-tiles of out = S W (S: the 16 x D staged operand, both halves), 3xTF32, k-steps
-// in order.  out[jl] is n-tile NH c + jl in output-fragment order.
+// in order.  out[jl] is n-tile NH c + jl in output-fragment order.  W: the operand in the
+// layout AdjSplit<D>::kPreSplit selects.
 template <int D>
-__device__ __forceinline__ void split_product(const float* S, float (&out)[D / 16][4], const float2* W, int c,
+__device__ __forceinline__ void split_product(const float* S, float (&out)[D / 16][4], const float* W, int c,
                                               int lane, int g, int t) {
   constexpr int NT = D / 8, NH = NT / 2, SS = AdjSplit<D>::SS;
 #pragma unroll
   for (int jl = 0; jl < NH; ++jl)
 #pragma unroll
     for (int r = 0; r < 4; ++r) out[jl][r] = 0.f;
-  const float2* Wc = W + NH * c * 32 + lane;
+  const float2* Wc = reinterpret_cast<const float2*>(W) + NH * c * 32 + lane;
+  const float4* Wc4 = reinterpret_cast<const float4*>(W) + NH * c * 32 + lane;
 #pragma unroll
   for (int kk = 0; kk < NT; ++kk) {
     // a0: row g slot t <- entry 8kk+2t; a1: row g+8 slot t; a2 / a3: slot t+4 <- 8kk+2t+1
@@ -102,9 +112,17 @@ __device__ __forceinline__ void split_product(const float* S, float (&out)[D / 1
     uint32_t bh0[NH], bl0[NH], bh1[NH], bl1[NH];
 #pragma unroll
     for (int jl = 0; jl < NH; ++jl) {
-      const float2 w = Wc[(kk * NT + jl) * 32];
-      wmma::split(w.x, bh0[jl], bl0[jl]);
-      wmma::split(w.y, bh1[jl], bl1[jl]);
+      if constexpr (AdjSplit<D>::kPreSplit) {
+        const float4 w = Wc4[(kk * NT + jl) * 32];
+        bh0[jl] = __float_as_uint(w.x);
+        bh1[jl] = __float_as_uint(w.y);
+        bl0[jl] = __float_as_uint(w.z);
+        bl1[jl] = __float_as_uint(w.w);
+      } else {
+        const float2 w = Wc[(kk * NT + jl) * 32];
+        wmma::split(w.x, bh0[jl], bl0[jl]);
+        wmma::split(w.y, bh1[jl], bl1[jl]);
+      }
     }
     // passes over the n-tiles: consecutive MMAs go to independent accumulators
 #pragma unroll
@@ -128,6 +146,39 @@ __device__ __forceinline__ void stage_half(float* S, const float (&v)[D / 16][4]
   }
 }
 
+// acc[nj][.] += sum_r SX[r][16 mi + m] * SY[(r + 8) % 16][8 (nj0 + nj) + n] over the 16
+// staged rows: n-tiles nj0 .. nj0 + NTU - 1 of one m-tile of grad_B / grad_Q, 3xTF32 (the
+// sums of accumulate_unit, restricted to the unit's n-tiles).
+template <int D, int NTU>
+__device__ __forceinline__ void accumulate_tiles(float (&acc)[NTU][4], const float* SX, const float* SY, int mi,
+                                                 int nj0, int g, int t) {
+  constexpr int SS = AdjSplit<D>::SS;
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    const float* x0 = SX + (8 * kk + t) * SS + 16 * mi;
+    const float* x1 = SX + (8 * kk + t + 4) * SS + 16 * mi;
+    uint32_t ah[4], al[4];
+    wmma::split(x0[g], ah[0], al[0]);
+    wmma::split(x0[g + 8], ah[1], al[1]);
+    wmma::split(x1[g], ah[2], al[2]);
+    wmma::split(x1[g + 8], ah[3], al[3]);
+    const float* y0 = SY + ((8 * kk + t + 8) & 15) * SS + 8 * nj0;
+    const float* y1 = SY + ((8 * kk + t + 12) & 15) * SS + 8 * nj0;
+    uint32_t bh0[NTU], bl0[NTU], bh1[NTU], bl1[NTU];
+#pragma unroll
+    for (int nj = 0; nj < NTU; ++nj) {
+      wmma::split(y0[8 * nj + g], bh0[nj], bl0[nj]);
+      wmma::split(y1[8 * nj + g], bh1[nj], bl1[nj]);
+    }
+#pragma unroll
+    for (int nj = 0; nj < NTU; ++nj) wmma::m16n8k8(acc[nj], al, bh0[nj], bh1[nj]);
+#pragma unroll
+    for (int nj = 0; nj < NTU; ++nj) wmma::m16n8k8(acc[nj], ah, bl0[nj], bl1[nj]);
+#pragma unroll
+    for (int nj = 0; nj < NTU; ++nj) wmma::m16n8k8(acc[nj], ah, bh0[nj], bh1[nj]);
+  }
+}
+
 // Backward from the forward's lambda0 and M (d_p = M d_u per head, fused_lqr.py:185-187).
 // Grid: ceil(N / R) CTAs of R rows x W = 2 ceil(nh / 8) warps.  Warp w of a row is half
 // c = w % 2 of head group w / 2; the pair meets at a named barrier before each product whose
@@ -135,7 +186,7 @@ __device__ __forceinline__ void stage_half(float* S, const float (&v)[D / 16][4]
 // accumulates grad_B / grad_Q units w, w + W (UPW at most) over every group's staged vectors
 // of that step, in group order.
 template <int D, typename TIn, int UPW>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(256, AdjSplit<D>::kMinBlocks)
 lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm, const TIn* __restrict__ Qm,
                      const TIn* __restrict__ Rinv, const TIn* __restrict__ lgA, const TIn* __restrict__ lgB,
                      const TIn* __restrict__ lgQ, const TIn* __restrict__ H0, const float* __restrict__ lam0_in,
@@ -145,7 +196,7 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                      TIn* __restrict__ glgA_out, TIn* __restrict__ glgB_out, TIn* __restrict__ glgQ_out,
                      TIn* __restrict__ gh0_out, int* __restrict__ status) {
   using C = AdjSplit<D>;
-  constexpr int NH = C::NH, MT = C::MT;
+  constexpr int NH = C::NH, MT = C::MT, NTU = C::NTU, kP = C::kParts;
   extern __shared__ __align__(128) float smem[];
   const int tid = threadIdx.x, nthreads = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -177,10 +228,17 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       float* base = rows_s + r * C::kRow;
       const TIn* Bn = Bm + nr * (D * D);
       const TIn* Qn = Qm + nr * (D * D);
-      build_operand_pairs<D>(base, [&](int k, int cc) { return ldf(Qn + cc * D + k); }, tid, nthreads);
-      build_operand_pairs<D>(base + C::kFrag, [&](int k, int cc) { return ldf(Bn + k * D + cc); }, tid, nthreads);
-      build_operand_pairs<D>(base + 2 * C::kFrag, [&](int k, int cc) { return ldf(Bn + cc * D + k); }, tid, nthreads);
-      build_operand_pairs<D>(base + 3 * C::kFrag, [&](int k, int cc) { return ldf(Qn + k * D + cc); }, tid, nthreads);
+      auto build = [&](float* dst, auto get) {
+        if constexpr (C::kPreSplit) {
+          build_operand<D>(dst, get, tid, nthreads);
+        } else {
+          build_operand_pairs<D>(dst, get, tid, nthreads);
+        }
+      };
+      build(base, [&](int k, int cc) { return ldf(Qn + cc * D + k); });
+      build(base + C::kFrag, [&](int k, int cc) { return ldf(Bn + k * D + cc); });
+      build(base + 2 * C::kFrag, [&](int k, int cc) { return ldf(Bn + cc * D + k); });
+      build(base + 3 * C::kFrag, [&](int k, int cc) { return ldf(Qn + k * D + cc); });
       bool asym = false;
       for (int e = tid; e < D * D; e += nthreads) asym |= ldf(Qn + e) != ldf(Qn + (e % D) * D + e / D);
       if (asym) reinterpret_cast<int*>(base + 4 * C::kFrag)[0] = 0;
@@ -188,10 +246,10 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     __syncthreads();
 
     const float* rbase = rows_s + rloc * C::kRow;
-    const float2* Wqt = reinterpret_cast<const float2*>(rbase);
-    const float2* Wb = reinterpret_cast<const float2*>(rbase + C::kFrag);
-    const float2* Wbt = reinterpret_cast<const float2*>(rbase + 2 * C::kFrag);
-    const float2* Wq = reinterpret_cast<const float2*>(rbase + 3 * C::kFrag);
+    const float* Wqt = rbase;
+    const float* Wb = rbase + C::kFrag;
+    const float* Wbt = rbase + 2 * C::kFrag;
+    const float* Wq = rbase + 3 * C::kFrag;
     const bool sym = reinterpret_cast<const int*>(rbase + 4 * C::kFrag)[0] != 0;
 
     const int h = grp * 8 + g;
@@ -242,11 +300,11 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         gA[jl][s] = glgQ[jl][s] = gR[jl][s] = glgB[jl][s] = 0.f;
         dqp[jl][s] = 1.0f;
       }
-    float acc[UPW][C::NT][4];
+    float acc[UPW][NTU][4];
 #pragma unroll
     for (int q = 0; q < UPW; ++q)
 #pragma unroll
-      for (int nj = 0; nj < C::NT; ++nj)
+      for (int nj = 0; nj < NTU; ++nj)
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[q][nj][r] = 0.f;
 
@@ -258,14 +316,15 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       for (int q = 0; q < UPW; ++q) {
         const int unit = hb + q * wpr;
         if (unit < C::kUnits) {
-          const bool isq = unit >= MT;
+          const bool isq = unit >= MT * kP;
           if (!isq || ks < T - 1) {
-            const int mi = isq ? unit - MT : unit;
+            const int um = isq ? unit - MT * kP : unit;
+            const int mi = um / kP, nj0 = (um % kP) * NTU;
             const int off = (ks & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : 0);
             const int offy = (ks & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : C::kStage);
             for (int w = 0; w < gpr; ++w) {
               const float* base = row_stage + (size_t)w * C::kGroup;
-              accumulate_unit<D>(acc[q], base + off, base + offy, mi, g, t);
+              accumulate_tiles<D, NTU>(acc[q], base + off, base + offy, mi, nj0, g, t);
             }
           }
         }
@@ -418,13 +477,14 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       for (int q = 0; q < UPW; ++q) {
         const int unit = hb + q * wpr;
         if (unit < C::kUnits) {
-          const bool isq = unit >= MT;
-          const int mi = isq ? unit - MT : unit;
+          const bool isq = unit >= MT * kP;
+          const int um = isq ? unit - MT * kP : unit;
+          const int mi = um / kP, nj0 = (um % kP) * NTU;
           const float sc = isq ? 0.5f : 1.0f;
           TIn* out = (isq ? gQ_out : gB_out) + n * (D * D);
 #pragma unroll
-          for (int nj = 0; nj < C::NT; ++nj) {
-            const int r0 = 16 * mi + g, c0 = 8 * nj + 2 * t;
+          for (int nj = 0; nj < NTU; ++nj) {
+            const int r0 = 16 * mi + g, c0 = 8 * (nj0 + nj) + 2 * t;
             const float v[4] = {sc * acc[q][nj][0], sc * acc[q][nj][1], sc * acc[q][nj][2], sc * acc[q][nj][3]};
             bad |= unstable(v[0]) | unstable(v[1]) | unstable(v[2]) | unstable(v[3]);
             stf(out + r0 * D + c0, v[0]);

@@ -298,11 +298,19 @@ int64_t bwd_mix_slices(int64_t N, int nh, int rQ) {
   }
 }
 
+#ifndef TTC_ADJ_SPLIT32
+#define TTC_ADJ_SPLIT32 0
+#endif
+
 template <int D, int DU, typename TIn>
 int launch_bwd(const void* A, const void* B, const void* Q, const void* R, const void* Qf,
                const void* lA, const void* lB, const void* lQ, const void* h0, const float* lam0,
                const float* M, const void* dU, int64_t N, int nh, int T, void* const* g,
                int* status, const QMix& mix, int opts, cudaStream_t st) {
+  if constexpr (TTC_ADJ_SPLIT32 && D == DU && D == 32) {
+    if (M != nullptr && mix.basis == nullptr && AdjSplit<D>::fits(nh))
+      return launch_bwd_split<D, TIn>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status, st);
+  }
   if constexpr (D == DU && D <= TTC_ADJ_MMA_MAXD) {
     if (M != nullptr && AdjMma<D>::fits(nh))
       return launch_bwd_mma<D, TIn, true>(A, B, Q, R, lA, lB, lQ, h0, lam0, M, dU, N, nh, T, g, status,
