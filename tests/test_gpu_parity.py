@@ -147,6 +147,22 @@ def test_split_adjoint_d64_agrees_with_recompute_and_repeats():
     assert torch.equal(u4, u1[2:4]) and all(torch.equal(a, b[2:4]) for a, b in zip(g4, g1))
 
 
+@pytest.mark.parametrize("d,nh", [(32, 32), (64, 32), (64, 16)])
+def test_solver_bf16_agrees_with_fp32_on_rounded_inputs(d, nh):
+    """bf16 activations (fp32 solver state): the same inputs rounded to bf16, solved with fp32
+    and with bf16 activations, agree up to the bf16 rounding of the outputs, forward and
+    backward, through the saved-state backward kernels of each shape."""
+    host = [torch.from_numpy(a).to(torch.bfloat16) for a in solver_inputs_synthetic(3, nh, d, d, seed=40 + d + nh)]
+    dy = torch.randn(3, nh, d, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16)
+    u32, g32 = run_cuda([a.to("cuda", torch.float32).requires_grad_(True) for a in host], 12, dy.float().cuda())
+    u16, g16 = run_cuda([a.cuda().requires_grad_(True) for a in host], 12, dy.cuda())
+    assert u16.dtype == torch.bfloat16
+    assert O.max_rel(u16.float().cpu(), u32.cpu()) < 1e-2
+    for name, a, b in zip(SOLVER_ARG_NAMES, g16, g32):
+        assert a.dtype == torch.bfloat16
+        assert O.max_rel(a.float().cpu(), b.cpu()) < 1e-2, name
+
+
 def test_deterministic_and_batch_invariant():
     """Bitwise reproducible, and a row's result does not depend on the batch around it."""
     host = [torch.from_numpy(a).float() for a in solver_inputs_synthetic(40, 8, 16, 16, seed=9)]
