@@ -18,6 +18,9 @@
 // fragment order (16 KB each) and split into tf32 hi / lo while loading.  The grad_B /
 // grad_Q tiles are dealt out to the row's warps, which meet at one row barrier per step and
 // each sum every group's staged vectors in group order: deterministic.
+// The kernel is written for any d >= 32; d = 32 builds it only with TTC_ADJ_SPLIT32=1 (there
+// the one-warp kernel of lqr_adjoint_mma.cuh is 10 % faster: the operand reloads and pair
+// barriers cost more than the doubled occupancy hides).
 #pragma once
 
 #include "lqr_adjoint_mma.cuh"
