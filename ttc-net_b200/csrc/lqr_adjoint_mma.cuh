@@ -47,6 +47,12 @@ __device__ __forceinline__ void m16n8k8(float (&c)[4], const uint32_t (&a)[4], u
 
 }  // namespace wmma
 
+// bf16 activations: the grad_B / grad_Q contractions over heads in single-pass rounded tf32
+// (TTC_BF16_ONEPASS=0 builds keep them in 3xTF32).
+#ifndef TTC_BF16_ONEPASS
+#define TTC_BF16_ONEPASS 1
+#endif
+
 template <int D>
 struct AdjMma {
   static_assert(D % 16 == 0, "d must be a multiple of 16");
@@ -164,10 +170,27 @@ __device__ __forceinline__ void stage_rows(float* S, const float (&v)[D / 8][4],
 // (K) for one m-tile of the output, 3xTF32.  KK = 1 takes the first 8 rows only (the primal
 // rows against the tangent rows): for a symmetric pair X = Y = [v; dv] that is
 // S = sum v dv^T, whose S + S^T is the full sum at half the MMAs.
-template <int D, int KK = 2>
+// ONE: single-pass tf32 with both operands rounded to nearest (relative error ~2^-11 per
+// product, unbiased), for bf16 activations, where these sums only reach outputs rounded to
+// bf16 (2^-9): grad_B, grad_Q and, in the layer's low-rank solve, the coefficient and basis
+// gradients formed from them.  The recursion's own products stay 3xTF32.
+template <int D, int KK = 2, bool ONE = false>
 __device__ __forceinline__ void accumulate_unit(float (&acc)[D / 8][4], const float* SX, const float* SY,
                                                 int mi, int g, int t) {
   constexpr int SS = AdjMma<D>::SS, NT = D / 8;
+  if constexpr (ONE) {
+#pragma unroll
+    for (int kk = 0; kk < KK; ++kk) {
+      const float* x0 = SX + (8 * kk + t) * SS + 16 * mi;
+      const float* x1 = SX + (8 * kk + t + 4) * SS + 16 * mi;
+      const uint32_t a[4] = {wmma::rna(x0[g]), wmma::rna(x0[g + 8]), wmma::rna(x1[g]), wmma::rna(x1[g + 8])};
+      const float* y0 = SY + ((8 * kk + t + 8) & 15) * SS;
+      const float* y1 = SY + ((8 * kk + t + 12) & 15) * SS;
+#pragma unroll
+      for (int nj = 0; nj < NT; ++nj) wmma::m16n8k8(acc[nj], a, wmma::rna(y0[8 * nj + g]), wmma::rna(y1[8 * nj + g]));
+    }
+    return;
+  }
 #pragma unroll
   for (int kk = 0; kk < KK; ++kk) {
     const float* x0 = SX + (8 * kk + t) * SS + 16 * mi;
@@ -393,6 +416,8 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
                    int* __restrict__ status, LowRank<TIn> lr) {
   using C = AdjMma<D>;
   constexpr int NT = C::NT, MT = C::MT;
+  // grad_B / grad_Q contractions in single-pass rounded tf32 for bf16 activations
+  constexpr bool kOneContract = sizeof(TIn) == 2 && TTC_BF16_ONEPASS;
   extern __shared__ __align__(128) float smem[];
   const int tid = threadIdx.x, nthreads = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -564,14 +589,14 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
             if constexpr (C::kOwn) {
               // grad_Q as S = sum (h Dq)(dh Dq)^T, symmetrised at the end
               if (isq) {
-                accumulate_unit<D, 1>(acc[q], stg + off, stg + offy, mi, g, t);
+                accumulate_unit<D, 1, kOneContract>(acc[q], stg + off, stg + offy, mi, g, t);
               } else {
-                accumulate_unit<D>(acc[q], stg + off, stg + offy, mi, g, t);
+                accumulate_unit<D, 2, kOneContract>(acc[q], stg + off, stg + offy, mi, g, t);
               }
             } else {
               for (int w = 0; w < wpr; ++w) {
                 const float* base = row_stage + (size_t)w * C::kWarp;
-                accumulate_unit<D>(acc[q], base + off, base + offy, mi, g, t);
+                accumulate_unit<D, 2, kOneContract>(acc[q], base + off, base + offy, mi, g, t);
               }
             }
           }

@@ -152,10 +152,23 @@ __device__ __forceinline__ void stage_half(float* S, const float (&v)[D / 16][4]
 // acc[nj][.] += sum_r SX[r][16 mi + m] * SY[(r + 8) % 16][8 (nj0 + nj) + n] over the 16
 // staged rows: n-tiles nj0 .. nj0 + NTU - 1 of one m-tile of grad_B / grad_Q, 3xTF32 (the
 // sums of accumulate_unit, restricted to the unit's n-tiles).
-template <int D, int NTU>
+template <int D, int NTU, bool ONE = false>
 __device__ __forceinline__ void accumulate_tiles(float (&acc)[NTU][4], const float* SX, const float* SY, int mi,
                                                  int nj0, int g, int t) {
   constexpr int SS = AdjSplit<D>::SS;
+  if constexpr (ONE) {  // single-pass rounded tf32, as accumulate_unit<.., ONE>
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const float* x0 = SX + (8 * kk + t) * SS + 16 * mi;
+      const float* x1 = SX + (8 * kk + t + 4) * SS + 16 * mi;
+      const uint32_t a[4] = {wmma::rna(x0[g]), wmma::rna(x0[g + 8]), wmma::rna(x1[g]), wmma::rna(x1[g + 8])};
+      const float* y0 = SY + ((8 * kk + t + 8) & 15) * SS + 8 * nj0;
+      const float* y1 = SY + ((8 * kk + t + 12) & 15) * SS + 8 * nj0;
+#pragma unroll
+      for (int nj = 0; nj < NTU; ++nj) wmma::m16n8k8(acc[nj], a, wmma::rna(y0[8 * nj + g]), wmma::rna(y1[8 * nj + g]));
+    }
+    return;
+  }
 #pragma unroll
   for (int kk = 0; kk < 2; ++kk) {
     const float* x0 = SX + (8 * kk + t) * SS + 16 * mi;
@@ -327,7 +340,8 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
             const int offy = (ks & 1) * 3 * C::kStage + (isq ? 2 * C::kStage : C::kStage);
             for (int w = 0; w < gpr; ++w) {
               const float* base = row_stage + (size_t)w * C::kGroup;
-              accumulate_tiles<D, NTU>(acc[q], base + off, base + offy, mi, nj0, g, t);
+              accumulate_tiles<D, NTU, sizeof(TIn) == 2 && TTC_BF16_ONEPASS>(acc[q], base + off, base + offy, mi,
+                                                                              nj0, g, t);
             }
           }
         }
