@@ -13,9 +13,10 @@ step: weak scaling, so N = 8 runs config 5's global batch of 64 sequences.  ``--
 instead splits config 5's global batch over the N GPUs (strong scaling, as BASELINE.json
 defines it).  Rank 0 prints one JSON line.
 
-``--impl reference`` times the reference's CPU algorithm (the oracle's restatement of the
-``riccati`` solver with autograd backward, all host threads) on a row sample of the same
-workload; rank 0 only.
+``--impl reference`` times the reference's CPU path, its own ``TTCLayer(solver_impl="riccati")``
+forward + autograd backward from the unmodified install in baseline/_ref (fla's Triton l2norm
+replaced by its formula on CPU tensors; the oracle's restatement when that install is absent),
+fp32, all host threads, on a row sample of the same workload; rank 0 only.
 """
 from __future__ import annotations
 
