@@ -115,7 +115,9 @@ __device__ __forceinline__ void build_operand(float* dst, Get get, int tid, int 
 // out (16 x D, output-fragment order) = in (16 x D, output-fragment order) * W, 3xTF32.
 // in[j] = {row g e0, row g e1, row g+8 e0, row g+8 e1} with e0/e1 = entries 8j+2t, 8j+2t+1.
 // k-steps outer, n-tiles inner: one A fragment live at a time and NT independent chains.
-template <int D>
+// EXACT_W: W is exactly representable in tf32 (bf16 activations: B and Q are bf16 values), so
+// its residual is zero and the in_hi * W_lo terms, exact zeros, are not issued.
+template <int D, bool EXACT_W = false>
 __device__ __forceinline__ void frag_product(const float (&in)[D / 8][4], float (&out)[D / 8][4],
                                              const float4* W, int lane) {
   constexpr int NT = D / 8;
@@ -139,8 +141,10 @@ __device__ __forceinline__ void frag_product(const float (&in)[D / 8][4], float 
       for (int nj = 0; nj < NT; ++nj) w[nj] = W[(kk * NT + nj) * 32 + lane];
 #pragma unroll
       for (int nj = 0; nj < NT; ++nj) wmma::m16n8k8(out[nj], al, __float_as_uint(w[nj].x), __float_as_uint(w[nj].y));
+      if constexpr (!EXACT_W) {
 #pragma unroll
-      for (int nj = 0; nj < NT; ++nj) wmma::m16n8k8(out[nj], ah, __float_as_uint(w[nj].z), __float_as_uint(w[nj].w));
+        for (int nj = 0; nj < NT; ++nj) wmma::m16n8k8(out[nj], ah, __float_as_uint(w[nj].z), __float_as_uint(w[nj].w));
+      }
 #pragma unroll
       for (int nj = 0; nj < NT; ++nj) wmma::m16n8k8(out[nj], ah, __float_as_uint(w[nj].x), __float_as_uint(w[nj].y));
     } else {
@@ -148,7 +152,7 @@ __device__ __forceinline__ void frag_product(const float (&in)[D / 8][4], float 
       for (int nj = 0; nj < NT; ++nj) {
         const float4 w = W[(kk * NT + nj) * 32 + lane];
         wmma::m16n8k8(out[nj], al, __float_as_uint(w.x), __float_as_uint(w.y));
-        wmma::m16n8k8(out[nj], ah, __float_as_uint(w.z), __float_as_uint(w.w));
+        if constexpr (!EXACT_W) wmma::m16n8k8(out[nj], ah, __float_as_uint(w.z), __float_as_uint(w.w));
         wmma::m16n8k8(out[nj], ah, __float_as_uint(w.x), __float_as_uint(w.y));
       }
     }
@@ -418,6 +422,8 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
   constexpr int NT = C::NT, MT = C::MT;
   // grad_B / grad_Q contractions in single-pass rounded tf32 for bf16 activations
   constexpr bool kOneContract = sizeof(TIn) == 2 && TTC_BF16_ONEPASS;
+  // bf16 activations: B and Q (inputs, or mixtures rounded to bf16) are tf32-exact
+  constexpr bool kExactW = sizeof(TIn) == 2;
   extern __shared__ __align__(128) float smem[];
   const int tid = threadIdx.x, nthreads = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -616,8 +622,8 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         for (int j = 0; j < NT; ++j)
 #pragma unroll
           for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r & 1];
-        frag_product<D>(HD, QH, Wqt, lane);
-        if (!sym) frag_product<D>(HD, QTH, Wq, lane);
+        frag_product<D, kExactW>(HD, QH, Wqt, lane);
+        if (!sym) frag_product<D, kExactW>(HD, QTH, Wq, lane);
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -659,7 +665,7 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       float UE[NT][4];
       {
         float BL[NT][4];
-        frag_product<D>(L, BL, Wb, lane);
+        frag_product<D, kExactW>(L, BL, Wb, lane);
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -680,7 +686,7 @@ lqr_bwd_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       // h <- A h + B e^lgB u (symplectic_iter.py:832-850)
       {
         float BU[NT][4];
-        frag_product<D>(UE, BU, Wbt, lane);
+        frag_product<D, kExactW>(UE, BU, Wbt, lane);
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
 #pragma unroll

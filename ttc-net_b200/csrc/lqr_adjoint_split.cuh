@@ -92,7 +92,7 @@ __device__ __forceinline__ void build_operand_pairs(float* dst, Get get, int tid
 // Warp c's n-tiles of out = S W (S: the 16 x D staged operand, both halves), 3xTF32, k-steps
 // in order.  out[jl] is n-tile NH c + jl in output-fragment order.  W: the operand in the
 // layout AdjSplit<D>::kPreSplit selects.
-template <int D>
+template <int D, bool EXACT_W = false>
 __device__ __forceinline__ void split_product(const float* S, float (&out)[D / 16][4], const float* W, int c,
                                               int lane, int g, int t) {
   constexpr int NT = D / 8, NH = NT / 2, SS = AdjSplit<D>::SS;
@@ -130,8 +130,10 @@ __device__ __forceinline__ void split_product(const float* S, float (&out)[D / 1
     // passes over the n-tiles: consecutive MMAs go to independent accumulators
 #pragma unroll
     for (int jl = 0; jl < NH; ++jl) wmma::m16n8k8(out[jl], al, bh0[jl], bh1[jl]);
+    if constexpr (!EXACT_W) {  // W's residual is zero for bf16 activations (frag_product)
 #pragma unroll
-    for (int jl = 0; jl < NH; ++jl) wmma::m16n8k8(out[jl], ah, bl0[jl], bl1[jl]);
+      for (int jl = 0; jl < NH; ++jl) wmma::m16n8k8(out[jl], ah, bl0[jl], bl1[jl]);
+    }
 #pragma unroll
     for (int jl = 0; jl < NH; ++jl) wmma::m16n8k8(out[jl], ah, bh0[jl], bh1[jl]);
   }
@@ -358,8 +360,8 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
         // the pair at step k-1 (visible since the row barrier of that step).
         const float* Sp = stg + ((k - 1) & 1) * 3 * C::kStage + 2 * C::kStage;
         float QH[NH][4], QTH[NH][4];
-        split_product<D>(Sp, QH, Wqt, c, lane, g, t);
-        if (!sym) split_product<D>(Sp, QTH, Wq, c, lane, g, t);
+        split_product<D, sizeof(TIn) == 2>(Sp, QH, Wqt, c, lane, g, t);
+        if (!sym) split_product<D, sizeof(TIn) == 2>(Sp, QTH, Wq, c, lane, g, t);
 #pragma unroll
         for (int jl = 0; jl < NH; ++jl) {
 #pragma unroll
@@ -402,7 +404,7 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       float UE[NH][4];
       {
         float BL[NH][4];
-        split_product<D>(S0, BL, Wb, c, lane, g, t);
+        split_product<D, sizeof(TIn) == 2>(S0, BL, Wb, c, lane, g, t);
 #pragma unroll
         for (int jl = 0; jl < NH; ++jl) {
 #pragma unroll
@@ -424,7 +426,7 @@ lqr_bwd_split_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       // h <- A h + B e^lgB u (symplectic_iter.py:832-850)
       {
         float BU[NH][4];
-        split_product<D>(S1, BU, Wbt, c, lane, g, t);
+        split_product<D, sizeof(TIn) == 2>(S1, BU, Wbt, c, lane, g, t);
 #pragma unroll
         for (int jl = 0; jl < NH; ++jl) {
 #pragma unroll

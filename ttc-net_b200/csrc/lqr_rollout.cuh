@@ -422,7 +422,7 @@ lqr_rollout_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ B
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int r = 0; r < 4; ++r) HD[j][r] = H[j][r] * dqp[j][r];
-      frag_product<D>(HD, QH, Wqt, lane);
+      frag_product<D, sizeof(TIn) == 2>(HD, QH, Wqt, lane);
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -447,7 +447,7 @@ lqr_rollout_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ B
     float UE[NT][4];
     {
       float BL[NT][4];
-      frag_product<D>(L, BL, Wb, lane);
+      frag_product<D, sizeof(TIn) == 2>(L, BL, Wb, lane);
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
         float u[4];
@@ -472,7 +472,7 @@ lqr_rollout_mma_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ B
     // h = A h + B (e^lgB u)
     {
       float BU[NT][4];
-      frag_product<D>(UE, BU, Wbt, lane);
+      frag_product<D, sizeof(TIn) == 2>(UE, BU, Wbt, lane);
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
 #pragma unroll

@@ -119,7 +119,10 @@ __device__ __forceinline__ bool slot_sync_or(int id, int count, bool pred) {
 // start-address field.  Called by one elected lane of a warp-uniform branch, so the
 // descriptors stay in uniform registers.
 // ACC_IN: the accumulator already holds a value to add to (the first MMA accumulates).
-template <int N, int K, bool ACC_IN = false>
+// OP_LO = false: the operand is exactly representable in tf32 (its residual block is zero,
+// as for bf16 activations, whose B and Q are bf16 values), so the A_hi * Op_lo terms, which
+// would add exact zeros, are not issued: 8 MMAs per K = 32 product instead of 12.
+template <int N, int K, bool ACC_IN = false, bool OP_LO = true>
 __device__ __forceinline__ void issue_3xtf32(uint32_t acc, uint32_t a_hi, uint32_t a_lo,
                                              uint64_t dh, uint64_t dl) {
   constexpr uint32_t idesc = tc::idesc_tf32(N);
@@ -127,7 +130,7 @@ __device__ __forceinline__ void issue_3xtf32(uint32_t acc, uint32_t a_hi, uint32
 #pragma unroll
   for (int kk = 0; kk < K / 8; ++kk) {
     tc::mma_tf32_ts(acc, a_lo + kk * 8, dh + kk * step, idesc, (kk > 0 || ACC_IN) ? 1 : 0);
-    tc::mma_tf32_ts(acc, a_hi + kk * 8, dl + kk * step, idesc, 1);
+    if constexpr (OP_LO) tc::mma_tf32_ts(acc, a_hi + kk * 8, dl + kk * step, idesc, 1);
   }
 #pragma unroll
   for (int kk = 0; kk < K / 8; ++kk) tc::mma_tf32_ts(acc, a_hi + kk * 8, dh + kk * step, idesc, 1);
@@ -158,7 +161,8 @@ struct NoOverlap {
 // PAIRS: the tf32 residuals of A are formed two at a time (one paired subtraction per two
 // columns; bitwise the same values): 2.8 % faster at d = 16, 0.5 % at d = 32, 1.6 % slower
 // at d = 64 (register pressure).
-template <int C, int N, int K, bool PAIRS = false, typename Overlap = NoOverlap>
+// OP_LO: issue the A_hi * Op_lo terms (false when the operand is tf32-exact: issue_3xtf32).
+template <int C, int N, int K, bool PAIRS = false, bool OP_LO = true, typename Overlap = NoOverlap>
 __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], float (&out)[N],
                                              uint64_t dh, uint64_t dl, Overlap&& overlap = Overlap(),
                                              const float (*acc_init)[N] = nullptr) {
@@ -189,9 +193,9 @@ __device__ __forceinline__ bool tile_product(TileCtx& X, const float (&a)[C], fl
   if (X.mma_warp) {
     if (tc::elect_one()) {
       if (acc_init != nullptr) {
-        issue_3xtf32<N, K, true>(X.t_acc, X.t_hi, X.t_lo, dh, dl);
+        issue_3xtf32<N, K, true, OP_LO>(X.t_acc, X.t_hi, X.t_lo, dh, dl);
       } else {
-        issue_3xtf32<N, K>(X.t_acc, X.t_hi, X.t_lo, dh, dl);
+        issue_3xtf32<N, K, false, OP_LO>(X.t_acc, X.t_hi, X.t_lo, dh, dl);
       }
       tc::mma_commit(X.mbar);
     }
@@ -289,7 +293,8 @@ struct Y3AffineSteps {
 struct NoMark {
   __device__ __forceinline__ void operator()(int) const {}
 };
-template <int D, int DU, typename Y3, typename Mark = NoMark>
+// OP_LO = false: B and Q are tf32-exact (bf16 activations), see issue_3xtf32.
+template <int D, int DU, bool OP_LO, typename Y3, typename Mark = NoMark>
 __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&y1)[D],
                                          float (&y2)[D], Y3& y3, const float* ops, float* vec,
                                          float a, float lgA2, float lgQ2, float lgB2, float rinv,
@@ -330,7 +335,7 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
     // t = Y2 B ; Y3 = -t EBR on the last step ; c = t * S2.  The diagonal scalings below
     // run on fp32 pairs (bitwise the scalar results; 1-3 % faster).
     float t[DU];
-    if (!tile_product<D, DU, D, kPairs>(X, y2, t, o1h, o1l)) return false;
+    if (!tile_product<D, DU, D, kPairs, OP_LO>(X, y2, t, o1h, o1l)) return false;
     if (Y3::kEveryStep || last) {
 #pragma unroll
       for (int j4 = 0; j4 < DU / 4; ++j4) {
@@ -352,7 +357,7 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
     // than it saves.
     float u[D];
     constexpr bool kAccY1 = D <= 16;
-    if (!tile_product<DU, D, DU, kPairs>(X, t, u, o2h, o2l, NoOverlap(), kAccY1 ? &y1 : nullptr)) return false;
+    if (!tile_product<DU, D, DU, kPairs, OP_LO>(X, t, u, o2h, o2l, NoOverlap(), kAccY1 ? &y1 : nullptr)) return false;
 #pragma unroll
     for (int k4 = 0; k4 < D / 4; ++k4) {
       const float4 ia = v4[V::kIA / 4 + k4];
@@ -372,7 +377,7 @@ __device__ __forceinline__ bool tc_sweep(const Group<D>& G, TileCtx& X, float (&
         up2(mul2(pk2(y1[4 * k4 + 0], y1[4 * k4 + 1]), lo2(dq)), u[4 * k4 + 0], u[4 * k4 + 1]);
         up2(mul2(pk2(y1[4 * k4 + 2], y1[4 * k4 + 3]), hi2(dq)), u[4 * k4 + 2], u[4 * k4 + 3]);
       }
-      if (!tile_product<D, D, D, kPairs>(X, u, u, o3h, o3l, [&] { step_vectors(s + 1); })) return false;
+      if (!tile_product<D, D, D, kPairs, OP_LO>(X, u, u, o3h, o3l, [&] { step_vectors(s + 1); })) return false;
 #pragma unroll
       for (int k4 = 0; k4 < D / 4; ++k4) {
         const float4 at = v4[V::kAt / 4 + k4];
@@ -685,7 +690,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     Y3T y3;  // without AFF, M is formed from P below instead of from Y3
     if constexpr (AFF) y3 = Y3T{valid ? r_traj + p * T * DU : nullptr, sh0 + 2 * D, 0.f};
     const bool marker = kStagger && stag_arrival == 1 && tile == 0 && tid == 0;
-    const bool swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T,
+    const bool swept = tc_sweep<D, DU, (sizeof(TIn) != 2)>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T,
                                        (opts & TTC_FLAG_INV_GUARD) != 0, [&](int s) {
                                          if (marker) {
 #pragma unroll
@@ -742,7 +747,7 @@ lqr_fwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
       float w[D], m[DU];
 #pragma unroll
       for (int k = 0; k < D; ++k) w[k] = y2[k] * v1[V::kIA + k];
-      if (!tile_product<D, DU, D>(X, w, m, tc::smem_desc(o1, DU * 16, 128),
+      if (!tile_product<D, DU, D, false, (sizeof(TIn) != 2)>(X, w, m, tc::smem_desc(o1, DU * 16, 128),
                                   tc::smem_desc(o1 + DU * D * 4, DU * 16, 128)) ||
           slot_sync_or(X.bar_id, 128, X.timed_out)) {
         flags |= TTC_STATUS_MMA_TIMEOUT;
@@ -919,7 +924,7 @@ lqr_bwd_tc_kernel(const TIn* __restrict__ A_diag, const TIn* __restrict__ Bm,
     }
     // sh0 / sdu are read after the sweep's first slot barrier: visible by then.
     Y3DotDu<DU> y3{sdu, 0.0f};
-    const bool swept = tc_sweep<D, DU>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T,
+    const bool swept = tc_sweep<D, DU, (sizeof(TIn) != 2)>(G, X, y1, y2, y3, ops, vec, a, lgA2, lgQ2, lgB2, rinv, T,
                                               (opts & TTC_FLAG_INV_GUARD) != 0);
     if (slot_sync_or(X.bar_id, 128, X.timed_out || !swept)) {
       flags |= TTC_STATUS_MMA_TIMEOUT;
