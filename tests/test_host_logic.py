@@ -180,3 +180,18 @@ def test_chunked_weight_gradients_match_torch(K):
     torch.einsum("...r,rmn->...mn", r1, r2).backward(go)
     assert torch.allclose(a1.grad, r1.grad, rtol=1e-12, atol=1e-10)
     assert torch.allclose(a2.grad, r2.grad, rtol=1e-12, atol=1e-10)
+
+
+def test_bf16_values_are_exact_tf32_operands():
+    """The kernels skip the A_hi * B_lo terms of their 3xTF32 products for bf16 activations:
+    B and Q then hold bf16 values (the solver's inputs, or the layer's mixtures rounded to
+    bf16), and a bf16 value widened to fp32 has its low 16 mantissa bits zero, so the tf32
+    truncation the tensor cores apply (the low 13 bits) leaves it unchanged and its residual
+    B_lo is exactly zero.  Checked over every finite bf16 bit pattern."""
+    bits = torch.arange(0, 1 << 16, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    f = bits.float()
+    f = f[torch.isfinite(f)]
+    u = f.view(torch.int32)
+    assert torch.equal(u & 0x1FFF, torch.zeros_like(u))
+    hi = (u & ~0x1FFF).view(torch.float32)
+    assert torch.equal(f - hi, torch.zeros_like(f))
