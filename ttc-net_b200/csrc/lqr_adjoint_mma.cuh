@@ -288,6 +288,11 @@ __device__ __forceinline__ bool qmix_cta(const float* warp_s, int stage_off, int
       const int64_t ns = n0 + sw / wpr;
       const int hb = sw % wpr;
       const bool rowv = ns < N;
+      // A row past N (the last row group of a partial batch) ran the recursion on zero vectors
+      // against operands that were never built: shared memory that may hold any bit pattern,
+      // NaN included.  Its staged vectors can then be NaN and its zero coefficients would not
+      // cancel them (0 * NaN), so it contributes nothing here.  Uniform over the warp.
+      if (!rowv) continue;
       const int64_t prow = ns * nh;
       // grad_coeff_Qf of the staged warp's heads: [h; dh] basis[r]
       float Hs[NT][4], P[NT][4];
